@@ -1,0 +1,194 @@
+/*
+ * ns_b200.h -- C ABI of the B200 (sm_100a) decode hot path of neurostream.
+ *
+ * The reference (hareramray/nurostream, package `neurostream`) is pure Python;
+ * its hot path is Python/Triton with no FFI.  Each entry point below replaces
+ * one Python operator of that path and keeps its argument meaning; the cited
+ * reference lines are the operator it stands in for.  The Python side binds
+ * this header with ctypes (nurostream_b200/_lib.py) and mirrors the reference's
+ * operator names on top of it.
+ *
+ * Conventions
+ *  - All buffers are caller-owned device memory passed as raw pointers plus
+ *    sizes; the library never allocates or frees caller memory.
+ *  - Every call is asynchronous and ordered on `stream`; none synchronises the
+ *    host except ns_device_error().
+ *  - Return value: NS_OK (0) or a negative ns_status; ns_last_error() returns a
+ *    message for the last failure on the calling host thread.
+ *  - Device-side waits are bounded (about one second); a wait that runs out
+ *    sets a bit in the per-device error word read by ns_device_error().
+ */
+#ifndef NS_B200_H
+#define NS_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define NS_ABI_VERSION 1
+#define NS_MAX_TOKENS 8     /* tokens per fused GEMV or MoE-decode call */
+#define NS_MAX_TOPK 16      /* experts used per token */
+#define NS_MAX_EXPERTS 512  /* experts in one stacked tensor */
+
+typedef struct CUstream_st* ns_stream_t; /* identical to cudaStream_t */
+
+/* GGUF tensor type ids (on-disk values, neurostream/format/gguf.py:19-35). */
+enum ns_ggml_type {
+  NS_GGML_F32 = 0,
+  NS_GGML_F16 = 1,
+  NS_GGML_Q4_0 = 2,
+  NS_GGML_Q8_0 = 8,
+  NS_GGML_Q4_K = 12,
+  NS_GGML_Q5_K = 13,
+  NS_GGML_Q6_K = 14,
+  NS_GGML_BF16 = 30,
+  NS_GGML_MXFP4 = 39
+};
+
+/* Element types of activations and outputs. */
+enum ns_float_type { NS_F32 = 0, NS_F16 = 1, NS_BF16 = 2 };
+
+enum ns_status {
+  NS_OK = 0,
+  NS_ERR_INVALID = -1,     /* null pointer, bad count or stride */
+  NS_ERR_UNSUPPORTED = -2, /* type or shape outside what the kernels handle */
+  NS_ERR_SIZE = -3,        /* buffer smaller than the shape requires */
+  NS_ERR_CUDA = -4,        /* a CUDA runtime call failed */
+  NS_ERR_TIMEOUT = -5      /* a bounded device wait ran out */
+};
+
+/* Router variants. */
+enum ns_route_mode {
+  NS_ROUTE_TOPK_SOFTMAX = 0,     /* GPT-OSS: top-k of biased logits, softmax over the k
+                                    (neurostream/model/gpt_oss.py:116-121) */
+  NS_ROUTE_SOFTMAX_TOPK_NORM = 1 /* Qwen3-MoE: softmax, top-k, renormalise
+                                    (neurostream/moe/router.py:59-69) */
+};
+
+/* Expert activations. */
+enum ns_act_mode {
+  NS_ACT_CLAMPED_SWIGLU = 0, /* GPT-OSS (neurostream/model/gpt_oss.py:61-70) */
+  NS_ACT_SILU_MUL = 1        /* Qwen3 silu(gate)*up (neurostream/moe/router.py:208) */
+};
+
+/* Bits of the per-device error word. */
+#define NS_DEVERR_GRID_WAIT 1u  /* grid-wide barrier ran out */
+#define NS_DEVERR_COPY_WAIT 2u  /* bulk-copy completion wait ran out */
+#define NS_DEVERR_ROUTE 4u      /* routing produced an invalid expert id */
+
+const char* ns_last_error(void);
+int ns_abi_version(void);
+
+/* Block layout of a GGML type: elements and bytes per block
+ * (neurostream/format/gguf.py:39-55). */
+int ns_type_layout(int ggml_type, int* block_elems, int* block_bytes);
+
+/* Read (and optionally clear) the error word of the current device.
+ * Synchronises the device. */
+int ns_device_error(uint32_t* bits, int clear);
+
+/*
+ * Expand GGML bytes to floats, bit-exact with the reference.
+ * Replaces neurostream/compute/quant.py:153-184 `dequantize(raw, dtype, n_elements, out_dtype)`.
+ * raw: raw_bytes bytes of type ggml_type; out: n_elements values of out_dtype.
+ * Decodes whole blocks and truncates to n_elements, like the reference.
+ */
+int ns_dequant(const uint8_t* raw, size_t raw_bytes, int ggml_type, int64_t n_elements,
+               void* out, int out_dtype, ns_stream_t stream);
+
+/*
+ * Fused dequant-GEMV straight from GGUF bytes: y[t, n] = sum_k x[t, k] * W[n, k],
+ * fp32 accumulation, for T <= NS_MAX_TOKENS activation rows.
+ * Replaces neurostream/compute/triton_kernels.py:199-228 `fused_gemv(raw, dtype, x, n_rows, K, out_dtype)`
+ * (kernels :37-174).  w: n_rows rows of row_bytes(ggml_type, K) bytes (w_bytes >= that);
+ * x: T rows of K values of x_dtype, row stride x_stride elements;
+ * y: T rows of n_rows values of y_dtype, row stride y_stride elements.
+ * Types: MXFP4, Q8_0, Q4_K, Q6_K.
+ */
+int ns_gemv(const uint8_t* w, size_t w_bytes, int ggml_type, int n_rows, int K,
+            const void* x, int x_dtype, int64_t x_stride, int T,
+            void* y, int y_dtype, int64_t y_stride, ns_stream_t stream);
+
+/*
+ * MoE router on device: logits = h @ W^T (+ b), then top-k and softmax per `mode`.
+ * Replaces neurostream/model/gpt_oss.py:116-121 `GptOssModel._route` and
+ * neurostream/moe/router.py:59-69 `route` (without their host sync).
+ * h: T x H (h_dtype), W: E x H (w_dtype, one of NS_F32/NS_F16/NS_BF16), b: E fp32 or NULL.
+ * ids: T x k int32 (descending score), weights: T x k fp32, logits: T x E fp32 or NULL.
+ */
+int ns_moe_route(const void* h, int h_dtype, int T, int H,
+                 const void* w, int w_dtype, const float* b, int E, int k, int mode,
+                 int32_t* ids, float* weights, float* logits, ns_stream_t stream);
+
+/*
+ * One fused MoE decode layer: RMSNorm -> router -> top-k -> for every routed
+ * expert gate/up (+bias) -> activation -> down (+bias) -> weighted combine
+ * (+ residual), as ONE cooperative launch over all SMs.
+ * Replaces neurostream/model/gpt_oss.py:123-177 `GptOssModel._ffn_block` (with
+ * stream_expert_ffn, neurostream/compute/blockffn.py:396-449) and
+ * neurostream/moe/router.py:173-219 `moe_ffn`.
+ *
+ * Expert parallelism: the stacked expert tensors hold only experts
+ * [expert_lo, expert_hi) (local expert i is global expert expert_lo + i).
+ * Routing is computed over all n_expert; only local experts contribute, so
+ * summing `out` over ranks (with residual added on one rank only) gives the
+ * full layer.
+ */
+typedef struct ns_moe_layer {
+  int T;            /* tokens, 1..NS_MAX_TOKENS */
+  int H;            /* hidden size (n_embd) */
+  int F;            /* expert ffn width */
+  int n_expert;     /* experts seen by the router */
+  int expert_lo;    /* first expert held by these tensors */
+  int expert_hi;    /* one past the last */
+  int k;            /* experts per token */
+  int route_mode;   /* ns_route_mode */
+  int act_mode;     /* ns_act_mode */
+  int ggml_type;    /* type of gate/up/down expert tensors */
+  float alpha;      /* clamped-SwiGLU sigmoid slope (1.702) */
+  float limit;      /* clamped-SwiGLU clamp (7.0) */
+  float rms_eps;    /* RMSNorm epsilon, used when norm_w != NULL */
+  int add_residual; /* 1: out = x + moe, 0: out = moe */
+  const float* x;   /* T x H fp32 layer input (residual stream) */
+  const float* norm_w;  /* H fp32 RMSNorm weight, or NULL for h = x */
+  const void* router_w; /* n_expert x H */
+  int router_dtype;     /* NS_F32 / NS_F16 / NS_BF16 */
+  const float* router_b;  /* n_expert fp32 or NULL */
+  const uint8_t* gate_w;  /* local experts x F rows of row_bytes(type, H) */
+  const uint8_t* up_w;    /* same layout as gate_w */
+  const uint8_t* down_w;  /* local experts x H rows of row_bytes(type, F) */
+  const float* gate_b;    /* local experts x F fp32, or NULL */
+  const float* up_b;      /* local experts x F fp32, or NULL */
+  const float* down_b;    /* local experts x H fp32, or NULL */
+  float* out;             /* T x H fp32 */
+  int32_t* ids;           /* T x k int32 routed experts, or NULL */
+  float* weights;         /* T x k fp32 routing weights, or NULL */
+} ns_moe_layer_t;
+
+/* Workspace bytes a layer call needs (zeroed once with ns_moe_workspace_init;
+ * one workspace serves any number of stream-ordered calls on one device). */
+int ns_moe_workspace_bytes(const ns_moe_layer_t* p, size_t* bytes);
+int ns_moe_workspace_init(void* workspace, size_t bytes, ns_stream_t stream);
+int ns_moe_decode_layer(const ns_moe_layer_t* p, void* workspace, size_t workspace_bytes,
+                        ns_stream_t stream);
+
+/*
+ * Synthetic tensors for benchmarks and tests (no reference counterpart: the
+ * reference's configurations are synthetic inputs).  Fills `count` bytes
+ * (quantized `kind` = ggml type) or `count` values (kind = NS_SYNTH_F32/BF16)
+ * starting at element/byte `start` of the stream (seed, stream); the host twin
+ * is nurostream_b200/synth.py and agrees bit for bit.
+ */
+#define NS_SYNTH_F32 1000
+#define NS_SYNTH_BF16 1001
+int ns_synth_fill(void* dst, uint64_t count, int kind, uint64_t seed, uint64_t stream,
+                  uint64_t start, float sigma, int e_lo, int e_hi, float scale_mult,
+                  ns_stream_t s);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* NS_B200_H */

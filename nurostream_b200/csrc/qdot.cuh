@@ -1,0 +1,299 @@
+// Quantized dot products straight from GGUF bytes staged in shared memory.
+//
+// Every supported format is read as "groups": group g of a row covers the 32
+// consecutive elements x[32g .. 32g+31] and decodes from a fixed set of bytes:
+//   MXFP4  block g (17 B): E8M0 exponent + 16 payload bytes; byte j holds
+//          element j (low nibble) and j+16 (high nibble).
+//   Q8_0   block g (34 B): fp16 d + 32 int8.
+//   Q4_K   superblock g/8 (144 B), sub-block s = g%8: 32 bytes of qs at
+//          16 + 32*(s/2), nibble s%2; 6-bit scale/min from the 12 scale bytes.
+//   Q6_K   superblock g/8 (210 B), half h = (g/4)%2, lane i = g%4: ql bytes at
+//          64h + 32*(i%2) (nibble i/2), qh bytes at 128 + 32h (bits 2i..2i+1),
+//          int8 scales at 192 + 8h + 2i (+1 for the second 16 elements), fp16 d at 208.
+// These mappings restate the reference decoders (neurostream/compute/quant.py:24-140)
+// group by group.  A group is processed as four 8-element sub-chunks so that
+// the x values of a sub-chunk are loaded once and reused for R rows.
+//
+// Arithmetic: products and sums in fp32.  Per group the partial sum
+// sum(x * q) is formed first and scaled once (the block scale factors out of
+// the group's elements), which is the reference's math in a different
+// rounding order.
+#pragma once
+
+#include "common.cuh"
+
+namespace ns {
+
+// e2m1 pairs -> fp16x2: 4 bytes of a word, each byte's low nibble to the low half.
+__device__ __forceinline__ void e2m1x4_to_f16x2(uint32_t w, uint32_t (&h)[4]) {
+  asm("{\n .reg .b8 b0, b1, b2, b3;\n mov.b32 {b0, b1, b2, b3}, %4;\n"
+      " cvt.rn.f16x2.e2m1x2 %0, b0;\n cvt.rn.f16x2.e2m1x2 %1, b1;\n"
+      " cvt.rn.f16x2.e2m1x2 %2, b2;\n cvt.rn.f16x2.e2m1x2 %3, b3;\n}"
+      : "=r"(h[0]), "=r"(h[1]), "=r"(h[2]), "=r"(h[3])
+      : "r"(w));
+}
+
+__device__ __forceinline__ float2 f16x2_to_float2(uint32_t h) {
+  return __half22float2(*reinterpret_cast<const __half2*>(&h));
+}
+
+// Byte i of w (0..255) as an exact float minus `bias`, via the 2^23 trick:
+// the word 0x4B0000bb is the float 2^23 + bb.
+__device__ __forceinline__ float byte_as_float(uint32_t w, int i, float bias_plus_2p23) {
+  return __int_as_float(__byte_perm(w, 0x4B00u, 0x5440u + (unsigned)i)) - bias_plus_2p23;
+}
+
+constexpr float k2p23 = 8388608.0f;
+
+// ----------------------------------------------------------------------------- per-format groups
+
+template <int FMT>
+struct QGroup;
+
+template <>
+struct QGroup<NS_GGML_MXFP4> {
+  static constexpr int kParts = 1;
+  uint32_t q[4];
+  float scale;  // 2^(e-128); cvt yields e2m1 values = GGML table / 2
+
+  __device__ __forceinline__ void load(const uint8_t* row, int g) {
+    uint32_t w[5];
+    lds_words_unaligned<5>(row + 17 * g, w);
+    scale = e8m0_half_scale(w[0] & 0xFFu);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) q[i] = __funnelshift_r(w[i], w[i + 1], 8);
+  }
+  // sub-chunk s: payload bytes 4s..4s+3 -> elements {4s+i, 16+4s+i}
+  template <int NT>
+  static __device__ __forceinline__ void load_x(const float* x, int64_t xs, const int (&tok)[NT], int nt, int g,
+                                                int s, float (&xv)[NT][8]) {
+#pragma unroll
+    for (int t = 0; t < NT; ++t) {
+      if (t < nt) {
+        const float* p = x + tok[t] * xs + 32 * g;
+        float4 a = *reinterpret_cast<const float4*>(p + 4 * s);
+        float4 b = *reinterpret_cast<const float4*>(p + 16 + 4 * s);
+        xv[t][0] = a.x; xv[t][1] = b.x; xv[t][2] = a.y; xv[t][3] = b.y;
+        xv[t][4] = a.z; xv[t][5] = b.z; xv[t][6] = a.w; xv[t][7] = b.w;
+      }
+    }
+  }
+  template <int NT>
+  __device__ __forceinline__ void fma(int s, const float (&xv)[NT][8], int nt, float (&part)[NT][kParts]) const {
+    uint32_t h[4];
+    e2m1x4_to_f16x2(q[s], h);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      float2 f = f16x2_to_float2(h[i]);
+#pragma unroll
+      for (int t = 0; t < NT; ++t)
+        if (t < nt) part[t][0] = fmaf(xv[t][2 * i + 1], f.y, fmaf(xv[t][2 * i], f.x, part[t][0]));
+    }
+  }
+  template <int NT>
+  __device__ __forceinline__ void finish(const float (&part)[NT][kParts], const float (&)[NT], int nt,
+                                         float (&acc)[NT]) const {
+#pragma unroll
+    for (int t = 0; t < NT; ++t)
+      if (t < nt) acc[t] = fmaf(part[t][0] * 2.0f, scale, acc[t]);
+  }
+};
+
+template <>
+struct QGroup<NS_GGML_Q8_0> {
+  static constexpr int kParts = 1;
+  uint32_t q[8];
+  float d;
+
+  __device__ __forceinline__ void load(const uint8_t* row, int g) {
+    uint32_t w[9];
+    lds_words_unaligned<9>(row + 34 * g, w);
+    d = f16_bits_to_float(w[0]);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) q[i] = __funnelshift_r(w[i], w[i + 1], 16) ^ 0x80808080u;
+  }
+  template <int NT>
+  static __device__ __forceinline__ void load_x(const float* x, int64_t xs, const int (&tok)[NT], int nt, int g,
+                                                int s, float (&xv)[NT][8]) {
+#pragma unroll
+    for (int t = 0; t < NT; ++t) {
+      if (t < nt) {
+        const float* p = x + tok[t] * xs + 32 * g + 8 * s;
+        float4 a = *reinterpret_cast<const float4*>(p);
+        float4 b = *reinterpret_cast<const float4*>(p + 4);
+        xv[t][0] = a.x; xv[t][1] = a.y; xv[t][2] = a.z; xv[t][3] = a.w;
+        xv[t][4] = b.x; xv[t][5] = b.y; xv[t][6] = b.z; xv[t][7] = b.w;
+      }
+    }
+  }
+  template <int NT>
+  __device__ __forceinline__ void fma(int s, const float (&xv)[NT][8], int nt, float (&part)[NT][kParts]) const {
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      float f = byte_as_float(q[2 * s + (j >> 2)], j & 3, k2p23 + 128.0f);  // int8 value
+#pragma unroll
+      for (int t = 0; t < NT; ++t)
+        if (t < nt) part[t][0] = fmaf(xv[t][j], f, part[t][0]);
+    }
+  }
+  template <int NT>
+  __device__ __forceinline__ void finish(const float (&part)[NT][kParts], const float (&)[NT], int nt,
+                                         float (&acc)[NT]) const {
+#pragma unroll
+    for (int t = 0; t < NT; ++t)
+      if (t < nt) acc[t] = fmaf(part[t][0], d, acc[t]);
+  }
+};
+
+template <>
+struct QGroup<NS_GGML_Q4_K> {
+  static constexpr int kParts = 1;
+  uint32_t q[8];
+  float dsc, mmn;  // d*sc and dmin*mn of this sub-block (both exact in fp32)
+
+  __device__ __forceinline__ void load(const uint8_t* row, int g) {
+    const uint8_t* p = row + 144 * (g >> 3);
+    const int s = g & 7;
+    uint32_t hd[4];
+    lds_words_unaligned<4>(p, hd);  // d | dmin | scales[0..11]
+    const float d = f16_bits_to_float(hd[0]);
+    const float dmin = f16_bits_to_float(hd[0] >> 16);
+    // scale byte j is byte (j % 4) of hd[1 + j / 4]
+    auto sb = [&](int j) -> uint32_t { return (hd[1 + (j >> 2)] >> (8 * (j & 3))) & 0xFFu; };
+    uint32_t sc, mn;
+    if (s < 4) {
+      sc = sb(s) & 63u;
+      mn = sb(s + 4) & 63u;
+    } else {
+      sc = (sb(s + 4) & 0x0Fu) | ((sb(s - 4) >> 6) << 4);
+      mn = (sb(s + 4) >> 4) | ((sb(s) >> 6) << 4);
+    }
+    dsc = d * (float)sc;
+    mmn = dmin * (float)mn;
+    uint32_t w[8];
+    lds_words_unaligned<8>(p + 16 + 32 * (s >> 1), w);
+    const unsigned sh = (s & 1) ? 4u : 0u;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) q[i] = (w[i] >> sh) & 0x0F0F0F0Fu;
+  }
+  template <int NT>
+  static __device__ __forceinline__ void load_x(const float* x, int64_t xs, const int (&tok)[NT], int nt, int g,
+                                                int s, float (&xv)[NT][8]) {
+    QGroup<NS_GGML_Q8_0>::load_x<NT>(x, xs, tok, nt, g, s, xv);
+  }
+  template <int NT>
+  __device__ __forceinline__ void fma(int s, const float (&xv)[NT][8], int nt, float (&part)[NT][kParts]) const {
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      float f = byte_as_float(q[2 * s + (j >> 2)], j & 3, k2p23);
+#pragma unroll
+      for (int t = 0; t < NT; ++t)
+        if (t < nt) part[t][0] = fmaf(xv[t][j], f, part[t][0]);
+    }
+  }
+  template <int NT>
+  __device__ __forceinline__ void finish(const float (&part)[NT][kParts], const float (&xsum)[NT], int nt,
+                                         float (&acc)[NT]) const {
+#pragma unroll
+    for (int t = 0; t < NT; ++t)
+      if (t < nt) acc[t] = fmaf(-mmn, xsum[t], fmaf(part[t][0], dsc, acc[t]));
+  }
+};
+
+template <>
+struct QGroup<NS_GGML_Q6_K> {
+  static constexpr int kParts = 2;  // elements 0..15 and 16..31 have their own scale
+  uint32_t q[8];
+  float dsc0, dsc1;
+
+  __device__ __forceinline__ void load(const uint8_t* row, int g) {
+    const uint8_t* p = row + 210 * (g >> 3);
+    const int h = (g >> 2) & 1, i = g & 3;
+    uint32_t ql[8], qh[8];
+    lds_words_unaligned<8>(p + 64 * h + 32 * (i & 1), ql);
+    lds_words_unaligned<8>(p + 128 + 32 * h, qh);
+    const unsigned lsh = (i >> 1) ? 4u : 0u, hsh = 2u * (unsigned)i;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      uint32_t lo = (ql[j] >> lsh) & 0x0F0F0F0Fu;
+      uint32_t hi = ((qh[j] >> hsh) & 0x03030303u) << 4;
+      q[j] = lo | hi;  // 6-bit q per byte
+    }
+    const uint32_t scw = lds_u32_unaligned(p + 192 + 8 * h + 2 * i);  // bytes sc[2i], sc[2i+1]
+    const uint32_t dw = lds_u32_unaligned(p + 208);
+    const float d = f16_bits_to_float(dw);
+    dsc0 = d * (float)(int8_t)(scw & 0xFFu);
+    dsc1 = d * (float)(int8_t)((scw >> 8) & 0xFFu);
+  }
+  template <int NT>
+  static __device__ __forceinline__ void load_x(const float* x, int64_t xs, const int (&tok)[NT], int nt, int g,
+                                                int s, float (&xv)[NT][8]) {
+    QGroup<NS_GGML_Q8_0>::load_x<NT>(x, xs, tok, nt, g, s, xv);
+  }
+  template <int NT>
+  __device__ __forceinline__ void fma(int s, const float (&xv)[NT][8], int nt, float (&part)[NT][kParts]) const {
+    const int pi = s >> 1;  // sub-chunks 0,1 -> scale 0; 2,3 -> scale 1
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      float f = byte_as_float(q[2 * s + (j >> 2)], j & 3, k2p23 + 32.0f);  // q - 32
+#pragma unroll
+      for (int t = 0; t < NT; ++t)
+        if (t < nt) part[t][pi] = fmaf(xv[t][j], f, part[t][pi]);
+    }
+  }
+  template <int NT>
+  __device__ __forceinline__ void finish(const float (&part)[NT][kParts], const float (&)[NT], int nt,
+                                         float (&acc)[NT]) const {
+#pragma unroll
+    for (int t = 0; t < NT; ++t)
+      if (t < nt) acc[t] = fmaf(part[t][1], dsc1, fmaf(part[t][0], dsc0, acc[t]));
+  }
+};
+
+// ----------------------------------------------------------------------------- row dots
+
+// acc[r][t] += sum over this lane's groups of row r (smem) . x[t]
+// rows[r] may be nullptr (row absent) for r >= nrows; nrows is warp-uniform.
+// x: generic pointer; token t's activations are the row x + tok[t]*xs (floats,
+// 16-byte aligned rows), for t < nt <= NT.
+template <int FMT, int NT, int R>
+__device__ __forceinline__ void dot_rows(const uint8_t* const (&rows)[R], int nrows, int ngroups, int lane,
+                                         const float* x, int64_t xs, const int (&tok)[NT], int nt,
+                                         float (&acc)[R][NT]) {
+  using G = QGroup<FMT>;
+  for (int g = lane; g < ngroups; g += 32) {
+    G q[R];
+#pragma unroll
+    for (int r = 0; r < R; ++r)
+      if (r < nrows) q[r].load(rows[r], g);
+    float part[R][NT][G::kParts];
+#pragma unroll
+    for (int r = 0; r < R; ++r)
+#pragma unroll
+      for (int t = 0; t < NT; ++t)
+#pragma unroll
+        for (int p = 0; p < G::kParts; ++p) part[r][t][p] = 0.f;
+    float xsum[NT];
+#pragma unroll
+    for (int t = 0; t < NT; ++t) xsum[t] = 0.f;
+#pragma unroll
+    for (int s = 0; s < 4; ++s) {
+      float xv[NT][8];
+      G::template load_x<NT>(x, xs, tok, nt, g, s, xv);
+      if (FMT == NS_GGML_Q4_K) {
+#pragma unroll
+        for (int t = 0; t < NT; ++t)
+          if (t < nt)
+            xsum[t] += ((xv[t][0] + xv[t][1]) + (xv[t][2] + xv[t][3])) + ((xv[t][4] + xv[t][5]) + (xv[t][6] + xv[t][7]));
+      }
+#pragma unroll
+      for (int r = 0; r < R; ++r)
+        if (r < nrows) q[r].template fma<NT>(s, xv, nt, part[r]);
+    }
+#pragma unroll
+    for (int r = 0; r < R; ++r)
+      if (r < nrows) q[r].template finish<NT>(part[r], xsum, nt, acc[r]);
+  }
+}
+
+}  // namespace ns

@@ -1,0 +1,161 @@
+"""GPT-OSS-shaped MoE decode stack on device (the benchmark and EP harness).
+
+A ``MoeDecoder`` holds ``n_layer`` MoE layers of one model shape with seeded
+synthetic weights generated directly in HBM (``nurostream_b200.synth``): the
+stacked MXFP4 expert slabs, a bf16 router with fp32 bias, fp32 expert biases
+and the post-attention RMSNorm weight.  ``step`` runs one decode token through
+every layer (x <- layer(x)); ``decode`` does the same from and to host memory.
+Per-token launches are captured once into a CUDA graph.
+
+Expert parallelism (``world > 1``): rank r holds experts
+[r*E/world, (r+1)*E/world) of every layer -- a contiguous row window of each
+stacked tensor -- and dense state is replicated.  Every rank computes the
+identical router; each adds its local experts' weighted outputs (rank 0 also
+adds the residual), and one all-reduce(sum) per layer over NCCL combines them.
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass
+
+import torch
+
+from . import _lib, synth
+from .ggml import GGMLType, row_bytes
+from .moe import MoeLayer
+
+
+@dataclass
+class MoeShape:
+    n_layer: int = 36
+    hidden: int = 2880
+    expert_ffn: int = 2880
+    n_expert: int = 128
+    top_k: int = 4
+    ggml_type: int = int(GGMLType.MXFP4)
+    router_dtype: torch.dtype = torch.bfloat16
+    seed: int = 0
+    bias_sigma: float = 0.02
+
+    @property
+    def expert_bytes(self) -> int:
+        """Bytes of one expert's gate + up + down matrices."""
+        t = GGMLType(self.ggml_type)
+        return 2 * self.expert_ffn * row_bytes(t, self.hidden) + self.hidden * row_bytes(t, self.expert_ffn)
+
+    def layer_bytes_per_token(self) -> int:
+        """Algorithmic bytes one layer reads/writes for one token (the roofline numerator)."""
+        H, F, E, k = self.hidden, self.expert_ffn, self.n_expert, self.top_k
+        router = E * H * (2 if self.router_dtype == torch.bfloat16 else 4) + 4 * E
+        experts = k * self.expert_bytes
+        biases = k * 4 * (2 * F + H)
+        acts = 4 * H * 3        # x in, norm weight, out
+        return router + experts + biases + acts
+
+
+class MoeDecoder:
+    def __init__(self, shape: MoeShape, device: torch.device | str = "cuda", rank: int = 0, world: int = 1,
+                 group=None, use_graph: bool = True):
+        self.shape = shape
+        self.device = torch.device(device)
+        self.rank, self.world, self.group = rank, world, group
+        E = shape.n_expert
+        if E % world:
+            raise ValueError(f"{E} experts do not split evenly over {world} ranks")
+        self.lo, self.hi = rank * E // world, (rank + 1) * E // world
+        self.layers = [self._make_layer(l) for l in range(shape.n_layer)]
+        H = shape.hidden
+        self.x = torch.zeros((1, H), device=self.device, dtype=torch.float32)
+        self.bufs = [torch.empty((1, H), device=self.device, dtype=torch.float32) for _ in range(2)]
+        self.ids = torch.zeros((shape.n_layer, shape.top_k), device=self.device, dtype=torch.int32)
+        self.out = None
+        self.graph = None
+        self.use_graph = use_graph
+        self.launches_per_step = shape.n_layer
+
+    def _make_layer(self, l: int) -> MoeLayer:
+        s, sh, dev = synth.LayerStreams(l), self.shape, self.device
+        H, F, E, t = sh.hidden, sh.expert_ffn, sh.n_expert, GGMLType(sh.ggml_type)
+        n_local = self.hi - self.lo
+
+        def quant(stream, rows, K):
+            rb = row_bytes(t, K)
+            buf = torch.empty(n_local * rows * rb, dtype=torch.uint8, device=dev)
+            synth.fill_quant(buf, t, sh.seed, stream, start=self.lo * rows * rb)
+            return buf
+
+        def flt(n, stream, sigma, dtype=torch.float32, start=0):
+            buf = torch.empty(n, dtype=dtype, device=dev)
+            synth.fill_float(buf, sh.seed, stream, start, sigma)
+            return buf
+
+        norm = flt(H, s.norm_w, 0.1) + 1.0
+        return MoeLayer(
+            H=H, F=F, n_expert=E, k=sh.top_k, ggml_type=t,
+            router_w=flt(E * H, s.router_w, 0.02, sh.router_dtype).reshape(E, H),
+            router_b=flt(E, s.router_b, 0.02),
+            norm_w=norm,
+            gate=quant(s.gate, F, H), up=quant(s.up, F, H), down=quant(s.down, H, F),
+            gate_b=flt(n_local * F, s.gate_b, sh.bias_sigma, start=self.lo * F).reshape(n_local, F),
+            up_b=flt(n_local * F, s.up_b, sh.bias_sigma, start=self.lo * F).reshape(n_local, F),
+            down_b=flt(n_local * H, s.down_b, sh.bias_sigma, start=self.lo * H).reshape(n_local, H),
+            expert_lo=self.lo, expert_hi=self.hi, rms_eps=1e-5, max_tokens=1,
+        )
+
+    # ------------------------------------------------------------------ one token
+
+    def _run_layers(self) -> torch.Tensor:
+        cur = self.x
+        for l, layer in enumerate(self.layers):
+            nxt = self.bufs[l % 2]
+            layer(cur, out=nxt, add_residual=(self.rank == 0), ids=self.ids[l])
+            if self.world > 1:
+                torch.distributed.all_reduce(nxt, group=self.group)
+            cur = nxt
+        return cur
+
+    def capture(self) -> bool:
+        """Capture the per-token launches into a CUDA graph (returns False if capture is refused)."""
+        if not self.use_graph:
+            return False
+        torch.cuda.synchronize(self.device)
+        self._run_layers()                       # warm-up outside capture (NCCL communicator, attributes)
+        torch.cuda.synchronize(self.device)
+        g = torch.cuda.CUDAGraph()
+        try:
+            with torch.cuda.graph(g):
+                self.out = self._run_layers()
+        except Exception:
+            self.graph = None
+            torch.cuda.synchronize(self.device)
+            return False
+        self.graph = g
+        return True
+
+    def step(self, x: torch.Tensor | None = None) -> torch.Tensor:
+        """One decode token through all layers; x (1, H) fp32 on device (copied into the input buffer)."""
+        if x is not None:
+            self.x.copy_(x, non_blocking=True)
+        if self.graph is not None:
+            self.graph.replay()
+            return self.out
+        return self._run_layers()
+
+    def decode(self, x_host: torch.Tensor, out_host: torch.Tensor | None = None) -> torch.Tensor:
+        """End to end from host memory: copy x in, run every layer, copy the result out."""
+        self.x.copy_(x_host, non_blocking=True)
+        y = self.step()
+        if out_host is None:
+            out_host = torch.empty(y.shape, dtype=y.dtype, pin_memory=True)
+        out_host.copy_(y, non_blocking=True)
+        torch.cuda.current_stream(self.device).synchronize()
+        return out_host
+
+    def release(self) -> None:
+        """Drop the graph (it may hold NCCL work) before the process group goes away."""
+        self.graph = None
+        self.out = None
+
+    def check_device_errors(self) -> None:
+        bits = _lib.device_error()
+        if bits:
+            raise RuntimeError(f"device error bits {bits:#x} (bounded wait ran out)")

@@ -1,0 +1,257 @@
+"""MoE decode step on the B200: router and the fused one-launch layer.
+
+``MoeLayer`` holds one layer's device tensors (router, norm, the stacked
+GGUF expert byte slabs -- used exactly as the reference's VRAM-Q cache keeps
+them, never repacked -- and the per-expert biases) plus the kernel workspace,
+and runs ``ns_moe_decode_layer``.
+
+The reference-facing functions mirror the reference's own operators:
+* ``gptoss_route(model, h, layer)``     -> ``GptOssModel._route`` (gpt_oss.py:116-121)
+* ``gptoss_ffn_block(model, x, layer)`` -> ``GptOssModel._ffn_block`` (gpt_oss.py:123-205)
+* ``moe_ffn(model, h, layer)``          -> ``moe.router.moe_ffn`` (router.py:173-219)
+They take the fused path when every expert slab of the layer is resident in
+VRAM (quantized) and the token count fits one launch; otherwise they hand the
+call to the reference's own streaming implementation (saved by
+``nurostream_b200.install``), whose per-block GEMVs then run on ``ns_gemv``.
+"""
+from __future__ import annotations
+
+import ctypes as C
+from collections import Counter
+from dataclasses import dataclass, field
+
+import torch
+
+from . import _lib
+from .fused import ns_dtype, stream_of
+from .ggml import FUSED_TYPES, GGMLType, as_ggml_type, row_bytes
+
+
+@dataclass
+class RouterStats:
+    """Counters the reference's ``pin_hot_experts`` reads (``neurostream/moe/router.py:27-56``)."""
+
+    tokens_routed: int = 0
+    expert_reads: int = 0
+    hits: Counter = field(default_factory=Counter)
+
+
+def route(h: torch.Tensor, w: torch.Tensor, b: torch.Tensor | None, k: int,
+          mode: int = _lib.NS_ROUTE_TOPK_SOFTMAX):
+    """Router on device: returns (ids (T,k) int64, weights (T,k) fp32, logits (T,E) fp32).
+
+    mode NS_ROUTE_TOPK_SOFTMAX follows ``neurostream/model/gpt_oss.py:116-121``;
+    NS_ROUTE_SOFTMAX_TOPK_NORM follows ``neurostream/moe/router.py:59-69``.
+    """
+    h2 = h.reshape(-1, h.shape[-1]).contiguous()
+    T, H = h2.shape
+    E = w.shape[0]
+    w = w.contiguous()
+    bf = None if b is None else b.to(torch.float32).contiguous()
+    ids = torch.empty((T, k), device=h.device, dtype=torch.int32)
+    weights = torch.empty((T, k), device=h.device, dtype=torch.float32)
+    logits = torch.empty((T, E), device=h.device, dtype=torch.float32)
+    _lib.call("ns_moe_route", h2.data_ptr(), ns_dtype(h2.dtype), T, H, w.data_ptr(), ns_dtype(w.dtype),
+              None if bf is None else bf.data_ptr(), E, k, mode, ids.data_ptr(), weights.data_ptr(),
+              logits.data_ptr(), stream_of(h2))
+    return ids.long(), weights, logits
+
+
+def _ptr(t: torch.Tensor | None):
+    return None if t is None else t.data_ptr()
+
+
+class MoeLayer:
+    """One MoE layer's device tensors + workspace, run by ``ns_moe_decode_layer``.
+
+    gate/up/down: flat uint8 CUDA tensors of stacked experts [expert_lo, expert_hi)
+    (gate/up: (n_local*F) rows over H; down: (n_local*H) rows over F).
+    """
+
+    def __init__(self, *, H: int, F: int, n_expert: int, k: int, ggml_type, router_w: torch.Tensor,
+                 gate: torch.Tensor, up: torch.Tensor, down: torch.Tensor,
+                 router_b: torch.Tensor | None = None, norm_w: torch.Tensor | None = None,
+                 gate_b: torch.Tensor | None = None, up_b: torch.Tensor | None = None,
+                 down_b: torch.Tensor | None = None, expert_lo: int = 0, expert_hi: int | None = None,
+                 route_mode: int = _lib.NS_ROUTE_TOPK_SOFTMAX, act_mode: int = _lib.NS_ACT_CLAMPED_SWIGLU,
+                 alpha: float = 1.702, limit: float = 7.0, rms_eps: float = 1e-5, max_tokens: int = 1):
+        self.t = as_ggml_type(ggml_type)
+        if self.t not in FUSED_TYPES:
+            raise NotImplementedError(f"no fused MoE kernel for {self.t.name}")
+        self.H, self.F, self.E, self.k = H, F, n_expert, k
+        self.lo = expert_lo
+        self.hi = n_expert if expert_hi is None else expert_hi
+        n_local = self.hi - self.lo
+        dev = router_w.device
+        f32 = lambda v: None if v is None else v.to(device=dev, dtype=torch.float32).contiguous()
+        self.router_w = router_w.contiguous()
+        self.router_b = f32(router_b)
+        self.norm_w = f32(norm_w)
+        self.gate_b, self.up_b, self.down_b = f32(gate_b), f32(up_b), f32(down_b)
+        for name, t, rows, K in (("gate", gate, F, H), ("up", up, F, H), ("down", down, H, F)):
+            need = n_local * rows * row_bytes(self.t, K)
+            if t.dtype != torch.uint8 or not t.is_cuda or t.numel() < need:
+                raise ValueError(f"{name}: expected >= {need} uint8 CUDA bytes, got {t.numel()} {t.dtype} {t.device}")
+        self.gate, self.up, self.down = gate.contiguous(), up.contiguous(), down.contiguous()
+        self.route_mode, self.act_mode = route_mode, act_mode
+        self.alpha, self.limit, self.rms_eps = alpha, limit, rms_eps
+        self.max_tokens = max_tokens
+        self.device = dev
+        p = self._params(max_tokens, None, None, True, None, None)
+        n = C.c_size_t(0)
+        _lib.call("ns_moe_workspace_bytes", C.byref(p), C.byref(n))
+        self.workspace = torch.empty(n.value + 256, device=dev, dtype=torch.uint8)
+        off = (-self.workspace.data_ptr()) % 256
+        self._ws_ptr = self.workspace.data_ptr() + off
+        self._ws_bytes = n.value
+        _lib.call("ns_moe_workspace_init", self._ws_ptr, self._ws_bytes, stream_of(self.workspace))
+
+    def _params(self, T, x, out, add_residual, ids, weights) -> _lib.MoeLayerParams:
+        p = _lib.MoeLayerParams()
+        p.T, p.H, p.F, p.n_expert = T, self.H, self.F, self.E
+        p.expert_lo, p.expert_hi, p.k = self.lo, self.hi, self.k
+        p.route_mode, p.act_mode, p.ggml_type = self.route_mode, self.act_mode, int(self.t)
+        p.alpha, p.limit, p.rms_eps = self.alpha, self.limit, self.rms_eps
+        p.add_residual = 1 if add_residual else 0
+        p.x, p.norm_w = _ptr(x), _ptr(self.norm_w)
+        p.router_w, p.router_dtype, p.router_b = self.router_w.data_ptr(), ns_dtype(self.router_w.dtype), _ptr(self.router_b)
+        p.gate_w, p.up_w, p.down_w = self.gate.data_ptr(), self.up.data_ptr(), self.down.data_ptr()
+        p.gate_b, p.up_b, p.down_b = _ptr(self.gate_b), _ptr(self.up_b), _ptr(self.down_b)
+        p.out, p.ids, p.weights = _ptr(out), _ptr(ids), _ptr(weights)
+        return p
+
+    def __call__(self, x: torch.Tensor, out: torch.Tensor | None = None, add_residual: bool = True,
+                 ids: torch.Tensor | None = None, weights: torch.Tensor | None = None) -> torch.Tensor:
+        """out = x + sum_e w_e expert_e(norm(x)) (fp32, (T, H)); ids/weights optional (T,k) outputs."""
+        if x.dtype != torch.float32 or not x.is_contiguous():
+            raise TypeError("x must be a contiguous float32 tensor")
+        T = x.shape[0]
+        if T > self.max_tokens:
+            raise ValueError(f"T={T} exceeds the layer's max_tokens={self.max_tokens}")
+        if out is None:
+            out = torch.empty_like(x)
+        p = self._params(T, x, out, add_residual, ids, weights)
+        _lib.call("ns_moe_decode_layer", C.byref(p), self._ws_ptr, self._ws_bytes, stream_of(x))
+        return out
+
+
+# ----------------------------------------------------------------------------- reference-facing drop-ins
+
+_ORIGINALS: dict = {}   # filled by nurostream_b200.install
+
+
+def _vram_payload(cache, name):
+    """Device bytes of a VRAM-Q resident tensor, or None (no host->device upload)."""
+    vram = getattr(cache, "_vram", None)
+    if vram is None or name not in vram:
+        return None
+    hit = cache.raw_quantized(name)
+    if hit is None or not hit[0].is_cuda:
+        return None
+    return hit
+
+
+def _stats(model):
+    stats = getattr(model, "router_stats", None)
+    if stats is None:
+        try:
+            from neurostream.moe.router import RouterStats as RefStats  # the reference's own class
+            stats = RefStats()
+        except Exception:
+            stats = RouterStats()
+        model.router_stats = stats
+    return stats
+
+
+def _layer_for(model, layer: int, gptoss: bool) -> MoeLayer | None:
+    cache = getattr(model, "_ns_layers", None)
+    if cache is None:
+        cache = model._ns_layers = {}
+    if layer in cache:
+        return cache[layer]
+    c = model.cfg
+    p = f"blk.{layer}."
+    hits = [_vram_payload(model.cache, p + f"ffn_{kind}_exps.weight") for kind in ("gate", "up", "down")]
+    if any(h is None for h in hits) or len({h[1] for h in hits}) != 1:
+        cache[layer] = None
+        return None
+    t = GGMLType(int(hits[0][1]))
+    if t not in FUSED_TYPES:
+        cache[layer] = None
+        return None
+    kw = {}
+    if gptoss:
+        kw.update(router_b=model.w(p + "ffn_gate_inp.bias"),
+                  norm_w=model.w(p + "post_attention_norm.weight"),
+                  gate_b=model.w(p + "ffn_gate_exps.bias"), up_b=model.w(p + "ffn_up_exps.bias"),
+                  down_b=model.w(p + "ffn_down_exps.bias"), rms_eps=c.rms_eps,
+                  route_mode=_lib.NS_ROUTE_TOPK_SOFTMAX, act_mode=_lib.NS_ACT_CLAMPED_SWIGLU)
+    else:
+        kw.update(route_mode=_lib.NS_ROUTE_SOFTMAX_TOPK_NORM, act_mode=_lib.NS_ACT_SILU_MUL)
+    rw = model.w(p + "ffn_gate_inp.weight")
+    try:
+        layer_obj = MoeLayer(H=c.n_embd, F=c.n_ffn_expert, n_expert=c.n_expert, k=c.n_expert_used,
+                             ggml_type=t, router_w=rw, gate=hits[0][0], up=hits[1][0], down=hits[2][0],
+                             max_tokens=_lib.NS_MAX_TOKENS, **kw)
+    except _lib.NsError:
+        layer_obj = None
+    cache[layer] = layer_obj
+    return layer_obj
+
+
+def _run_fused(model, layer_obj: MoeLayer, x: torch.Tensor, layer: int, add_residual: bool):
+    T = x.shape[0]
+    xf = x.to(torch.float32).contiguous()
+    ids = torch.empty((T, layer_obj.k), device=x.device, dtype=torch.int32)
+    weights = torch.empty((T, layer_obj.k), device=x.device, dtype=torch.float32)
+    try:
+        out = layer_obj(xf, add_residual=add_residual, ids=ids, weights=weights)
+    except _lib.NsError as e:
+        if e.status == -2:  # shape outside the fused kernel: use the streaming path
+            return None
+        raise
+    stats = _stats(model)
+    stats.tokens_routed += T
+    for e in sorted(set(ids.view(-1).tolist())):      # one device->host copy per layer
+        rows = int((ids == e).any(-1).sum())
+        stats.hits[(layer, e)] += rows
+        stats.expert_reads += 1
+    return out.to(x.dtype)
+
+
+def gptoss_route(model, h: torch.Tensor, layer: int):
+    """Drop-in for ``GptOssModel._route``: (chosen list, ids (T,k), weights (T,k))."""
+    p = f"blk.{layer}."
+    if not h.is_cuda:
+        return _ORIGINALS["gptoss_route"](model, h, layer)
+    ids, w, _ = route(h, model.w(p + "ffn_gate_inp.weight"), model.w(p + "ffn_gate_inp.bias"),
+                      model.cfg.n_expert_used, _lib.NS_ROUTE_TOPK_SOFTMAX)
+    return torch.unique(ids).tolist(), ids, w.to(h.dtype)
+
+
+def gptoss_ffn_block(model, x: torch.Tensor, layer: int):
+    """Drop-in for ``GptOssModel._ffn_block``: ``x + MoE(rms_norm(x))``."""
+    if x.is_cuda and x.shape[0] <= _lib.NS_MAX_TOKENS:
+        lay = _layer_for(model, layer, gptoss=True)
+        if lay is not None:
+            out = _run_fused(model, lay, x, layer, add_residual=True)
+            if out is not None:
+                return out
+    return _ORIGINALS["gptoss_ffn_block"](model, x, layer)
+
+
+def moe_ffn(model, h: torch.Tensor, layer: int) -> torch.Tensor:
+    """Drop-in for ``neurostream.moe.router.moe_ffn`` (Qwen3-MoE; returns the MoE output only)."""
+    if h.is_cuda and h.shape[0] <= _lib.NS_MAX_TOKENS:
+        lay = _layer_for(model, layer, gptoss=False)
+        if lay is not None:
+            out = _run_fused(model, lay, h, layer, add_residual=False)
+            if out is not None:
+                p = f"blk.{layer}."
+                if model.has(p + "ffn_gate_shexp.weight"):   # shared expert, as router.py:215-218
+                    import torch.nn.functional as F
+                    sg = model._linear(p + "ffn_gate_shexp.weight", h)
+                    su = model._linear(p + "ffn_up_shexp.weight", h)
+                    out = out + model._linear(p + "ffn_down_shexp.weight", F.silu(sg) * su)
+                return out
+    return _ORIGINALS["moe_ffn"](model, h, layer)

@@ -148,3 +148,27 @@ class LayerStreams:
         self.gate_b = base + 13    # ffn_gate_exps.bias (E, F)
         self.up_b = base + 14      # ffn_up_exps.bias (E, F)
         self.down_b = base + 15    # ffn_down_exps.bias (E, H)
+
+
+# ----------------------------------------------------------------------------- device fill
+
+def fill_quant(dst, dtype, seed: int, stream: int, start: int = 0, e_lo: int = 118, e_hi: int = 124,
+               scale_mult: float = 1e-3) -> None:
+    """Fill a uint8 CUDA tensor with bytes [start, start+numel) of a synthetic tensor."""
+    import torch
+
+    from . import _lib
+    assert dst.dtype == torch.uint8 and dst.is_cuda and dst.is_contiguous()
+    _lib.call("ns_synth_fill", dst.data_ptr(), dst.numel(), int(GGMLType(int(dtype))), seed, stream, start,
+              1.0, e_lo, e_hi, scale_mult, torch.cuda.current_stream(dst.device).cuda_stream)
+
+
+def fill_float(dst, seed: int, stream: int, start: int = 0, sigma: float = 1.0) -> None:
+    """Fill a float32 or bfloat16 CUDA tensor with values [start, start+numel) of a synthetic stream."""
+    import torch
+
+    from . import _lib
+    assert dst.is_cuda and dst.is_contiguous()
+    kind = {torch.float32: _lib.NS_SYNTH_F32, torch.bfloat16: _lib.NS_SYNTH_BF16}[dst.dtype]
+    _lib.call("ns_synth_fill", dst.data_ptr(), dst.numel(), kind, seed, stream, start, sigma, 0, 0, 0.0,
+              torch.cuda.current_stream(dst.device).cuda_stream)

@@ -1,0 +1,130 @@
+"""GPU parity of the MoE decode step: router and the fused one-launch layer,
+against the reference's golden layer outputs and the CPU oracle."""
+import numpy as np
+import pytest
+import torch
+
+from nurostream_b200 import _lib
+from nurostream_b200.moe import MoeLayer, route
+from oracle import moe as omoe
+from tests import goldens
+from tests.gpu_util import assert_rel_close, layer_from_synth, run_layer
+
+pytestmark = pytest.mark.gpu
+
+
+def _margin_ok(logits, ids, k):
+    """Gap between the k-th and (k+1)-th logit, to flag near-ties instead of hiding them."""
+    s = np.sort(logits, axis=-1)[:, ::-1]
+    return (s[:, k - 1] - s[:, k]) if s.shape[1] > k else np.full(s.shape[0], np.inf)
+
+
+@pytest.mark.parametrize("mode", [_lib.NS_ROUTE_TOPK_SOFTMAX, _lib.NS_ROUTE_SOFTMAX_TOPK_NORM])
+@pytest.mark.parametrize("E,k,T", [(32, 4, 1), (128, 4, 3), (128, 8, 8), (16, 16, 2)])
+def test_route_matches_oracle(mode, E, k, T):
+    rng = np.random.default_rng(E * 100 + k * 10 + T)
+    H = 2880
+    h = rng.standard_normal((T, H)).astype(np.float32)
+    w = (rng.standard_normal((E, H)) * 0.02).astype(np.float32)
+    b = (rng.standard_normal(E) * 0.02).astype(np.float32) if mode == 0 else None
+    ids, weights, logits = route(torch.from_numpy(h).cuda(), torch.from_numpy(w).cuda(),
+                                 None if b is None else torch.from_numpy(b).cuda(), k, mode)
+    if mode == 0:
+        oid, ow, ol = omoe.route_gptoss(h, w, b, k, acc=np.float64)
+    else:
+        oid, ow, ol = omoe.route_qwen(h, w, k, acc=np.float64)
+    assert_rel_close(logits.cpu().numpy(), ol, 1e-6, "logits")
+    assert (_margin_ok(ol, oid, k) > 1e-5).all(), "near-tie in the random draw; pick another seed"
+    np.testing.assert_array_equal(ids.cpu().numpy(), oid)
+    np.testing.assert_allclose(weights.cpu().numpy(), ow, rtol=2e-6, atol=1e-7)
+
+
+@pytest.mark.parametrize("name", ["gptoss_cfg1", "gptoss_small_bias_t3", "qwen_q4k_t2"])
+def test_fused_layer_matches_reference_golden(name):
+    g = goldens.load("moe")
+    c = goldens.cases(g)[name]
+    L = goldens.SynthLayer(c)
+    layer = layer_from_synth(L)
+    out, ids, w = run_layer(layer, L.x, add_residual=L.gptoss)
+    np.testing.assert_array_equal(ids, g[f"{name}__ids"])
+    np.testing.assert_allclose(w, g[f"{name}__weights"], rtol=2e-6, atol=1e-7)
+    assert_rel_close(out, g[f"{name}__out"], 1e-3, name)
+    assert_rel_close(out, g[f"{name}__out"], 2e-5, name + " (tight)")
+
+
+def _oracle_layer(L):
+    if L.gptoss:
+        return omoe.gptoss_ffn_block(L.x, L.norm_w, 1e-5, L.router_w, L.router_b, L.rows_fn(), L.biases, L.k,
+                                     acc=np.float64)
+    return omoe.qwen_moe_ffn(L.x, L.router_w, L.rows_fn(), L.k, acc=np.float64)
+
+
+def _cfg(**kw):
+    c = dict(name="t", arch="gpt-oss", type=39, E=128, H=2880, F=2880, k=4, T=1, seed=11, bias=True,
+             norm="random", block_rows=512)
+    c.update(kw)
+    return c
+
+
+def test_fused_layer_gpt_oss_120b_shape():
+    """A layer of the GPT-OSS-120B shape: 128 experts, top-4, H=F=2880, MXFP4, biases."""
+    L = goldens.SynthLayer(_cfg())
+    out, ids, w = run_layer(layer_from_synth(L), L.x)
+    o_out, o_ids, o_w = _oracle_layer(L)
+    np.testing.assert_array_equal(ids, o_ids)
+    assert_rel_close(out, o_out, 2e-5, "gpt-oss-120b layer")
+
+
+@pytest.mark.parametrize("T", [1, 2])
+def test_fused_layer_qwen3_235b_shape(T):
+    """A layer of the Qwen3-235B-A22B shape: 128 experts, top-8, H=4096, F=1536, Q4_K."""
+    L = goldens.SynthLayer(_cfg(arch="qwen3moe", type=12, H=4096, F=1536, k=8, T=T, bias=False, norm=None))
+    out, ids, w = run_layer(layer_from_synth(L), L.x, add_residual=False)
+    o_out, o_ids, o_w = _oracle_layer(L)
+    np.testing.assert_array_equal(ids, o_ids)
+    assert_rel_close(out, o_out, 2e-5, f"qwen3 layer T={T}")
+
+
+def test_fused_layer_bf16_router_and_q8_0_experts():
+    L = goldens.SynthLayer(_cfg(type=8, E=16, H=1024, F=512, k=2, T=2, seed=3))
+    layer = layer_from_synth(L, router_dtype=torch.bfloat16)
+    out, ids, _ = run_layer(layer, L.x)
+    Lb = L
+    Lb.router_w = torch.from_numpy(L.router_w).to(torch.bfloat16).float().numpy()
+    o_out, o_ids, _ = _oracle_layer(Lb)
+    np.testing.assert_array_equal(ids, o_ids)
+    assert_rel_close(out, o_out, 2e-5, "q8_0 + bf16 router")
+
+
+def test_expert_parallel_shards_sum_to_full_layer():
+    """Experts split by index over shards; the sum of shard outputs (residual on one) is the layer."""
+    L = goldens.SynthLayer(_cfg(E=64, T=2, seed=21))
+    full, ids, w = run_layer(layer_from_synth(L), L.x)
+    parts = []
+    for r, (lo, hi) in enumerate([(0, 16), (16, 32), (32, 48), (48, 64)]):
+        out, sids, sw = run_layer(layer_from_synth(L, lo=lo, hi=hi), L.x, add_residual=(r == 0))
+        np.testing.assert_array_equal(sids, ids)      # every shard routes identically
+        parts.append(out)
+    assert_rel_close(sum(parts), full, 1e-5, "sum of 4 shards")
+
+
+def test_repeated_launches_reuse_the_workspace():
+    """The grid barrier's epoch counter carries over launches; outputs stay identical."""
+    L = goldens.SynthLayer(_cfg(E=32, seed=4))
+    layer = layer_from_synth(L)
+    first, _, _ = run_layer(layer, L.x)
+    xt = torch.from_numpy(L.x).cuda()
+    out = torch.empty_like(xt)
+    for _ in range(50):
+        layer(xt, out=out)
+    torch.cuda.synchronize()
+    assert _lib.device_error() == 0
+    assert np.array_equal(out.cpu().numpy(), first)
+
+
+def test_too_many_activation_rows_is_reported_not_run():
+    L = goldens.SynthLayer(_cfg(E=64, k=16, T=8, F=2880, seed=2))
+    layer = layer_from_synth(L, max_tokens=8)
+    with pytest.raises(_lib.NsError) as e:
+        layer(torch.from_numpy(L.x).cuda())
+    assert e.value.status == -2

@@ -1,0 +1,105 @@
+"""Host-side logic that runs without a GPU: the synthetic generator, the
+drop-in operator surface and the installer."""
+import importlib.util
+import os
+import sys
+
+import numpy as np
+import pytest
+import torch
+
+from nurostream_b200 import fused, synth
+from nurostream_b200.ggml import FUSED_TYPES, GGMLType, TYPE_LAYOUT, row_bytes
+from oracle import quant as oquant
+
+
+@pytest.mark.parametrize("t", [GGMLType.MXFP4, GGMLType.Q8_0, GGMLType.Q4_K, GGMLType.Q6_K, GGMLType.Q5_K,
+                               GGMLType.Q4_0])
+def test_synth_slices_are_consistent(t):
+    whole = synth.quant_bytes(t, 3, 17, 0, 4096)
+    for a, b in [(0, 1), (5, 700), (1023, 2049), (4000, 4096)]:
+        np.testing.assert_array_equal(synth.quant_bytes(t, 3, 17, a, b - a), whole[a:b])
+    assert not np.array_equal(whole, synth.quant_bytes(t, 4, 17, 0, 4096))
+
+
+def test_synth_distributions():
+    be, bb = TYPE_LAYOUT[GGMLType.MXFP4]
+    raw = synth.quant_bytes(GGMLType.MXFP4, 0, 1, 0, bb * 2000).reshape(2000, bb)
+    assert raw[:, 0].min() == 118 and raw[:, 0].max() == 124
+    vals = oquant.dequantize(raw.reshape(-1), GGMLType.MXFP4, 2000 * 32)
+    assert np.isfinite(vals).all()
+    q8 = synth.quant_bytes(GGMLType.Q8_0, 0, 2, 0, 34 * 1000).reshape(1000, 34)
+    d = q8[:, :2].copy().view(np.float16).astype(np.float32).ravel()
+    assert (d >= 0.5e-3 * 0.999).all() and (d <= 1.5e-3 * 1.001).all()
+    x = synth.float_values(0, 3, 0, 20000)
+    assert abs(float(x.mean())) < 0.03 and abs(float(x.std()) - 1.0) < 0.03
+    assert np.abs(x).max() <= 6.0
+    np.testing.assert_array_equal(synth.float_values(0, 3, 100, 50), x[100:150])
+    bf = synth.float_values(0, 3, 0, 100, 0.02, dtype="bf16")
+    np.testing.assert_allclose(synth.bf16_to_f32(bf), x[:100] * np.float32(0.02), rtol=2 ** -8)
+
+
+def test_can_fuse_gates_on_device_and_type():
+    x = torch.zeros(1, 64)
+    assert not fused.can_fuse(GGMLType.MXFP4, x)            # CPU tensor
+    assert not fused.can_fuse(GGMLType.Q5_K, x)
+    assert not fused.can_fuse(12345, x)
+    assert FUSED_TYPES == {GGMLType.MXFP4, GGMLType.Q8_0, GGMLType.Q4_K, GGMLType.Q6_K}
+
+
+def test_fused_gemv_errors_like_reference():
+    with pytest.raises(KeyError):
+        fused.fused_gemv(torch.zeros(176, dtype=torch.uint8), GGMLType.Q5_K, torch.zeros(1, 256), 1, 256)
+    with pytest.raises(TypeError):
+        fused.fused_gemv(torch.zeros(17, dtype=torch.uint8), GGMLType.MXFP4, torch.zeros(1, 32), 1, 32)
+
+
+def test_dequantize_refuses_cpu_tensors():
+    with pytest.raises(RuntimeError, match="no CPU fallback"):
+        fused.dequantize(torch.zeros(17, dtype=torch.uint8), GGMLType.MXFP4, 32)
+    with pytest.raises(TypeError):
+        fused.dequantize(torch.zeros(17, dtype=torch.int8), GGMLType.MXFP4, 32)
+
+
+def test_row_bytes():
+    assert row_bytes(GGMLType.MXFP4, 2880) == 1530
+    assert row_bytes(GGMLType.Q4_K, 4096) == 2304
+    assert row_bytes(GGMLType.Q8_0, 4096) == 4352
+    with pytest.raises(ValueError):
+        row_bytes(GGMLType.Q4_K, 1000)
+
+
+REF = os.environ.get("NS_REFERENCE_PATH", "/root/reference")
+
+
+def _reference_importable():
+    if not os.path.isdir(os.path.join(REF, "neurostream")):
+        return False
+    return importlib.util.find_spec("gguf") is not None
+
+
+@pytest.mark.skipif(not _reference_importable(), reason="reference package not present on this machine")
+def test_install_patches_and_restores_reference(monkeypatch):
+    monkeypatch.syspath_prepend(REF)
+    monkeypatch.setenv("PYTHONDONTWRITEBYTECODE", "1")
+    sys.dont_write_bytecode = True
+    import nurostream_b200
+    from nurostream_b200 import moe
+    import neurostream.compute.triton_kernels as tk
+    import neurostream.compute.quant as q
+    import neurostream.residency.cache as cache_mod
+    import neurostream.model.gpt_oss as go
+    import neurostream.moe.router as rt
+    originals = (tk.can_fuse, tk.fused_gemv, q.dequantize, cache_mod.dequantize, go.GptOssModel._route,
+                 go.GptOssModel._ffn_block, rt.moe_ffn)
+    with nurostream_b200.install():
+        assert tk.can_fuse is fused.can_fuse and tk.fused_gemv is fused.fused_gemv
+        assert rt.moe_ffn is moe.moe_ffn
+        assert go.GptOssModel._ffn_block is not originals[5]
+        # CPU tensors still take the reference's own path, unchanged
+        raw = synth.quant_bytes(GGMLType.Q4_K, 1, 1, 0, 2 * row_bytes(GGMLType.Q4_K, 256))
+        got = q.dequantize(torch.from_numpy(raw.copy()), GGMLType.Q4_K, 512)
+        np.testing.assert_array_equal(got.numpy(), oquant.dequantize(raw, GGMLType.Q4_K, 512))
+        assert not tk.can_fuse(GGMLType.MXFP4, torch.zeros(1, 32))
+    assert (tk.can_fuse, tk.fused_gemv, q.dequantize, cache_mod.dequantize, go.GptOssModel._route,
+            go.GptOssModel._ffn_block, rt.moe_ffn) == originals
