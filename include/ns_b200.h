@@ -176,6 +176,16 @@ int ns_moe_decode_layer(const ns_moe_layer_t* p, void* workspace, size_t workspa
                         ns_stream_t stream);
 
 /*
+ * Phase tracer of the fused layer (profiling aid; no reference counterpart --
+ * the reference times with time.perf_counter around whole calls).  While set,
+ * every ns_moe_decode_layer launch on the current device writes, per CTA,
+ * NS_TRACE_EVENTS globaltimer stamps (ns) to buf[cta * NS_TRACE_EVENTS + event].
+ * buf = NULL switches tracing off.  buf must hold grid * NS_TRACE_EVENTS uint64.
+ */
+#define NS_TRACE_EVENTS 16
+int ns_moe_set_trace(uint64_t* buf, size_t bytes);
+
+/*
  * Synthetic tensors for benchmarks and tests (no reference counterpart: the
  * reference's configurations are synthetic inputs).  Fills `count` bytes
  * (quantized `kind` = ggml type) or `count` values (kind = NS_SYNTH_F32/BF16)

@@ -6,40 +6,52 @@
 //   2. router logits, one expert per CTA (CTA c: experts c, c+G, ...) -> workspace;
 //   3. grid barrier; every CTA re-derives top-k + weights from the logits and
 //      builds the routed-expert slots (ascending expert id, as the reference
-//      walks torch.unique(ids));
+//      walks torch.unique(ids)) and its own tile list;
 //   4. phase 1: the (slot, neuron) space is split evenly over CTAs; a tile is
-//      up to TN neurons of one slot: its gate and up rows stream in by bulk
-//      copy, the CTA computes gate.h + b, up.h + b and the activation, and
-//      writes the activation rows to the workspace;
-//   5. grid barrier; phase 2: output rows are split evenly over CTAs; for each
-//      row sub-tile the CTA walks the slots in ascending expert order, streams
-//      that expert's down rows, and accumulates w * (down.a + b) in the
-//      reference's order, then adds the residual.
-// Weight copies run ahead across the phase-2 barrier (the ring is filled with
-// phase-2 tiles before the barrier wait), and every device wait is bounded.
+//      up to 12 neurons of one slot (their gate and up rows);
+//   5. grid barrier; phase 2: output rows are split evenly over CTAs; a tile is
+//      this CTA's rows (up to 24) of one slot's down matrix, slots in
+//      ascending expert order, accumulating w * (down.a + b) per row in the
+//      reference's order; then the residual is added.
+//
+// Inside a CTA, one producer warp streams tiles (1-D bulk copies on the TMA
+// engine) through a ring of shared-memory stages guarded by full/empty
+// mbarriers, so weight bytes keep flowing across both grid barriers.  Twelve
+// consumer warps split each tile as 3 row-groups x 4 K-chunks; every
+// (group, chunk) partial lands in shared memory and the group's four warps
+// reduce them in a fixed order (results are deterministic).  MXFP4 tiles run
+// on the tensor cores (mma_mxfp4.cuh); the K-quant formats use the CUDA-core
+// group decoders (qdot.cuh).  Every device wait is bounded.
+#include "mma_mxfp4.cuh"
 #include "qdot.cuh"
 
 namespace ns {
 
-constexpr int kMoeThreads = 256;
-constexpr int kMoeWarps = kMoeThreads / 32;
-constexpr int kMoeStages = 3;
 constexpr int kMaxPairs = NS_MAX_TOKENS * NS_MAX_TOPK;  // (slot, token) pairs
-constexpr int kMaxTiles = 512;
-constexpr int kMoeSmemBudget = 224 * 1024;
+constexpr int kWsHeader = 1024;  // workspace: barrier counter at 0, activation maxima at 64
+constexpr int kMaxTiles = 256;
+constexpr int kMoeSmemBudget = 225 * 1024;
 
 // ----------------------------------------------------------------------------- routing helpers
 
 // Top-k of v[0..E) by (value desc, index asc), one warp.  Writes ids/vals to smem arrays.
 __device__ void warp_topk(const float* v, int E, int k, int* ids, float* vals, int lane) {
-  uint32_t taken[NS_MAX_EXPERTS / 32];
-  for (int i = 0; i < NS_MAX_EXPERTS / 32; ++i) taken[i] = 0u;
+  // lane holds experts lane + 32*i (i < 16); bit i of `taken` marks one already chosen
+  uint32_t taken = 0u;
+  float mine[NS_MAX_EXPERTS / 32];
+#pragma unroll
+  for (int i = 0; i < NS_MAX_EXPERTS / 32; ++i) {
+    const int e = lane + 32 * i;
+    mine[i] = e < E ? v[e] : 0.f;
+  }
   for (int j = 0; j < k; ++j) {
     float best = -INFINITY;
     int bi = 0x7FFFFFFF;
-    for (int e = lane; e < E; e += 32) {
-      if ((taken[e >> 5] >> (e & 31)) & 1u) continue;
-      float x = v[e];
+#pragma unroll
+    for (int i = 0; i < NS_MAX_EXPERTS / 32; ++i) {
+      const int e = lane + 32 * i;
+      if (e >= E || ((taken >> i) & 1u)) continue;
+      const float x = mine[i];
       if (bi == 0x7FFFFFFF || x > best || (x == best && e < bi)) {
         best = x;
         bi = e;
@@ -55,7 +67,7 @@ __device__ void warp_topk(const float* v, int E, int k, int* ids, float* vals, i
       }
     }
     if (bi == 0x7FFFFFFF) bi = 0;  // E < k cannot happen (validated on the host)
-    taken[bi >> 5] |= 1u << (bi & 31);
+    if ((bi & 31) == lane) taken |= 1u << (bi >> 5);
     if (lane == 0) {
       ids[j] = bi;
       vals[j] = best;
@@ -140,22 +152,46 @@ __global__ void route_select_kernel(const float* logits, int T, int E, int k, in
 
 // ----------------------------------------------------------------------------- fused layer
 
+constexpr int kComputeWarps = 12;
+constexpr int kGroups = 3;          // row-groups of 8 weight rows per tile
+constexpr int kKChunks = 4;         // K-chunks per tile (kGroups * kKChunks = kComputeWarps)
+constexpr int kTileCols = 24;       // weight rows per tile
+constexpr int kMoeThreads = (kComputeWarps + 1) * 32;
+constexpr int kComputeThreads = kComputeWarps * 32;
+constexpr int kProducerWarp = kComputeWarps;
+constexpr int kMaxStages = 4;
+constexpr int kRedFloats = kKChunks * kTileCols * 16;  // one parity of the partial-sum buffer
+
 struct MoeArgs {
   ns_moe_layer_t p;
-  int rb_h, rb_f;     // bytes of a gate/up row (K=H) and of a down row (K=F)
+  int rb_h, rb_f;          // bytes of a gate/up row (K=H) and of a down row (K=F)
+  int nb_h, nb_f;          // 32-element blocks per row
   int n_local;
   const uint8_t* gate_end;
   const uint8_t* up_end;
   const uint8_t* down_end;
-  float* logits;      // workspace: T x E
-  float* act;         // workspace: pairs x F
+  float* logits;           // workspace: T x E
+  float* act;              // workspace: pairs x F
+  unsigned* amax;          // workspace: max |activation| bits per pair (kMaxPairs)
   unsigned long long* bar;
-  int stage_bytes;
-  int tn;             // phase-1 neurons per tile
-  int tr;             // phase-2 rows per tile
-  int region_floats;  // shared region holding h, later the activations
-  int rows_cta_max;   // phase-2 output rows per CTA, upper bound
+  int stages, stage_bytes, half;
+  int tn;                  // phase-1 neurons per tile (<= 12)
+  int tr;                  // phase-2 rows per tile (<= 24)
+  int rows_cta_max;        // phase-2 output rows per CTA, upper bound
+  int sc_stride;           // floats of each warp's scale buffer
+  // shared-memory layout (byte offsets)
+  int off_oacc, off_red, off_sc, off_stages, off_bars, off_shared, off_bias;
+  unsigned long long* trace;  // per-CTA phase stamps, or nullptr
 };
+
+// Phase stamps (event ids of ns_moe_set_trace)
+enum { kEvStart = 0, kEvNorm, kEvRouter, kEvBarrier1, kEvRoute, kEvImages, kEvFirstTile, kEvPhase1End,
+       kEvBarrier2, kEvPhase2Images, kEvTilesEnd, kEvEnd, kEvProducerFirst, kEvProducerLast, kEvLogits,
+       kEvTopk };
+
+__device__ __forceinline__ void stamp(unsigned long long* tr, int ev) {
+  if (tr) tr[blockIdx.x * NS_TRACE_EVENTS + ev] = globaltimer_ns();
+}
 
 struct Tile {
   short phase;  // 1 or 2
@@ -171,10 +207,18 @@ struct MoeShared {
   int slot_pair0[kMaxPairs + 1];
   int pair_token[kMaxPairs];
   float pair_w[kMaxPairs];
+  float fac_tok[NS_MAX_TOKENS];   // 2^(1-sigma) of each token's h image (1 on the CUDA-core path)
+  float fac_pair[kMaxPairs];      // same for each activation image
+  int sig_tok[NS_MAX_TOKENS];
+  int sig_pair[kMaxPairs];
   int ok;
-  float red[kMoeWarps][NS_MAX_TOKENS];
+  unsigned long long bar_target;
+  float rscale[NS_MAX_TOKENS];
+  float topv[NS_MAX_TOKENS][NS_MAX_TOPK];
+  float red[kComputeWarps + 1][NS_MAX_TOKENS];
+  float red2[kComputeWarps + 1][NS_MAX_TOKENS];
   Tile tiles[kMaxTiles];
-  float scratch[NS_MAX_EXPERTS];
+  __align__(16) float scratch[NS_MAX_EXPERTS];
 };
 
 __device__ __forceinline__ unsigned long long ld_acquire_u64(const unsigned long long* p) {
@@ -183,28 +227,30 @@ __device__ __forceinline__ unsigned long long ld_acquire_u64(const unsigned long
   return v;
 }
 
+__device__ __forceinline__ void named_sync(int id, int nthreads) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_addr(bar)) : "memory");
+}
+
 // Grid-wide barrier on a monotonically increasing 64-bit counter: barrier
 // instance n completes when the counter reaches (n+1)*G.  Bounded wait.
-__device__ bool grid_barrier(unsigned long long* bar, unsigned G, int* s_ok) {
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    __threadfence();
-    unsigned long long old = atomicAdd(bar, 1ull);
-    unsigned long long target = (old / G + 1ull) * G;
-    int ok = 1;
-    uint64_t t0 = globaltimer_ns();
-    while (ld_acquire_u64(bar) < target) {
-      if (globaltimer_ns() - t0 > kWaitLimitNs) {
-        raise_device_error(NS_DEVERR_GRID_WAIT);
-        ok = 0;
-        break;
-      }
-      __nanosleep(32);
+// Called by thread 0 only; the caller synchronises its CTA around it.
+__device__ int grid_barrier_thread0(unsigned long long* bar, unsigned G) {
+  __threadfence();
+  unsigned long long old = atomicAdd(bar, 1ull);
+  unsigned long long target = (old / G + 1ull) * G;
+  uint64_t t0 = globaltimer_ns();
+  while (ld_acquire_u64(bar) < target) {
+    if (globaltimer_ns() - t0 > kWaitLimitNs) {
+      raise_device_error(NS_DEVERR_GRID_WAIT);
+      return 0;
     }
-    *s_ok = ok;
+    __nanosleep(32);
   }
-  __syncthreads();
-  return *s_ok != 0;
+  return 1;
 }
 
 __device__ __forceinline__ float activate(int mode, float g, float u, float alpha, float limit) {
@@ -219,305 +265,678 @@ __device__ __forceinline__ float activate(int mode, float g, float u, float alph
   return __fmul_rn(__fmul_rn(g, sg), u);
 }
 
+// Weight-row address of tile column c (0..23) in the staged tile.
+// Phase 1: group gi = c/8 holds neurons 4gi..4gi+3; column 8gi + 2j is the
+// gate row of neuron 4gi+j and 8gi + 2j + 1 its up row.  Phase 2: column c is
+// tile row c.  Columns past the tile's rows point at its last row.
+__device__ __forceinline__ const uint8_t* tile_row(int phase, int c, const uint8_t* s0base, const uint8_t* s1base,
+                                                   int nvalid, int rb) {
+  if (phase == 1) {
+    int n = (c >> 3) * 4 + ((c & 7) >> 1);
+    n = min(n, nvalid - 1);
+    return ((c & 1) ? s1base : s0base) + (int64_t)n * rb;
+  }
+  return s0base + (int64_t)min(c, nvalid - 1) * rb;
+}
+
+// The tile's spans (bulk-copy sources) and their buffers.
+struct TileSpans {
+  Span s0, s1;
+  const uint8_t *b0, *e0, *b1, *e1;
+};
+
+__device__ __forceinline__ TileSpans tile_spans(const MoeArgs& a, const MoeShared& S, int i) {
+  const ns_moe_layer_t& p = a.p;
+  const Tile tl = S.tiles[i];
+  const int el = S.slot_expert[tl.slot] - p.expert_lo;
+  TileSpans t;
+  if (tl.phase == 1) {
+    const int64_t row0 = (int64_t)el * p.F + tl.r0, row1 = (int64_t)el * p.F + tl.r1;
+    t.s0 = Span{p.gate_w + row0 * a.rb_h, p.gate_w + row1 * a.rb_h};
+    t.s1 = Span{p.up_w + row0 * a.rb_h, p.up_w + row1 * a.rb_h};
+    t.b0 = p.gate_w;
+    t.e0 = a.gate_end;
+    t.b1 = p.up_w;
+    t.e1 = a.up_end;
+  } else {
+    const int64_t row0 = (int64_t)el * p.H + tl.r0, row1 = (int64_t)el * p.H + tl.r1;
+    t.s0 = Span{p.down_w + row0 * a.rb_f, p.down_w + row1 * a.rb_f};
+    t.s1 = Span{nullptr, nullptr};
+    t.b0 = p.down_w;
+    t.e0 = a.down_end;
+    t.b1 = t.e1 = nullptr;
+  }
+  return t;
+}
+
+// One (group, K-chunk) unit of a tile on the CUDA-core path: writes
+// red[kc][col][2i] = partial dot of tile column col with token i and
+// red[kc][col][2i+1] = 0.
+template <int FMT, int NT>
+__device__ __forceinline__ void unit_cuda_core(int phase, int gi, int kc, const uint8_t* s0base,
+                                               const uint8_t* s1base, int nvalid, int rb, int ngroups,
+                                               const float* x, int64_t xs, const int (&tok)[NT], int nt,
+                                               float* red, int lane) {
+  using G = QGroup<FMT>;
+  const int g0 = (ngroups * kc) / kKChunks, g1 = (ngroups * (kc + 1)) / kKChunks;
+#pragma unroll 1
+  for (int hf = 0; hf < 2; ++hf) {
+    const uint8_t* rs[4];
+#pragma unroll
+    for (int r = 0; r < 4; ++r) rs[r] = tile_row(phase, 8 * gi + 4 * hf + r, s0base, s1base, nvalid, rb);
+    float part[4][NT];
+#pragma unroll
+    for (int r = 0; r < 4; ++r)
+#pragma unroll
+      for (int t = 0; t < NT; ++t) part[r][t] = 0.f;
+    for (int g = g0 + lane; g < g1; g += 32) {
+      G qg[4];
+#pragma unroll
+      for (int r = 0; r < 4; ++r) qg[r].load(rs[r], g);
+      float pt[4][NT][G::kParts];
+#pragma unroll
+      for (int r = 0; r < 4; ++r)
+#pragma unroll
+        for (int t = 0; t < NT; ++t)
+#pragma unroll
+          for (int pp = 0; pp < G::kParts; ++pp) pt[r][t][pp] = 0.f;
+      float xsum[NT];
+#pragma unroll
+      for (int t = 0; t < NT; ++t) xsum[t] = 0.f;
+#pragma unroll
+      for (int s = 0; s < 4; ++s) {
+        float xv[NT][8];
+        G::template load_x<NT>(x, xs, tok, nt, g, s, xv);
+        if (FMT == NS_GGML_Q4_K) {
+#pragma unroll
+          for (int t = 0; t < NT; ++t)
+            if (t < nt)
+              xsum[t] += ((xv[t][0] + xv[t][1]) + (xv[t][2] + xv[t][3])) + ((xv[t][4] + xv[t][5]) + (xv[t][6] + xv[t][7]));
+        }
+#pragma unroll
+        for (int r = 0; r < 4; ++r) qg[r].template fma<NT>(s, xv, nt, pt[r]);
+      }
+#pragma unroll
+      for (int r = 0; r < 4; ++r) qg[r].template finish<NT>(pt[r], xsum, nt, part[r]);
+    }
+#pragma unroll
+    for (int r = 0; r < 4; ++r) {
+#pragma unroll
+      for (int t = 0; t < NT; ++t) {
+        float v = warp_sum(part[r][t]);
+        if (lane == 0 && t < nt) {
+          const int col = 8 * gi + 4 * hf + r;
+          red[(kc * kTileCols + col) * 16 + 2 * t] = v;
+          red[(kc * kTileCols + col) * 16 + 2 * t + 1] = 0.f;
+        }
+      }
+    }
+  }
+}
+
 template <int FMT, int NT>
 __global__ void __launch_bounds__(kMoeThreads, 1) moe_layer_kernel(MoeArgs a) {
+  constexpr bool kMma = (FMT == NS_GGML_MXFP4);
   extern __shared__ __align__(128) uint8_t smem[];
   const ns_moe_layer_t& p = a.p;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int G = gridDim.x, c = blockIdx.x;
   const int T = p.T, H = p.H, F = p.F, E = p.n_expert, k = p.k;
 
-  float* region = reinterpret_cast<float*>(smem);                       // h, then activations
-  float* o_acc = region + a.region_floats;                              // T x rows_cta_max
-  uint8_t* stages = reinterpret_cast<uint8_t*>(o_acc + ((T * a.rows_cta_max + 31) / 32) * 32);
-  uint64_t* bars = reinterpret_cast<uint64_t*>(stages + kMoeStages * a.stage_bytes);
-  MoeShared& S = *reinterpret_cast<MoeShared*>(bars + kMoeStages);
+  float* region = reinterpret_cast<float*>(smem);
+  float* o_acc = reinterpret_cast<float*>(smem + a.off_oacc);
+  float* red_base = reinterpret_cast<float*>(smem + a.off_red);
+  float* sc_base = reinterpret_cast<float*>(smem + a.off_sc);
+  uint8_t* stages = smem + a.off_stages;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + a.off_bars);
+  uint64_t* empty = full + kMaxStages;
+  float* stage_bias = reinterpret_cast<float*>(smem + a.off_bias);  // kTileCols floats per stage
+  MoeShared& S = *reinterpret_cast<MoeShared*>(smem + a.off_shared);
 
   if (tid == 0) {
-    for (int s = 0; s < kMoeStages; ++s) mbar_init(&bars[s], 1);
+    stamp(a.trace, kEvStart);
+    for (int s = 0; s < a.stages; ++s) {
+      mbar_init(&full[s], 2);  // producer: bulk-copy arm + bias/ragged bytes written
+      mbar_init(&empty[s], kComputeWarps);
+    }
     fence_mbar_init();
   }
 
-  // ---- 1. h = RMSNorm(x) (or x) into shared memory
+  if (c == 0 && tid < kMaxPairs) a.amax[tid] = 0u;  // activation maxima of this launch (phase 1 -> 2)
+
+  // ---- 1+2. one pass over the layer input: raw x into shared memory, sum of
+  // squares for RMSNorm, and this CTA's router logit in the same loop.  The
+  // norm is a per-token scalar r times the weight w, so
+  //   logit = sum_i (x_i r w_i) W_ci = r * sum_i (x_i w_i) W_ci.
+  float* h = region;
+  const bool own_expert = c < E;
   for (int t = 0; t < T; ++t) {
-    float ss = 0.f;
+    float ss = 0.f, dot = 0.f;
     for (int i = tid; i < H; i += kMoeThreads) {
-      float v = p.x[(int64_t)t * H + i];
-      region[t * H + i] = v;
-      ss = fmaf(v, v, ss);
+      const float xv = p.x[(int64_t)t * H + i];
+      const float wv = p.norm_w ? p.norm_w[i] : 1.0f;
+      const float rv = own_expert ? load_float(p.router_w, p.router_dtype, (int64_t)c * H + i) : 0.f;
+      h[t * H + i] = xv;
+      ss = fmaf(xv, xv, ss);
+      dot = fmaf(xv * wv, rv, dot);
     }
     ss = warp_sum(ss);
-    if (lane == 0) S.red[warp][t] = ss;
-  }
-  __syncthreads();
-  if (p.norm_w) {
-    for (int t = 0; t < T; ++t) {
-      float ss = 0.f;
-      for (int w = 0; w < kMoeWarps; ++w) ss += S.red[w][t];
-      const float r = 1.0f / sqrtf(ss / (float)H + p.rms_eps);
-      for (int i = tid; i < H; i += kMoeThreads)
-        region[t * H + i] = __fmul_rn(__fmul_rn(region[t * H + i], r), p.norm_w[i]);
+    dot = warp_sum(dot);
+    if (lane == 0) {
+      S.red[warp][t] = ss;
+      S.red2[warp][t] = dot;
     }
   }
   __syncthreads();
+  if (tid < T) {
+    float ss = 0.f, dot = 0.f;
+    for (int w = 0; w <= kComputeWarps; ++w) {
+      ss += S.red[w][tid];
+      dot += S.red2[w][tid];
+    }
+    const float r = p.norm_w ? 1.0f / sqrtf(ss / (float)H + p.rms_eps) : 1.0f;
+    S.rscale[tid] = r;
+    if (own_expert) a.logits[(int64_t)tid * E + c] = r * dot + (p.router_b ? p.router_b[c] : 0.f);
+  }
+  __syncthreads();
+  if (p.norm_w)
+    for (int t = 0; t < T; ++t) {
+      const float r = S.rscale[t];
+      for (int i = tid; i < H; i += kMoeThreads) h[t * H + i] = __fmul_rn(__fmul_rn(h[t * H + i], r), p.norm_w[i]);
+    }
+  __syncthreads();
+  if (tid == 0) stamp(a.trace, kEvNorm);
 
-  // ---- 2. router logits: CTA c computes experts c, c+G, ...
-  for (int e = c; e < E; e += G) {
-    float s[NS_MAX_TOKENS];
+  // more experts than CTAs: the rest of this CTA's router rows from h
+  for (int e = c + G; e < E; e += G) {
+    float sacc[NS_MAX_TOKENS];
 #pragma unroll
-    for (int t = 0; t < NS_MAX_TOKENS; ++t) s[t] = 0.f;
+    for (int t = 0; t < NS_MAX_TOKENS; ++t) sacc[t] = 0.f;
     for (int i = tid; i < H; i += kMoeThreads) {
       const float wv = load_float(p.router_w, p.router_dtype, (int64_t)e * H + i);
 #pragma unroll
       for (int t = 0; t < NS_MAX_TOKENS; ++t)
-        if (t < T) s[t] = fmaf(region[t * H + i], wv, s[t]);
+        if (t < T) sacc[t] = fmaf(h[t * H + i], wv, sacc[t]);
     }
 #pragma unroll
-    for (int t = 0; t < NS_MAX_TOKENS; ++t) {
+    for (int t = 0; t < NS_MAX_TOKENS; ++t)
       if (t < T) {
-        float v = warp_sum(s[t]);
+        const float v = warp_sum(sacc[t]);
         if (lane == 0) S.red[warp][t] = v;
       }
-    }
     __syncthreads();
     if (tid < T) {
       float v = 0.f;
-      for (int w = 0; w < kMoeWarps; ++w) v += S.red[w][tid];
-      if (p.router_b) v += p.router_b[e];
-      a.logits[(int64_t)tid * E + e] = v;
+      for (int w = 0; w <= kComputeWarps; ++w) v += S.red[w][tid];
+      a.logits[(int64_t)tid * E + e] = v + (p.router_b ? p.router_b[e] : 0.f);
     }
     __syncthreads();
   }
 
-  // ---- 3. barrier, then routing + slots (identical in every CTA)
-  grid_barrier(a.bar, (unsigned)G, &S.ok);
-  for (int t = 0; t < T; ++t) {
-    if (warp == 0) {
-      for (int e = lane; e < E; e += 32) S.scratch[e] = __ldcg(a.logits + (int64_t)t * E + e);
-      __syncwarp();
-      // Qwen mode overwrites scratch with probabilities; it holds a private copy
-      warp_route(S.scratch, E, k, p.route_mode, S.ids[t], S.w[t], S.scratch, lane);
+  // ---- 3. split-phase grid barrier: arrive now, build the h images, wait later
+  if (tid == 0) {
+    stamp(a.trace, kEvRouter);
+    __threadfence();
+    const unsigned long long old = atomicAdd(a.bar, 1ull);
+    S.bar_target = (old / (unsigned)G + 1ull) * (unsigned)G;
+  }
+  uint4* ximg = reinterpret_cast<uint4*>(region + ((T * H + 31) / 32) * 32);
+  if (kMma) {
+    for (int t = 0; t < T; ++t) {
+      float m = 0.f;
+      for (int i = tid; i < H; i += kMoeThreads) m = fmaxf(m, fabsf(h[t * H + i]));
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+      if (lane == 0) S.red[warp][t] = m;
     }
     __syncthreads();
-  }
-  if (tid == 0) {
-    // distinct local experts in ascending order
-    int n = 0;
+    if (tid < T) {
+      float m = 0.f;
+      for (int w = 0; w <= kComputeWarps; ++w) m = fmaxf(m, S.red[w][tid]);
+      const int sg = xsplit_sigma(m);
+      S.sig_tok[tid] = sg;
+      S.fac_tok[tid] = ldexpf(1.0f, 1 - sg);
+    }
+    __syncthreads();
     for (int t = 0; t < T; ++t)
-      for (int j = 0; j < k; ++j) {
-        int e = S.ids[t][j];
-        if (e < p.expert_lo || e >= p.expert_hi) continue;
-        int pos = 0;
-        while (pos < n && S.slot_expert[pos] < e) ++pos;
-        if (pos < n && S.slot_expert[pos] == e) continue;
-        for (int q = n; q > pos; --q) S.slot_expert[q] = S.slot_expert[q - 1];
-        S.slot_expert[pos] = e;
-        ++n;
+      build_xfrag(h + t * H, a.nb_h, S.sig_tok[t], ximg + t * xfrag_vec_u4(a.nb_h), tid, kMoeThreads);
+  } else if (tid < T) {
+    S.fac_tok[tid] = 1.0f;
+  }
+  for (int i = tid; i < T * a.rows_cta_max; i += kMoeThreads) o_acc[i] = 0.f;
+  if (tid == 0) {
+    S.ok = 1;
+    const uint64_t t0 = globaltimer_ns();
+    while (ld_acquire_u64(a.bar) < S.bar_target) {
+      if (globaltimer_ns() - t0 > kWaitLimitNs) {
+        raise_device_error(NS_DEVERR_GRID_WAIT);
+        S.ok = 0;
+        break;
       }
-    int np = 0;
-    for (int j = 0; j < n; ++j) {
-      S.slot_pair0[j] = np;
-      for (int t = 0; t < T; ++t)
-        for (int q = 0; q < k; ++q)
-          if (S.ids[t][q] == S.slot_expert[j]) {
-            S.pair_token[np] = t;
-            S.pair_w[np] = S.w[t][q];
-            ++np;
-          }
+      __nanosleep(32);
     }
-    S.slot_pair0[n] = np;
-    S.nslots = n;
-    S.npairs = np;
-    // tiles: phase 1 over the flattened (slot, neuron) space, then phase 2
-    int nt = 0;
-    const int64_t N1 = (int64_t)n * F;
-    int64_t pos = N1 * c / G, end1 = N1 * (c + 1) / G;
-    while (pos < end1 && nt < kMaxTiles) {
-      int j = (int)(pos / F), n0 = (int)(pos - (int64_t)j * F);
-      int64_t lim = (int64_t)n0 + (end1 - pos);
-      if (lim > (int64_t)n0 + a.tn) lim = (int64_t)n0 + a.tn;
-      if (lim > (int64_t)F) lim = F;
-      int n1 = (int)lim;
-      S.tiles[nt++] = Tile{1, (short)j, n0, n1};
-      pos += n1 - n0;
-    }
-    S.n1_tiles = nt;
-    const int ra = (int)((int64_t)H * c / G), rb = (int)((int64_t)H * (c + 1) / G);
-    for (int r0 = ra; r0 < rb; r0 += a.tr)
-      for (int j = 0; j < n && nt < kMaxTiles; ++j) S.tiles[nt++] = Tile{2, (short)j, r0, min(rb, r0 + a.tr)};
-    S.ntiles = nt;
-    if (c == 0) {
-      for (int t = 0; t < T; ++t)
-        for (int j = 0; j < k; ++j) {
-          if (p.ids) p.ids[t * k + j] = S.ids[t][j];
-          if (p.weights) p.weights[t * k + j] = S.w[t][j];
-        }
-    }
+    stamp(a.trace, kEvBarrier1);
   }
   __syncthreads();
-  const int nslots = S.nslots, ntiles = S.ntiles;
 
-  // ---- weight streaming: tile i -> stage i % kMoeStages
-  const int half = (a.stage_bytes / 2) & ~15;
-  auto spans = [&](int i, Span* s0, Span* s1, const uint8_t** e0, const uint8_t** e1, const uint8_t** b0) {
-    const Tile tl = S.tiles[i];
-    const int el = S.slot_expert[tl.slot] - p.expert_lo;
-    if (tl.phase == 1) {
-      const int64_t row0 = (int64_t)el * F + tl.r0, row1 = (int64_t)el * F + tl.r1;
-      *s0 = Span{p.gate_w + row0 * a.rb_h, p.gate_w + row1 * a.rb_h};
-      *s1 = Span{p.up_w + row0 * a.rb_h, p.up_w + row1 * a.rb_h};
-      *b0 = p.gate_w;
-      *e0 = a.gate_end;
-      *e1 = a.up_end;
+  // ---- 4. routing: every thread ranks one expert against all (value desc,
+  // index asc -- the order torch.topk returns), so the k winners are found in
+  // one parallel pass instead of k sequential arg-max rounds.
+  float* sc_e = S.scratch;  // scores of the current token
+  for (int t = 0; t < T; ++t) {
+    const float lg = tid < E ? __ldcg(a.logits + (int64_t)t * E + tid) : -INFINITY;
+    float score = lg;
+    if (p.route_mode == NS_ROUTE_SOFTMAX_TOPK_NORM) {
+      // softmax over all experts first (neurostream/moe/router.py:64-65)
+      float m = lg;
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+      if (lane == 0) S.red[warp][0] = m;
+      __syncthreads();
+      m = S.red[0][0];
+      for (int w = 1; w <= kComputeWarps; ++w) m = fmaxf(m, S.red[w][0]);
+      const float ex = tid < E ? expf(lg - m) : 0.f;
+      float sum = warp_sum(ex);
+      __syncthreads();
+      if (lane == 0) S.red[warp][0] = sum;
+      __syncthreads();
+      sum = 0.f;
+      for (int w = 0; w <= kComputeWarps; ++w) sum += S.red[w][0];
+      score = ex / sum;
+    }
+    if (tid < E) sc_e[tid] = score;
+    __syncthreads();
+    if (tid < E) {
+      int rank = 0;
+      int e2 = 0;
+      for (; e2 + 4 <= E; e2 += 4) {
+        const float4 v4 = *reinterpret_cast<const float4*>(sc_e + e2);
+        rank += (v4.x > score || (v4.x == score && e2 < tid));
+        rank += (v4.y > score || (v4.y == score && e2 + 1 < tid));
+        rank += (v4.z > score || (v4.z == score && e2 + 2 < tid));
+        rank += (v4.w > score || (v4.w == score && e2 + 3 < tid));
+      }
+      for (; e2 < E; ++e2) rank += (sc_e[e2] > score || (sc_e[e2] == score && e2 < tid));
+      if (rank < k) {
+        S.ids[t][rank] = tid;
+        S.topv[t][rank] = score;
+      }
+    }
+    __syncthreads();
+    if (warp == 0) {
+      const float v = lane < k ? S.topv[t][lane] : 0.f;
+      float wgt;
+      if (p.route_mode == NS_ROUTE_TOPK_SOFTMAX) {
+        // softmax over the k (neurostream/model/gpt_oss.py:119-120)
+        const float m = S.topv[t][0];
+        const float ex = lane < k ? expf(v - m) : 0.f;
+        wgt = ex / warp_sum(ex);
+      } else {
+        wgt = v / warp_sum(v);  // renormalise the top-k probabilities (router.py:66-68)
+      }
+      if (lane < k) S.w[t][lane] = wgt;
+    }
+    __syncthreads();
+  }
+  if (tid == 0) stamp(a.trace, kEvTopk);
+
+  // ---- 5. slots (distinct local experts, ascending) and this CTA's tiles
+  if (warp == 0) {
+    if (T == 1) {
+      const int e = lane < k ? S.ids[0][lane] : 0x7FFFFFFF;
+      const bool local = lane < k && e >= p.expert_lo && e < p.expert_hi;
+      int rank = 0, n = 0;
+      for (int j = 0; j < k; ++j) {
+        const int ej = __shfl_sync(0xffffffffu, e, j);
+        const bool lj = ej >= p.expert_lo && ej < p.expert_hi;
+        rank += lj && ej < e;
+        n += lj;
+      }
+      if (local) {
+        S.slot_expert[rank] = e;
+        S.slot_pair0[rank] = rank;
+        S.pair_token[rank] = 0;
+        S.pair_w[rank] = S.w[0][lane];
+      }
+      if (lane == 0) {
+        S.slot_pair0[n] = n;
+        S.nslots = n;
+        S.npairs = n;
+      }
     } else {
-      const int64_t row0 = (int64_t)el * H + tl.r0, row1 = (int64_t)el * H + tl.r1;
-      *s0 = Span{p.down_w + row0 * a.rb_f, p.down_w + row1 * a.rb_f};
-      *s1 = Span{nullptr, nullptr};
-      *b0 = p.down_w;
-      *e0 = a.down_end;
-      *e1 = nullptr;
+      // Lane l owns experts [32l, 32l+32) as a bitmap; a scan of the popcounts places them.
+      uint32_t bits = 0u;
+      for (int t = 0; t < T; ++t)
+        for (int j = 0; j < k; ++j) {
+          const int e = S.ids[t][j];
+          if (e >= p.expert_lo && e < p.expert_hi && (e >> 5) == lane) bits |= 1u << (e & 31);
+        }
+      const int cnt = __popc(bits);
+      int incl = cnt;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int v = __shfl_up_sync(0xffffffffu, incl, o);
+        if (lane >= o) incl += v;
+      }
+      const int n = __shfl_sync(0xffffffffu, incl, 31);
+      {
+        int pos = incl - cnt;
+        for (uint32_t b = bits; b; b &= b - 1) S.slot_expert[pos++] = 32 * lane + __ffs(b) - 1;
+      }
+      __syncwarp();
+      int base = 0;
+      for (int j0 = 0; j0 < n; j0 += 32) {
+        const int j = j0 + lane;
+        int cj = 0;
+        if (j < n)
+          for (int t = 0; t < T; ++t)
+            for (int q2 = 0; q2 < k; ++q2) cj += S.ids[t][q2] == S.slot_expert[j];
+        int inc = cj;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+          const int v = __shfl_up_sync(0xffffffffu, inc, o);
+          if (lane >= o) inc += v;
+        }
+        if (j < n) {
+          int pp = base + inc - cj;
+          S.slot_pair0[j] = pp;
+          for (int t = 0; t < T; ++t)
+            for (int q2 = 0; q2 < k; ++q2)
+              if (S.ids[t][q2] == S.slot_expert[j]) {
+                S.pair_token[pp] = t;
+                S.pair_w[pp] = S.w[t][q2];
+                ++pp;
+              }
+        }
+        base += __shfl_sync(0xffffffffu, inc, 31);
+      }
+      if (lane == 0) {
+        S.slot_pair0[n] = base;
+        S.nslots = n;
+        S.npairs = base;
+      }
     }
-  };
-  auto issue = [&](int i) {
-    const int st = i % kMoeStages;
-    uint8_t* buf = stages + st * a.stage_bytes;
-    Span s0, s1;
-    const uint8_t *e0, *e1, *b0;
-    spans(i, &s0, &s1, &e0, &e1, &b0);
-    uintptr_t lo, hi;
-    uint32_t bytes = 0;
-    bulk_window(s0, b0, e0, &lo, &hi);
-    bytes += hi > lo ? (uint32_t)(hi - lo) : 0u;
-    if (s1.g0) {
-      bulk_window(s1, p.up_w, e1, &lo, &hi);
-      bytes += hi > lo ? (uint32_t)(hi - lo) : 0u;
+    __syncwarp();
+    if (lane == 0) {
+      const int n = S.nslots;
+      int nt = 0;
+      const int N1 = n * F;  // <= NS_MAX_TOKENS * NS_MAX_TOPK * F: int32 is enough
+      int pos = N1 * c / G;
+      const int end1 = N1 * (c + 1) / G;
+      int j = pos / F, n0 = pos - j * F;
+      while (pos < end1 && nt < kMaxTiles) {
+        const int lim = min(min(n0 + a.tn, F), n0 + (end1 - pos));
+        S.tiles[nt++] = Tile{1, (short)j, n0, lim};
+        pos += lim - n0;
+        n0 = lim;
+        if (n0 == F) {
+          n0 = 0;
+          ++j;
+        }
+      }
+      S.n1_tiles = nt;
+      const int ra = H * c / G, rb = H * (c + 1) / G;
+      for (int r0 = ra; r0 < rb; r0 += a.tr)
+        for (int jj = 0; jj < n && nt < kMaxTiles; ++jj) S.tiles[nt++] = Tile{2, (short)jj, r0, min(rb, r0 + a.tr)};
+      S.ntiles = nt;
+      stamp(a.trace, kEvRoute);
     }
-    mbar_arrive_expect_tx(&bars[st], bytes);
-    issue_span(buf, s0, b0, e0, &bars[st]);
-    if (s1.g0) issue_span(buf + half, s1, p.up_w, e1, &bars[st]);
-  };
-  if (tid == 0)
-    for (int i = 0; i < kMoeStages && i < ntiles; ++i) issue(i);
+    if (c == 0)
+      for (int i = lane; i < T * k; i += 32) {
+        if (p.ids) p.ids[i] = S.ids[i / k][i % k];
+        if (p.weights) p.weights[i] = S.w[i / k][i % k];
+      }
+  }
+  __syncthreads();
+  if (tid == 0) stamp(a.trace, kEvImages);
 
-  // phase-2 output accumulators
-  for (int i = tid; i < T * a.rows_cta_max; i += kMoeThreads) o_acc[i] = 0.f;
-
-  const int ngroups_h = H / 32, ngroups_f = F / 32;
-  constexpr int RN = (NT <= 2) ? 2 : 1;  // phase-1 neurons per warp step (2*RN rows)
-  constexpr int R2 = (NT <= 2) ? 4 : 2;  // phase-2 rows per warp step
+  const int ntiles = S.ntiles, n1_tiles = S.n1_tiles;
   const int ra = (int)((int64_t)H * c / G);
 
+  // ================================================================= producer warp
+  if (warp == kProducerWarp) {
+    for (int i = 0; i < ntiles; ++i) {
+      const int st = i % a.stages;
+      if (i >= a.stages) {
+        if (lane == 0) mbar_wait_bounded(&empty[st], (uint32_t)(((i / a.stages) - 1) & 1));
+        __syncwarp();  // on a timeout the error bit is set; keep going so every wait stays bounded
+      }
+      uint8_t* buf = stages + st * a.stage_bytes;
+      const TileSpans ts = tile_spans(a, S, i);
+      if (lane == 0) {
+        // weight bytes first: they are the long pole
+        uintptr_t lo, hi;
+        uint32_t bytes = 0;
+        bulk_window(ts.s0, ts.b0, ts.e0, &lo, &hi);
+        bytes += hi > lo ? (uint32_t)(hi - lo) : 0u;
+        if (ts.s1.g0) {
+          bulk_window(ts.s1, ts.b1, ts.e1, &lo, &hi);
+          bytes += hi > lo ? (uint32_t)(hi - lo) : 0u;
+        }
+        mbar_arrive_expect_tx(&full[st], bytes);
+        issue_span(buf, ts.s0, ts.b0, ts.e0, &full[st]);
+        if (ts.s1.g0) issue_span(buf + a.half, ts.s1, ts.b1, ts.e1, &full[st]);
+        if (i == 0) stamp(a.trace, kEvProducerFirst);
+        if (i == ntiles - 1) stamp(a.trace, kEvProducerLast);
+      }
+      {
+        // the tile's bias values: phase 1 gate [0, 12) and up [12, 24); phase 2 down [0, 24)
+        const Tile tl = S.tiles[i];
+        const int el = S.slot_expert[tl.slot] - p.expert_lo;
+        const int nv = tl.r1 - tl.r0;
+        float bv = 0.f;
+        if (tl.phase == 1) {
+          if (lane < 12 && lane < nv && p.gate_b) bv = __ldg(p.gate_b + (int64_t)el * F + tl.r0 + lane);
+          if (lane >= 12 && lane < 24 && lane - 12 < nv && p.up_b)
+            bv = __ldg(p.up_b + (int64_t)el * F + tl.r0 + lane - 12);
+        } else if (lane < nv && lane < kTileCols && p.down_b) {
+          bv = __ldg(p.down_b + (int64_t)el * H + tl.r0 + lane);
+        }
+        if (lane < kTileCols) stage_bias[st * kTileCols + lane] = bv;
+      }
+      if (span_has_ragged(ts.s0, ts.b0, ts.e0)) copy_ragged(buf, ts.s0, ts.b0, ts.e0, lane);
+      if (ts.s1.g0 && span_has_ragged(ts.s1, ts.b1, ts.e1)) copy_ragged(buf + a.half, ts.s1, ts.b1, ts.e1, lane);
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&full[st]);  // release: biases and ragged bytes are visible
+    }
+    return;
+  }
+
+  // ================================================================= consumer warps
+  const int gi = warp % kGroups, kc = warp / kGroups;
+  const int g = lane >> 2, q = lane & 3;
+  float* sc = sc_base + warp * a.sc_stride;
+  bool phase2_started = false;
+
+  auto phase_boundary = [&]() {
+    // every activation row of every CTA is written -> build the phase-2 operands
+    named_sync(1, kComputeThreads);
+    if (tid == 0) {
+      stamp(a.trace, kEvPhase1End);
+      S.ok = grid_barrier_thread0(a.bar, (unsigned)G);
+      stamp(a.trace, kEvBarrier2);
+    }
+    named_sync(1, kComputeThreads);
+    const int np = S.npairs;
+    if (kMma) {
+      // per-pair scale from the maxima the phase-1 epilogues recorded
+      if (tid < np) {
+        const int sg = xsplit_sigma(__uint_as_float(__ldcg(a.amax + tid)));
+        S.fac_pair[tid] = ldexpf(1.0f, 1 - sg);
+        S.sig_pair[tid] = sg;
+      }
+      named_sync(1, kComputeThreads);
+      uint4* aimg = reinterpret_cast<uint4*>(region);
+      const int ps = xfrag_part_stride_u4(a.nb_f);
+      const int per_pair = a.nb_f * 4;
+      for (int it = tid; it < np * per_pair; it += kComputeThreads) {
+        const int pr = it / per_pair, i = it - pr * per_pair;
+        const int b = i >> 2, qq = i & 3;
+        const float scl = ldexpf(1.0f, S.sig_pair[pr]);
+        const float* v = a.act + (int64_t)pr * F + 32 * b + 4 * qq;
+        const float4 lo4 = __ldcg(reinterpret_cast<const float4*>(v));
+        const float4 hi4 = __ldcg(reinterpret_cast<const float4*>(v + 16));
+        const float xa[4] = {lo4.x, lo4.y, lo4.z, lo4.w}, xb[4] = {hi4.x, hi4.y, hi4.z, hi4.w};
+        uint32_t hi[4], lo[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const float x0 = xa[j] * scl, x1 = xb[j] * scl;
+          const __half h0 = __float2half_rn(x0), h1 = __float2half_rn(x1);
+          __half2 hh = __halves2half2(h0, h1);
+          hi[j] = *reinterpret_cast<uint32_t*>(&hh);
+          lo[j] = pack_f16x2(x0 - __half2float(h0), x1 - __half2float(h1));
+        }
+        uint4* img = aimg + pr * xfrag_vec_u4(a.nb_f);
+        img[b * 4 + qq] = make_uint4(hi[0], hi[1], hi[2], hi[3]);
+        img[ps + b * 4 + qq] = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+      }
+    } else {
+      const int nf = np * F;
+      for (int i = tid * 4; i < nf; i += kComputeThreads * 4)
+        *reinterpret_cast<float4*>(region + i) = __ldcg(reinterpret_cast<const float4*>(a.act + i));
+      for (int pr = tid; pr < np; pr += kComputeThreads) S.fac_pair[pr] = 1.0f;
+    }
+    named_sync(1, kComputeThreads);
+    if (tid == 0) stamp(a.trace, kEvPhase2Images);
+  };
+
   for (int i = 0; i < ntiles; ++i) {
-    if (i == S.n1_tiles) {
-      // all activations written -> barrier, then stage them in shared memory
-      grid_barrier(a.bar, (unsigned)G, &S.ok);
-      const int nf = S.npairs * F;
-      for (int q = tid * 4; q < nf; q += kMoeThreads * 4)
-        *reinterpret_cast<float4*>(region + q) = __ldcg(reinterpret_cast<const float4*>(a.act + q));
-      __syncthreads();
+    if (i == n1_tiles) {
+      phase_boundary();
+      phase2_started = true;
     }
-    const int st = i % kMoeStages;
-    uint8_t* buf = stages + st * a.stage_bytes;
-    Span s0, s1;
-    const uint8_t *e0, *e1, *b0;
-    spans(i, &s0, &s1, &e0, &e1, &b0);
-    const bool ok = mbar_wait_bounded(&bars[st], (uint32_t)((i / kMoeStages) & 1));
-    const bool rag0 = span_has_ragged(s0, b0, e0);
-    const bool rag1 = s1.g0 && span_has_ragged(s1, p.up_w, e1);
-    if (rag0 || rag1) {
-      if (warp == 0 && rag0) copy_ragged(buf, s0, b0, e0, lane);
-      if (warp == 1 && rag1) copy_ragged(buf + half, s1, p.up_w, e1, lane);
-      __syncthreads();
-    }
+    const int st = i % a.stages;
+    const uint8_t* buf = stages + st * a.stage_bytes;
     const Tile tl = S.tiles[i];
+    const TileSpans ts = tile_spans(a, S, i);
+    mbar_wait_bounded(&full[st], (uint32_t)((i / a.stages) & 1));
+    if (i == 0 && tid == 0) stamp(a.trace, kEvFirstTile);
     const int j = tl.slot;
     const int el = S.slot_expert[j] - p.expert_lo;
     const int pr0 = S.slot_pair0[j], nt = S.slot_pair0[j + 1] - pr0;
-    int tok[NT];
-    if (ok && tl.phase == 1) {
-#pragma unroll
-      for (int t = 0; t < NT; ++t) tok[t] = t < nt ? S.pair_token[pr0 + t] : 0;
-      const uint8_t* gbase = buf + (reinterpret_cast<uintptr_t>(s0.g0) & 15);
-      const uint8_t* ubase = buf + half + (reinterpret_cast<uintptr_t>(s1.g0) & 15);
-      const int nn = tl.r1 - tl.r0;
-      for (int n = warp * RN; n < nn; n += kMoeWarps * RN) {
-        const int nr = min(RN, nn - n);
-        const uint8_t* rows[2 * RN];
-#pragma unroll
-        for (int r = 0; r < RN; ++r) {
-          rows[r] = gbase + (int64_t)(n + min(r, nr - 1)) * a.rb_h;
-          rows[RN + r] = ubase + (int64_t)(n + min(r, nr - 1)) * a.rb_h;
+    const int nvalid = tl.r1 - tl.r0;
+    const uint8_t* s0base = buf + (reinterpret_cast<uintptr_t>(ts.s0.g0) & 15);
+    const uint8_t* s1base = buf + a.half + (reinterpret_cast<uintptr_t>(ts.s1.g0) & 15);
+    const int rb = tl.phase == 1 ? a.rb_h : a.rb_f;
+    const int nb = tl.phase == 1 ? a.nb_h : a.nb_f;
+    float* red = red_base + (i & 1) * kRedFloats;
+    const int nlive = tl.phase == 1 ? (nvalid + 3) / 4 : (nvalid + 7) / 8;  // live row-groups
+    const bool group_live = gi < nlive;
+
+    if (group_live) {
+      if (kMma) {
+        const int b0 = (nb * kc) / kKChunks, b1 = (nb * (kc + 1)) / kKChunks;
+        // this warp's scales: 8 rows x (b1 - b0) blocks, block-major
+        for (int it = lane; it < 8 * (b1 - b0); it += 32) {
+          const int r = it & 7, b = b0 + (it >> 3);
+          const uint8_t* rp = tile_row(tl.phase, 8 * gi + r, s0base, s1base, nvalid, rb);
+          sc[(b - b0) * 8 + r] = e8m0_half_scale(rp[17 * b]);
         }
-        float acc[2 * RN][NT];
-#pragma unroll
-        for (int r = 0; r < 2 * RN; ++r)
-#pragma unroll
-          for (int t = 0; t < NT; ++t) acc[r][t] = 0.f;
-        dot_rows<FMT, NT, 2 * RN>(rows, 2 * RN, ngroups_h, lane, region, H, tok, nt, acc);
-#pragma unroll
-        for (int r = 0; r < RN; ++r) {
-#pragma unroll
-          for (int t = 0; t < NT; ++t) {
-            const float gv = warp_sum(acc[r][t]);
-            const float uv = warp_sum(acc[RN + r][t]);
-            if (lane == 0 && r < nr && t < nt) {
-              const int neuron = tl.r0 + n + r;
-              float g = gv, u = uv;
-              if (p.gate_b) g = __fadd_rn(g, p.gate_b[(int64_t)el * F + neuron]);
-              if (p.up_b) u = __fadd_rn(u, p.up_b[(int64_t)el * F + neuron]);
-              a.act[(int64_t)(pr0 + t) * F + neuron] = activate(p.act_mode, g, u, p.alpha, p.limit);
-            }
-          }
+        __syncwarp();
+        const uint8_t* rowg = tile_row(tl.phase, 8 * gi + g, s0base, s1base, nvalid, rb);
+        const uint4* img;
+        int img_stride;
+        if (tl.phase == 1) {
+          img = ximg;
+          img_stride = xfrag_vec_u4(a.nb_h);
+        } else {
+          img = reinterpret_cast<const uint4*>(region) + pr0 * xfrag_vec_u4(a.nb_f);
+          img_stride = xfrag_vec_u4(a.nb_f);
         }
+        const int ps = xfrag_part_stride_u4(nb);
+        // x-part xp -> (token slot xp/2, part xp%2)
+        auto xrow = [&](int xp) -> const uint4* {
+          const int ti = xp >> 1;
+          if (ti >= nt) return nullptr;
+          const int tokslot = tl.phase == 1 ? S.pair_token[pr0 + ti] : ti;
+          return img + tokslot * img_stride + (xp & 1) * ps;
+        };
+        float acc[4] = {0.f, 0.f, 0.f, 0.f};
+        mxfp4_group_mma(rowg, xrow(g), NT > 4 ? xrow(g + 8) : nullptr, b0, b1, q, sc - b0 * 8, 8, 0, acc);
+        float* rr = red + (kc * kTileCols + 8 * gi + 2 * q) * 16;
+        rr[g] = acc[0];
+        rr[16 + g] = acc[1];
+        rr[g + 8] = acc[2];
+        rr[16 + g + 8] = acc[3];
+      } else {
+        int tok[NT];
+        const float* x;
+        int64_t xs;
+        if (tl.phase == 1) {
+#pragma unroll
+          for (int t = 0; t < NT; ++t) tok[t] = t < nt ? S.pair_token[pr0 + t] : 0;
+          x = h;
+          xs = H;
+        } else {
+#pragma unroll
+          for (int t = 0; t < NT; ++t) tok[t] = t;
+          x = region + (int64_t)pr0 * F;
+          xs = F;
+        }
+        unit_cuda_core<FMT, NT>(tl.phase, gi, kc, s0base, s1base, nvalid, rb, nb, x, xs, tok, nt, red, lane);
       }
-    } else if (ok) {
+    }
+    named_sync(2 + gi, 4 * 32);  // the group's four K-chunk partials are in `red`
+    const float* tb = stage_bias + st * kTileCols;
+    if (group_live) {
+      // epilogue of group gi by its 128 threads (fixed item -> thread map)
+      const int gt = kc * 32 + lane;
+      if (tl.phase == 1) {
+        const int nn = min(4, nvalid - 4 * gi);
+        for (int it = gt; it < nn * nt; it += 128) {
+          const int jn = it / nt, ti = it - jn * nt;
+          const int col = 8 * gi + 2 * jn;
+          float gs = 0.f, us = 0.f;
 #pragma unroll
-      for (int t = 0; t < NT; ++t) tok[t] = t;
-      const uint8_t* base = buf + (reinterpret_cast<uintptr_t>(s0.g0) & 15);
-      const int nn = tl.r1 - tl.r0;
-      for (int n = warp * R2; n < nn; n += kMoeWarps * R2) {
-        const int nr = min(R2, nn - n);
-        const uint8_t* rows[R2];
-#pragma unroll
-        for (int r = 0; r < R2; ++r) rows[r] = base + (int64_t)(n + min(r, nr - 1)) * a.rb_f;
-        float acc[R2][NT];
-#pragma unroll
-        for (int r = 0; r < R2; ++r)
-#pragma unroll
-          for (int t = 0; t < NT; ++t) acc[r][t] = 0.f;
-        dot_rows<FMT, NT, R2>(rows, nr, ngroups_f, lane, region + (int64_t)pr0 * F, F, tok, nt, acc);
-#pragma unroll
-        for (int r = 0; r < R2; ++r) {
-#pragma unroll
-          for (int t = 0; t < NT; ++t) {
-            const float v = warp_sum(acc[r][t]);
-            if (lane == 0 && r < nr && t < nt) {
-              const int row = tl.r0 + n + r;
-              float y = v;
-              if (p.down_b) y = __fadd_rn(y, p.down_b[(int64_t)el * H + row]);
-              float& o = o_acc[S.pair_token[pr0 + t] * a.rows_cta_max + (row - ra)];
-              o = __fadd_rn(o, __fmul_rn(S.pair_w[pr0 + t], y));
-            }
+          for (int kk = 0; kk < kKChunks; ++kk) {
+            const float* rg = red + (kk * kTileCols + col) * 16;
+            gs += rg[2 * ti] + rg[2 * ti + 1];
+            us += rg[16 + 2 * ti] + rg[16 + 2 * ti + 1];
           }
+          const int tokid = S.pair_token[pr0 + ti];
+          const float fac = S.fac_tok[tokid];
+          const int neuron = tl.r0 + 4 * gi + jn;
+          float gv = gs * fac, uv = us * fac;
+          if (p.gate_b) gv = __fadd_rn(gv, tb[4 * gi + jn]);
+          if (p.up_b) uv = __fadd_rn(uv, tb[12 + 4 * gi + jn]);
+          const float av = activate(p.act_mode, gv, uv, p.alpha, p.limit);
+          a.act[(int64_t)(pr0 + ti) * F + neuron] = av;
+          if (kMma) atomicMax(a.amax + pr0 + ti, __float_as_uint(fabsf(av)));
+        }
+      } else {
+        const int nr = min(8, nvalid - 8 * gi);
+        for (int it = gt; it < nr * nt; it += 128) {
+          const int r = it / nt, ti = it - r * nt;
+          const int col = 8 * gi + r;
+          float ys = 0.f;
+#pragma unroll
+          for (int kk = 0; kk < kKChunks; ++kk) {
+            const float* rg = red + (kk * kTileCols + col) * 16;
+            ys += rg[2 * ti] + rg[2 * ti + 1];
+          }
+          const int row = tl.r0 + col;
+          float y = ys * S.fac_pair[pr0 + ti];
+          if (p.down_b) y = __fadd_rn(y, tb[col]);
+          float& o = o_acc[S.pair_token[pr0 + ti] * a.rows_cta_max + (row - ra)];
+          o = __fadd_rn(o, __fmul_rn(S.pair_w[pr0 + ti], y));
         }
       }
     }
-    __syncthreads();  // stage consumed; o_acc updates visible
-    if (tid == 0 && i + kMoeStages < ntiles) issue(i + kMoeStages);
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty[st]);  // stage bytes and biases no longer needed by this warp
   }
-  if (S.n1_tiles == ntiles) {
-    // no phase-2 tile ran here; still take part in the second barrier
-    grid_barrier(a.bar, (unsigned)G, &S.ok);
-  }
+  if (!phase2_started) phase_boundary();  // no phase-2 tile here; still take part in the barrier
 
   // ---- output rows of this CTA: out = x + o (or o)
+  named_sync(1, kComputeThreads);
+  if (tid == 0) stamp(a.trace, kEvTilesEnd);
   const int rb_end = (int)((int64_t)H * (c + 1) / G);
-  for (int q = tid; q < T * (rb_end - ra); q += kMoeThreads) {
-    const int t = q / (rb_end - ra), r = ra + (q - t * (rb_end - ra));
+  for (int qq = tid; qq < T * (rb_end - ra); qq += kComputeThreads) {
+    const int t = qq / (rb_end - ra), r = ra + (qq - t * (rb_end - ra));
     const float o = o_acc[t * a.rows_cta_max + (r - ra)];
     p.out[(int64_t)t * H + r] = p.add_residual ? __fadd_rn(p.x[(int64_t)t * H + r], o) : o;
   }
-  (void)nslots;
+  if (tid == 0) stamp(a.trace, kEvEnd);
 }
 
 template <int FMT, int NT>
@@ -551,6 +970,14 @@ static int dispatch_moe_t(const MoeArgs& a, int grid, size_t smem, cudaStream_t 
 
 static size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 
+// Trace buffer per device (host-side table, set by ns_moe_set_trace).
+static unsigned long long* g_trace_buf[64] = {nullptr};
+static int trace_slot() {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 0;
+  return dev;
+}
+
 struct MoePlan {
   size_t ws_logits, ws_act, ws_total;
   int pairs_max;
@@ -580,8 +1007,67 @@ static int moe_validate(const ns_moe_layer_t* p, MoePlan* plan) {
   plan->pairs_max = p->T * p->k;
   plan->ws_logits = align_up((size_t)p->T * p->n_expert * 4, 256);
   plan->ws_act = align_up((size_t)plan->pairs_max * p->F * 4, 256);
-  plan->ws_total = 256 + plan->ws_logits + plan->ws_act;
+  plan->ws_total = kWsHeader + plan->ws_logits + plan->ws_act;
   return NS_OK;
+}
+
+// Shared-memory layout of one launch; returns total bytes, or 0 if it cannot fit.
+static size_t moe_layout(const ns_moe_layer_t* p, const MoePlan& plan, int grid, MoeArgs* a) {
+  const bool mma = p->ggml_type == NS_GGML_MXFP4;
+  const int nb_h = p->H / 32, nb_f = p->F / 32;
+  // region: phase 1 = h (+ h images), phase 2 = activation images (or fp32 activations)
+  const size_t img_h = (size_t)2 * (nb_h * 4 + 4) * 16, img_f = (size_t)2 * (nb_f * 4 + 4) * 16;
+  const size_t h_bytes = align_up((size_t)p->T * p->H * 4, 128);
+  const size_t r1 = h_bytes + (mma ? p->T * img_h : 0);
+  const size_t r2 = mma ? plan.pairs_max * img_f : (size_t)plan.pairs_max * p->F * 4;
+  const size_t region = align_up(std::max(r1, r2), 128);
+  a->rows_cta_max = (p->H + grid - 1) / grid + 1;
+  const size_t oacc = align_up((size_t)p->T * a->rows_cta_max * 4, 128);
+  const size_t red = (size_t)2 * kRedFloats * 4;
+  const int max_chunk_blocks = (std::max(nb_h, nb_f) + kKChunks - 1) / kKChunks + 1;
+  a->sc_stride = mma ? 8 * max_chunk_blocks : 0;
+  const size_t scb = align_up((size_t)kComputeWarps * a->sc_stride * 4, 128);
+  const size_t fixed = region + oacc + red + scb + 2 * kMaxStages * 8 + kMaxStages * kTileCols * 4 +
+                       sizeof(MoeShared) + 256;
+  const int rb_h = (int)row_bytes_of(p->ggml_type, p->H), rb_f = (int)row_bytes_of(p->ggml_type, p->F);
+  if (fixed >= (size_t)kMoeSmemBudget) return 0;
+  const size_t avail = kMoeSmemBudget - fixed;
+  // tiles: phase 1 up to 12 neurons (two spans), phase 2 up to 24 rows
+  int stages = kMaxStages;
+  int tn = 12, tr = 24;
+  auto stage_of = [&](int n1, int n2) {
+    size_t hf = align_up((size_t)n1 * rb_h + 48, 16);
+    return align_up(std::max(2 * hf, (size_t)n2 * rb_f + 48), 128);
+  };
+  while (stages >= 2 && stage_of(tn, tr) * stages > avail) {
+    if (stages > 3) {
+      --stages;
+    } else if (tn > 4 || tr > 8) {
+      if (tn > 4) tn -= 4;
+      if (tr > 8) tr -= 8;
+    } else if (tn > 1 || tr > 1) {
+      tn = std::max(1, tn - 1);
+      tr = std::max(1, tr - 1);
+    } else {
+      --stages;
+    }
+  }
+  if (stages < 2) return 0;
+  a->stages = stages;
+  a->tn = tn;
+  a->tr = tr;
+  a->half = (int)align_up((size_t)tn * rb_h + 48, 16);
+  a->stage_bytes = (int)stage_of(tn, tr);
+  a->nb_h = nb_h;
+  a->nb_f = nb_f;
+  a->off_oacc = (int)region;
+  a->off_red = (int)(region + oacc);
+  a->off_sc = (int)(region + oacc + red);
+  a->off_stages = (int)align_up(region + oacc + red + scb, 128);
+  a->off_bars = a->off_stages + stages * a->stage_bytes;
+  a->off_bias = a->off_bars + 2 * kMaxStages * 8;
+  a->off_shared = (int)align_up((size_t)a->off_bias + kMaxStages * kTileCols * 4, 16);
+  return (size_t)a->off_shared + sizeof(MoeShared);
 }
 
 }  // namespace ns
@@ -605,6 +1091,19 @@ extern "C" int ns_moe_route(const void* h, int h_dtype, int T, int H, const void
   const size_t smem = (size_t)wpb * (NS_MAX_EXPERTS + 2 * NS_MAX_TOPK) * 4;
   route_select_kernel<<<(T + wpb - 1) / wpb, wpb * 32, smem, s>>>(logits, T, E, k, mode, ids, weights);
   NS_CUDA_TRY(cudaGetLastError());
+  return NS_OK;
+}
+
+extern "C" int ns_moe_set_trace(uint64_t* buf, size_t bytes) {
+  using namespace ns;
+  int nsm = 0;
+  if (buf) {
+    int st = num_sms(&nsm);
+    if (st) return st;
+    if (bytes < (size_t)nsm * NS_TRACE_EVENTS * 8)
+      return fail(NS_ERR_SIZE, "ns_moe_set_trace: %zu bytes, need %d", bytes, nsm * NS_TRACE_EVENTS * 8);
+  }
+  g_trace_buf[trace_slot()] = reinterpret_cast<unsigned long long*>(buf);
   return NS_OK;
 }
 
@@ -641,6 +1140,7 @@ extern "C" int ns_moe_decode_layer(const ns_moe_layer_t* p, void* workspace, siz
   if (st) return st;
 
   MoeArgs a;
+  memset(&a, 0, sizeof a);
   a.p = *p;
   a.rb_h = (int)row_bytes_of(p->ggml_type, p->H);
   a.rb_f = (int)row_bytes_of(p->ggml_type, p->F);
@@ -650,36 +1150,23 @@ extern "C" int ns_moe_decode_layer(const ns_moe_layer_t* p, void* workspace, siz
   a.down_end = p->down_w + (size_t)a.n_local * p->H * a.rb_f;
   uint8_t* ws = reinterpret_cast<uint8_t*>(workspace);
   a.bar = reinterpret_cast<unsigned long long*>(ws);
-  a.logits = reinterpret_cast<float*>(ws + 256);
-  a.act = reinterpret_cast<float*>(ws + 256 + plan.ws_logits);
+  a.amax = reinterpret_cast<unsigned*>(ws + 64);
+  a.logits = reinterpret_cast<float*>(ws + kWsHeader);
+  a.act = reinterpret_cast<float*>(ws + kWsHeader + plan.ws_logits);
+  a.trace = g_trace_buf[trace_slot()];
 
   const int grid = nsm;
-  a.rows_cta_max = (p->H + grid - 1) / grid + 1;
-  a.region_floats = (int)align_up((size_t)std::max(p->T * p->H, plan.pairs_max * p->F), 32);
-  const size_t fixed = (size_t)a.region_floats * 4 + align_up((size_t)p->T * a.rows_cta_max, 32) * 4 +
-                       kMoeStages * 8 + sizeof(MoeShared) + 128;
-  if (fixed + kMoeStages * 4096 > (size_t)kMoeSmemBudget)
+  const size_t smem = moe_layout(p, plan, grid, &a);
+  if (smem == 0 || smem > (size_t)kMoeSmemBudget)
     return fail(NS_ERR_UNSUPPORTED,
                 "ns_moe_decode_layer: T=%d x k=%d activation rows of F=%d do not fit in shared memory; "
                 "use the per-expert GEMV path", p->T, p->k, p->F);
-  a.stage_bytes = (int)std::min<size_t>(48 * 1024, ((kMoeSmemBudget - fixed) / kMoeStages) & ~size_t(15));
-  const int half = (a.stage_bytes / 2) & ~15;
-  a.tn = (half - 64) / a.rb_h;
-  a.tr = (a.stage_bytes - 64) / a.rb_f;
-  if (a.tn < 1 || a.tr < 1)
-    return fail(NS_ERR_UNSUPPORTED, "ns_moe_decode_layer: rows of %d / %d bytes exceed the %d-byte stage", a.rb_h,
-                a.rb_f, a.stage_bytes);
-  a.tn = std::min(a.tn, 64);
-  a.tr = std::min(a.tr, 64);
-  // tile list bound
   {
     const int64_t n1 = (int64_t)plan.pairs_max * p->F;
     const int64_t t1 = (n1 / grid + 2) / a.tn + plan.pairs_max + 2;
     const int64_t t2 = ((int64_t)a.rows_cta_max / a.tr + 1) * plan.pairs_max;
     if (t1 + t2 > kMaxTiles) return fail(NS_ERR_UNSUPPORTED, "ns_moe_decode_layer: tile list too long");
   }
-  const size_t smem = (size_t)a.region_floats * 4 + align_up((size_t)p->T * a.rows_cta_max, 32) * 4 +
-                      (size_t)kMoeStages * a.stage_bytes + kMoeStages * 8 + sizeof(MoeShared);
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   switch (p->ggml_type) {
     case NS_GGML_MXFP4: return dispatch_moe_t<NS_GGML_MXFP4>(a, grid, smem, s);

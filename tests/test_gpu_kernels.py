@@ -78,8 +78,9 @@ def test_gemv_golden_cases():
 
 def _gemv_case(t, n, K, T, seed=1, offset=0, x_dtype=torch.float32, y_dtype=torch.float32):
     rb = row_bytes(t, K)
-    raw_all = synth.quant_bytes(t, seed, 5, 0, n * rb + offset + 16)
-    raw = raw_all[offset:offset + n * rb]
+    raw = synth.quant_bytes(t, seed, 5, 0, n * rb)
+    raw_all = np.zeros(n * rb + offset + 16, np.uint8)
+    raw_all[offset:offset + n * rb] = raw          # valid blocks starting off a 16-byte boundary
     x = synth.float_values(seed, 6, 0, T * K).reshape(T, K)
     dev_all = torch.from_numpy(raw_all).cuda()
     dev = dev_all[offset:offset + n * rb]          # a view with a storage offset

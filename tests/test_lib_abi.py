@@ -73,8 +73,8 @@ def _params(**kw):
 def test_moe_workspace_bytes_and_validation(lib):
     n = C.c_size_t(0)
     assert lib.ns_moe_workspace_bytes(C.byref(_params()), C.byref(n)) == 0
-    # barrier word + logits (T*E fp32) + activations (T*k*F fp32), 256-byte aligned pieces
-    assert n.value == 256 + 256 + 4 * 2880 * 4
+    # header (barrier word, activation maxima) + logits (T*E fp32) + activations (T*k*F fp32)
+    assert n.value == 1024 + 256 + 4 * 2880 * 4
     bad = [dict(T=0), dict(T=9), dict(k=0), dict(k=33), dict(n_expert=600), dict(expert_lo=4, expert_hi=4),
            dict(H=100), dict(route_mode=7), dict(act_mode=3), dict(ggml_type=int(GGMLType.Q5_K)),
            dict(router_dtype=9)]
