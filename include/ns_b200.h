@@ -176,6 +176,27 @@ int ns_moe_decode_layer(const ns_moe_layer_t* p, void* workspace, size_t workspa
                         ns_stream_t stream);
 
 /*
+ * ns_moe_decode_layer without a caller workspace and without any allocation.
+ * No counterpart in the reference (its Python layer allocates torch tensors
+ * per call); it exists for callers that cannot allocate device memory per
+ * call: a plain C / FFI host binding only this header, with no caching
+ * allocator, or a decoder whose weight cache has budgeted all free HBM --
+ * cudaMalloc/cudaFree there would synchronise the device mid-step and
+ * fragment that budget.
+ *
+ * Same computation and results as ns_moe_decode_layer; the scratch comes from
+ * one fixed array of NS_MOE_STATIC_SCRATCH_BYTES linked into the library, one
+ * per device.  A layer whose ns_moe_workspace_bytes exceeds that returns
+ * NS_ERR_SIZE without launching (T=1, k=4, F=2880, 128 experts needs 47,616).
+ * The first call on a device (that device current) resolves and clears the
+ * array and synchronises the device: make it before any stream capture.
+ * Calls that overlap on the GPU (unordered streams) race on the one array and
+ * give wrong results; calls ordered on one stream are safe.
+ */
+#define NS_MOE_STATIC_SCRATCH_BYTES (512 * 1024)
+int ns_moe_decode_layer_static(const ns_moe_layer_t* p, ns_stream_t stream);
+
+/*
  * Phase tracer of the fused layer (profiling aid; no reference counterpart --
  * the reference times with time.perf_counter around whole calls).  While set,
  * every ns_moe_decode_layer launch on the current device writes, per CTA,

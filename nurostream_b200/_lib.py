@@ -19,6 +19,7 @@ NS_ROUTE_TOPK_SOFTMAX, NS_ROUTE_SOFTMAX_TOPK_NORM = 0, 1
 NS_ACT_CLAMPED_SWIGLU, NS_ACT_SILU_MUL = 0, 1
 NS_SYNTH_F32, NS_SYNTH_BF16 = 1000, 1001
 NS_MAX_TOKENS, NS_MAX_TOPK, NS_MAX_EXPERTS = 8, 16, 512
+NS_MOE_STATIC_SCRATCH_BYTES = 512 * 1024
 DEVERR_GRID_WAIT, DEVERR_COPY_WAIT, DEVERR_ROUTE = 1, 2, 4
 
 _STATUS = {-1: "invalid argument", -2: "unsupported", -3: "buffer too small", -4: "CUDA error", -5: "timeout"}
@@ -62,6 +63,7 @@ SIGNATURES = {
     "ns_moe_workspace_bytes": (_I, [C.POINTER(MoeLayerParams), C.POINTER(_SZ)]),
     "ns_moe_workspace_init": (_I, [_P, _SZ, _P]),
     "ns_moe_decode_layer": (_I, [C.POINTER(MoeLayerParams), _P, _SZ, _P]),
+    "ns_moe_decode_layer_static": (_I, [C.POINTER(MoeLayerParams), _P]),
     "ns_synth_fill": (_I, [_P, _U64, _I, _U64, _U64, _U64, _F, _I, _I, _F, _P]),
     "ns_moe_set_trace": (_I, [_P, _SZ]),
 }

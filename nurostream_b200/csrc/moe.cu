@@ -22,6 +22,8 @@
 // reduce them in a fixed order (results are deterministic).  MXFP4 tiles run
 // on the tensor cores (mma_mxfp4.cuh); the K-quant formats use the CUDA-core
 // group decoders (qdot.cuh).  Every device wait is bounded.
+#include <mutex>
+
 #include "mma_mxfp4.cuh"
 #include "qdot.cuh"
 
@@ -1123,20 +1125,13 @@ extern "C" int ns_moe_workspace_init(void* workspace, size_t bytes, ns_stream_t 
   return NS_OK;
 }
 
-extern "C" int ns_moe_decode_layer(const ns_moe_layer_t* p, void* workspace, size_t workspace_bytes,
-                                   ns_stream_t stream) {
-  using namespace ns;
-  MoePlan plan;
-  int st = moe_validate(p, &plan);
-  if (st) return st;
-  if (!workspace || workspace_bytes < plan.ws_total)
-    return fail(NS_ERR_SIZE, "ns_moe_decode_layer: workspace of %zu bytes, need %zu", workspace_bytes, plan.ws_total);
-  if (reinterpret_cast<uintptr_t>(workspace) & 255)
-    return fail(NS_ERR_INVALID, "ns_moe_decode_layer: workspace must be 256-byte aligned");
-  if (!p->x || !p->out || !p->router_w || !p->gate_w || !p->up_w || !p->down_w)
-    return fail(NS_ERR_INVALID, "ns_moe_decode_layer: null tensor pointer");
+namespace ns {
+
+// Builds the launch arguments over a validated, 256-byte aligned scratch of at
+// least plan.ws_total bytes and launches the fused layer on `s`.
+static int moe_launch(const ns_moe_layer_t* p, const MoePlan& plan, uint8_t* ws, cudaStream_t s) {
   int nsm = 0;
-  st = num_sms(&nsm);
+  int st = num_sms(&nsm);
   if (st) return st;
 
   MoeArgs a;
@@ -1148,7 +1143,6 @@ extern "C" int ns_moe_decode_layer(const ns_moe_layer_t* p, void* workspace, siz
   a.gate_end = p->gate_w + (size_t)a.n_local * p->F * a.rb_h;
   a.up_end = p->up_w + (size_t)a.n_local * p->F * a.rb_h;
   a.down_end = p->down_w + (size_t)a.n_local * p->H * a.rb_f;
-  uint8_t* ws = reinterpret_cast<uint8_t*>(workspace);
   a.bar = reinterpret_cast<unsigned long long*>(ws);
   a.amax = reinterpret_cast<unsigned*>(ws + 64);
   a.logits = reinterpret_cast<float*>(ws + kWsHeader);
@@ -1167,11 +1161,99 @@ extern "C" int ns_moe_decode_layer(const ns_moe_layer_t* p, void* workspace, siz
     const int64_t t2 = ((int64_t)a.rows_cta_max / a.tr + 1) * plan.pairs_max;
     if (t1 + t2 > kMaxTiles) return fail(NS_ERR_UNSUPPORTED, "ns_moe_decode_layer: tile list too long");
   }
-  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   switch (p->ggml_type) {
     case NS_GGML_MXFP4: return dispatch_moe_t<NS_GGML_MXFP4>(a, grid, smem, s);
     case NS_GGML_Q8_0: return dispatch_moe_t<NS_GGML_Q8_0>(a, grid, smem, s);
     case NS_GGML_Q4_K: return dispatch_moe_t<NS_GGML_Q4_K>(a, grid, smem, s);
     default: return dispatch_moe_t<NS_GGML_Q6_K>(a, grid, smem, s);
   }
+}
+
+}  // namespace ns
+
+extern "C" int ns_moe_decode_layer(const ns_moe_layer_t* p, void* workspace, size_t workspace_bytes,
+                                   ns_stream_t stream) {
+  using namespace ns;
+  MoePlan plan;
+  int st = moe_validate(p, &plan);
+  if (st) return st;
+  if (!workspace || workspace_bytes < plan.ws_total)
+    return fail(NS_ERR_SIZE, "ns_moe_decode_layer: workspace of %zu bytes, need %zu", workspace_bytes, plan.ws_total);
+  if (reinterpret_cast<uintptr_t>(workspace) & 255)
+    return fail(NS_ERR_INVALID, "ns_moe_decode_layer: workspace must be 256-byte aligned");
+  if (!p->x || !p->out || !p->router_w || !p->gate_w || !p->up_w || !p->down_w)
+    return fail(NS_ERR_INVALID, "ns_moe_decode_layer: null tensor pointer");
+  return moe_launch(p, plan, reinterpret_cast<uint8_t*>(workspace), reinterpret_cast<cudaStream_t>(stream));
+}
+
+// ---------------------------------------------------------------------------------------------------------
+// Allocation-free variant: ns_moe_decode_layer_static.
+//
+// For callers that cannot allocate device memory per layer call: a plain C / FFI host that binds only this
+// library and has no caching allocator of its own, or a decoder whose weight cache has already budgeted
+// every free byte of HBM.  cudaMalloc / cudaFree would synchronise the device in the middle of a decode
+// step and fragment that budget, so this entry point takes its scratch (grid-barrier counter, activation
+// maxima, router logits, expert activations) from one fixed device array linked into the library instead
+// of a caller workspace.  It allocates nothing: no cudaMalloc, no cudaFree, no allocating library routine.
+//
+// Limit: a layer whose scratch (ns_moe_workspace_bytes) exceeds NS_MOE_STATIC_SCRATCH_BYTES is rejected
+// with NS_ERR_SIZE before anything is launched.
+//
+// Set-up: the first call on each device (with that device current) looks the array's address up with
+// cudaGetSymbolAddress and clears its header with a synchronous cudaMemset: the grid barrier counter must
+// start at zero, so that every launch's barrier targets are whole multiples of the grid.  That first call
+// synchronises the device and must come before any stream capture on the device.
+//
+// One array serves every call on a device: calls that overlap on the GPU (on different streams without an
+// ordering between them) race on the scratch and give wrong results.  Calls ordered on one stream are safe.
+// ---------------------------------------------------------------------------------------------------------
+
+static __device__ __align__(256) uint8_t g_moe_static_scratch[NS_MOE_STATIC_SCRATCH_BYTES];
+
+namespace ns {
+
+static std::mutex g_static_mu;
+static uint8_t* g_static_ptr[64] = {nullptr};
+
+// Address of this device's static scratch; the first call per device resolves and clears it.
+static int static_scratch(uint8_t** out) {
+  int dev = 0;
+  NS_CUDA_TRY(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= 64) return fail(NS_ERR_INVALID, "device ordinal %d out of range", dev);
+  std::lock_guard<std::mutex> lock(g_static_mu);
+  if (!g_static_ptr[dev]) {
+    void* ptr = nullptr;
+    cudaError_t e = cudaGetSymbolAddress(&ptr, g_moe_static_scratch);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaGetSymbolAddress(static MoE scratch)");
+    if (reinterpret_cast<uintptr_t>(ptr) & 255)
+      return fail(NS_ERR_CUDA, "static MoE scratch at %p is not 256-byte aligned", ptr);
+    e = cudaMemset(ptr, 0, kWsHeader);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaMemset(static MoE scratch header)");
+    e = cudaDeviceSynchronize();
+    if (e != cudaSuccess) return cuda_fail(e, "cudaDeviceSynchronize after clearing the static MoE scratch");
+    g_static_ptr[dev] = static_cast<uint8_t*>(ptr);
+  }
+  *out = g_static_ptr[dev];
+  return NS_OK;
+}
+
+}  // namespace ns
+
+extern "C" int ns_moe_decode_layer_static(const ns_moe_layer_t* p, ns_stream_t stream) {
+  using namespace ns;
+  MoePlan plan;
+  int st = moe_validate(p, &plan);
+  if (st) return st;
+  if (plan.ws_total > (size_t)NS_MOE_STATIC_SCRATCH_BYTES)
+    return fail(NS_ERR_SIZE,
+                "ns_moe_decode_layer_static: this layer needs %zu bytes of scratch (T=%d, k=%d, F=%d, "
+                "n_expert=%d); the static scratch holds %d (NS_MOE_STATIC_SCRATCH_BYTES). "
+                "Use ns_moe_decode_layer with a caller workspace",
+                plan.ws_total, p->T, p->k, p->F, p->n_expert, NS_MOE_STATIC_SCRATCH_BYTES);
+  if (!p->x || !p->out || !p->router_w || !p->gate_w || !p->up_w || !p->down_w)
+    return fail(NS_ERR_INVALID, "ns_moe_decode_layer_static: null tensor pointer");
+  uint8_t* ws = nullptr;
+  st = static_scratch(&ws);
+  if (st) return st;
+  return moe_launch(p, plan, ws, reinterpret_cast<cudaStream_t>(stream));
 }
