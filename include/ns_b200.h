@@ -197,6 +197,15 @@ int ns_moe_decode_layer(const ns_moe_layer_t* p, void* workspace, size_t workspa
 int ns_moe_decode_layer_static(const ns_moe_layer_t* p, ns_stream_t stream);
 
 /*
+ * Kernel choice of ns_moe_decode_layer (diagnostic and benchmarking aid; no
+ * reference counterpart).  0 (default): the tcgen05 tensor-core kernel for
+ * layers it takes (MXFP4 experts, T <= 2, H and F multiples of 64, 16-byte
+ * aligned expert tensors), the CUDA-core / mma.sync kernel otherwise; 1: always
+ * the latter; 2: the tensor-core kernel or NS_ERR_UNSUPPORTED.  Process-wide.
+ */
+int ns_moe_select_kernel(int path);
+
+/*
  * Phase tracer of the fused layer (profiling aid; no reference counterpart --
  * the reference times with time.perf_counter around whole calls).  While set,
  * every ns_moe_decode_layer launch on the current device writes, per CTA,

@@ -980,9 +980,23 @@ static int trace_slot() {
   return dev;
 }
 
+}  // namespace ns
+
+#include "moe_tc.cu"
+
+namespace ns {
+
+constexpr int kTcGridMax = 192;  // SMs the tensor-core workspace is sized for
+
+// Kernel choice: 0 = tensor-core kernel where the layer qualifies, 1 = always the
+// CUDA-core / mma.sync kernel, 2 = tensor-core kernel or NS_ERR_UNSUPPORTED.
+static int g_moe_path = 0;
+
 struct MoePlan {
   size_t ws_logits, ws_act, ws_total;
   int pairs_max;
+  bool tc_ok;
+  TcPlan tp;
 };
 
 static int moe_validate(const ns_moe_layer_t* p, MoePlan* plan) {
@@ -1010,6 +1024,11 @@ static int moe_validate(const ns_moe_layer_t* p, MoePlan* plan) {
   plan->ws_logits = align_up((size_t)p->T * p->n_expert * 4, 256);
   plan->ws_act = align_up((size_t)plan->pairs_max * p->F * 4, 256);
   plan->ws_total = kWsHeader + plan->ws_logits + plan->ws_act;
+  plan->tc_ok = moe_tc_eligible(p);
+  if (plan->tc_ok) {
+    moe_tc_plan(p, kTcGridMax, &plan->tp);
+    plan->ws_total = std::max(plan->ws_total, plan->tp.ws_total);
+  }
   return NS_OK;
 }
 
@@ -1096,6 +1115,12 @@ extern "C" int ns_moe_route(const void* h, int h_dtype, int T, int H, const void
   return NS_OK;
 }
 
+extern "C" int ns_moe_select_kernel(int path) {
+  if (path < 0 || path > 2) return ns::fail(NS_ERR_INVALID, "ns_moe_select_kernel: path %d outside 0..2", path);
+  ns::g_moe_path = path;
+  return NS_OK;
+}
+
 extern "C" int ns_moe_set_trace(uint64_t* buf, size_t bytes) {
   using namespace ns;
   int nsm = 0;
@@ -1133,6 +1158,15 @@ static int moe_launch(const ns_moe_layer_t* p, const MoePlan& plan, uint8_t* ws,
   int nsm = 0;
   int st = num_sms(&nsm);
   if (st) return st;
+  if (g_moe_path != 1) {
+    if (plan.tc_ok && moe_tc_aligned(p) && nsm <= kTcGridMax) {
+      TcPlan tp = plan.tp;
+      tp.grid = nsm;
+      return moe_tc_launch(p, tp, ws, s);
+    }
+    if (g_moe_path == 2)
+      return fail(NS_ERR_UNSUPPORTED, "ns_moe_decode_layer: layer does not qualify for the tensor-core kernel");
+  }
 
   MoeArgs a;
   memset(&a, 0, sizeof a);

@@ -1,0 +1,124 @@
+// Blackwell (sm_100a) tensor-core plumbing: TMEM allocation, UMMA descriptors,
+// block-scaled MXF4 MMAs (tcgen05.mma ... kind::mxf4.block_scale.block32),
+// tensor-memory loads, TMA tile loads and the cross-proxy fences they need.
+//
+// Operand layout (SWIZZLE_NONE, K-major): a core matrix is 8 rows x 16 bytes
+// (32 e2m1 values per row) stored contiguously; `lbo` is the byte distance
+// between core matrices adjacent in K, `sbo` between core matrices adjacent in
+// M/N.  One MMA consumes K = 64 (two core matrices along K).
+//
+// Scale factors (UE8M0, one per row per 32-element block) live in TMEM.  They
+// are copied from shared memory with tcgen05.cp.32x128b.warpx4, whose source
+// "atom" is 32 rows x 16 bytes: byte 16*(m%32) + 4*(m/32) + (kb%4) holds the
+// scale of row m, block kb of a 4-block group.  The copy fills 4 TMEM columns
+// (replicated over the 4 lane quadrants); an MMA addresses its two blocks with
+// the atom's first column and a byte selector (0 or 2) carried both in the
+// instruction descriptor and in bits 30-31 of the scale address.  The atom's
+// first column must be a multiple of 4.
+#pragma once
+
+#include <cuda.h>
+
+#include "common.cuh"
+
+namespace ns {
+
+__device__ __forceinline__ void tmem_alloc(uint32_t* slot_smem, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_addr(slot_smem)),
+               "r"(ncols)
+               : "memory");
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+
+__device__ __forceinline__ void tc_fence_before() {
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tc_fence_after() {
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+
+// Generic-proxy writes to shared memory -> visible to the tensor core / TMA (async proxy).
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+__device__ __forceinline__ uint64_t umma_desc(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
+  uint64_t d = 0;
+  d |= (uint64_t)((saddr >> 4) & 0x3FFFu);
+  d |= (uint64_t)((lbo >> 4) & 0x3FFFu) << 16;
+  d |= (uint64_t)((sbo >> 4) & 0x3FFFu) << 32;
+  d |= (uint64_t)1 << 46;  // descriptor version of sm_100
+  return d;                // base offset 0, absolute LBO mode, SWIZZLE_NONE
+}
+
+// Instruction descriptor of kind::mxf4 (E2M1 x E2M1, UE8M0 scales, fp32 accumulate, K = 64).
+__host__ __device__ __forceinline__ uint32_t idesc_mxf4(int M, int N, int sfa_id, int sfb_id) {
+  uint32_t d = 0;
+  d |= (uint32_t)(sfb_id & 3) << 4;
+  d |= 1u << 7;   // A format E2M1
+  d |= 1u << 10;  // B format E2M1
+  d |= (uint32_t)(N >> 3) << 17;
+  d |= 1u << 23;  // scale format UE8M0
+  d |= (uint32_t)(M >> 4) << 24;
+  d |= (uint32_t)(sfa_id & 3) << 29;
+  return d;
+}
+
+__device__ __forceinline__ void tc_cp_sf(uint32_t tcol, uint64_t sdesc) {
+  asm volatile("tcgen05.cp.cta_group::1.32x128b.warpx4 [%0], %1;" ::"r"(tcol), "l"(sdesc) : "memory");
+}
+
+// D[tmem] (+)= A[smem] x B[smem]^T with per-block scales; `acc` = 0 overwrites D.
+__device__ __forceinline__ void mma_mxf4(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                         uint32_t tsfa, uint32_t tsfb, uint32_t acc) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+      " tcgen05.mma.cta_group::1.kind::mxf4.block_scale.block32 [%0], %1, %2, %3, [%5], [%6], p;\n}"
+      ::"r"(tmem_d), "l"(adesc), "l"(bdesc), "r"(idesc), "r"(acc), "r"(tsfa), "r"(tsfb)
+      : "memory");
+}
+
+// Arrive on `bar` once every tcgen05 operation this thread issued so far has completed.
+__device__ __forceinline__ void tc_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_addr(bar))
+               : "memory");
+}
+
+// 32 lanes x 8 / 16 consecutive 32-bit columns (lane = TMEM lane 32*(warp%4) + laneid).
+__device__ __forceinline__ void tmem_ld_x8(uint32_t taddr, uint32_t (&v)[8]) {
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+               : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7])
+               : "r"(taddr));
+}
+__device__ __forceinline__ void tmem_ld_x16(uint32_t taddr, uint32_t (&v)[16]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+      : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]),
+        "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15])
+      : "r"(taddr));
+}
+__device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
+// 2-D TMA tile load (no multicast) of box [x, y] of `tmap` into shared memory, completing on `bar`.
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* tmap, int x, int y, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];"
+      ::"r"(smem_addr(dst)), "l"(reinterpret_cast<uint64_t>(tmap)), "r"(x), "r"(y), "r"(smem_addr(bar))
+      : "memory");
+}
+
+__device__ __forceinline__ void prefetch_tmap(const CUtensorMap* tmap) {
+  asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(tmap)) : "memory");
+}
+
+__device__ __forceinline__ uint32_t ld_acquire_u32(const unsigned* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+}  // namespace ns

@@ -74,7 +74,15 @@ def test_moe_workspace_bytes_and_validation(lib):
     n = C.c_size_t(0)
     assert lib.ns_moe_workspace_bytes(C.byref(_params()), C.byref(n)) == 0
     # header (barrier word, activation maxima) + logits (T*E fp32) + activations (T*k*F fp32)
-    assert n.value == 1024 + 256 + 4 * 2880 * 4
+    # MXFP4, T <= 2: the larger of the two kernels' workspaces.  CUDA-core kernel: header
+    # (barrier word, activation maxima) + logits (T*E fp32) + activations (T*k*F fp32).
+    # Tensor-core kernel: header with counters + logits + split-tile partials (192 SMs x 2 x T x 128
+    # fp32) + activation planes per pair (90 blocks x (128 + 8) B, 256-aligned) + down outputs per pair.
+    v2 = 1024 + 256 + 4 * 2880 * 4
+    tc = 16384 + 256 + 192 * 2 * 128 * 4 + 4 * 12288 + 4 * 2880 * 4
+    assert n.value == max(v2, tc)
+    assert lib.ns_moe_workspace_bytes(C.byref(_params(ggml_type=int(GGMLType.Q8_0))), C.byref(n)) == 0
+    assert n.value == v2
     bad = [dict(T=0), dict(T=9), dict(k=0), dict(k=33), dict(n_expert=600), dict(expert_lo=4, expert_hi=4),
            dict(H=100), dict(route_mode=7), dict(act_mode=3), dict(ggml_type=int(GGMLType.Q5_K)),
            dict(router_dtype=9)]
