@@ -193,7 +193,7 @@ int ns_moe_decode_layer(const ns_moe_layer_t* p, void* workspace, size_t workspa
  * Calls that overlap on the GPU (unordered streams) race on the one array and
  * give wrong results; calls ordered on one stream are safe.
  */
-#define NS_MOE_STATIC_SCRATCH_BYTES (512 * 1024)
+#define NS_MOE_STATIC_SCRATCH_BYTES (1024 * 1024)
 int ns_moe_decode_layer_static(const ns_moe_layer_t* p, ns_stream_t stream);
 
 /*

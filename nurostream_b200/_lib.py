@@ -19,7 +19,7 @@ NS_ROUTE_TOPK_SOFTMAX, NS_ROUTE_SOFTMAX_TOPK_NORM = 0, 1
 NS_ACT_CLAMPED_SWIGLU, NS_ACT_SILU_MUL = 0, 1
 NS_SYNTH_F32, NS_SYNTH_BF16 = 1000, 1001
 NS_MAX_TOKENS, NS_MAX_TOPK, NS_MAX_EXPERTS = 8, 16, 512
-NS_MOE_STATIC_SCRATCH_BYTES = 512 * 1024
+NS_MOE_STATIC_SCRATCH_BYTES = 1024 * 1024
 DEVERR_GRID_WAIT, DEVERR_COPY_WAIT, DEVERR_ROUTE = 1, 2, 4
 
 _STATUS = {-1: "invalid argument", -2: "unsupported", -3: "buffer too small", -4: "CUDA error", -5: "timeout"}

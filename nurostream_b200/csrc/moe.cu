@@ -986,8 +986,6 @@ static int trace_slot() {
 
 namespace ns {
 
-constexpr int kTcGridMax = 192;  // SMs the tensor-core workspace is sized for
-
 // Kernel choice: 0 = tensor-core kernel where the layer qualifies, 1 = always the
 // CUDA-core / mma.sync kernel, 2 = tensor-core kernel or NS_ERR_UNSUPPORTED.
 static int g_moe_path = 0;

@@ -20,18 +20,26 @@
 //     split), and digit d is the e2m1 value d/2 with block scale 2^(3p+e-22).
 //   * D accumulates in fp32 in TMEM; the epilogue adds the 8 plane columns.
 //
-// Work.  Phase 1 tiles are 64-neuron slabs of one routed expert (64 gate rows
-// + 64 up rows = M); phase 2 tiles are 128 down rows of one (token, expert)
-// pair.  The concatenated K-blocks of all tiles are split evenly over the CTAs
-// at 8-block chunk boundaries ("stream-K"), so every SM streams the same
-// number of weight bytes.  A tile split over CTAs is finished by the last one
-// to arrive (fixed summation order, so results are deterministic).  Phase 2
-// of expert e starts as soon as all slabs of e are done (per-expert counters);
-// the combine of a row block runs when all of its pairs are done.  No grid
+// Staging.  A K-chunk of a tile is 14 blocks (238 bytes) of 128 rows.  Rows
+// r, r+8, .. of one tile share their alignment (8 GGUF rows of a 64-multiple
+// width are a 16-byte multiple), so one TMA box of 256 bytes x 16 row groups
+// fetches row phase j of the chunk; 8 boxes (4 KB each) fill a stage.  Repack
+// warps move each 17-byte block into the operand layout.
+//
+// Work.  A phase-1 tile is 128 neurons of one routed expert; its K runs over
+// the gate rows and then the up rows (separate accumulators), so the
+// activation of a neuron sees both in one thread.  A phase-2 tile is 128 down
+// rows of one (token, expert) pair.  Each phase's K blocks are split evenly
+// over the CTAs at chunk boundaries ("stream-K"), so every SM streams the same
+// number of weight bytes; a CTA streams its phase-1 share, then its phase-2
+// share.  A tile split over CTAs is finished by the last one to arrive, in a
+// fixed summation order, so results are deterministic.  Phase 2 of expert e
+// starts as soon as all tiles of e are done (per-expert counters); the
+// combine of a row block runs when all of its pairs are done.  No grid
 // barrier follows the routing barrier.
 //
-// Warps: 0 producer (TMA), 1 MMA issuer, 2..9 repack raw rows into the
-// operand layout, 10..13 epilogue (TMEM -> registers, finish tiles).  Every
+// Warps: 0 producer (TMA), 1 MMA issuer, 2..13 repack raw rows into the
+// operand layout, 14..17 epilogue (TMEM -> registers, finish tiles).  Every
 // wait is bounded; a wait that runs out raises a device error bit, stops the
 // CTA's pipeline, lets in-flight copies and MMAs land, frees TMEM and returns.
 
@@ -39,43 +47,59 @@
 
 namespace ns {
 
-constexpr int kTcWarps = 14;
+constexpr int kTcWarps = 18;
 constexpr int kTcThreads = kTcWarps * 32;
-constexpr int kTcRepackWarp0 = 2, kTcRepackWarps = 8, kTcEpiWarp0 = 10;
-constexpr int kTcRawStages = 4, kTcCanStages = 3;
-constexpr int kTcChunk = 8;                          // K blocks (32 elements) per chunk
-constexpr int kTcBoxW = 160;                         // TMA box width (bytes): >= 8*17 + 14, multiple of 16
-constexpr int kTcBoxBytes = kTcBoxW * 8;             // 8 row groups per box
-constexpr int kTcRawBytes = 16 * kTcBoxBytes;        // 2 halves x 8 row phases
-constexpr int kTcCanA = 16 * kTcChunk * 128;         // 16 row groups x 8 blocks x 128 B
-constexpr int kTcCanSFA = 2 * 512;
-constexpr int kTcCanB = kTcChunk * 128;              // phase-2 B: 8 planes x 8 blocks
-constexpr int kTcCanSFB = 2 * 512;
+constexpr int kTcRepackWarps = 12;
+// Warp roles.  Warp w issues from SM sub-partition w % 4; the MMA issuer (1) shares its
+// sub-partition only with the producer (5), one epilogue warp (13) and two repack warps, so its
+// instruction stream is not starved.  The epilogue has one warp per TMEM lane quadrant (w % 4).
+constexpr int kTcMmaWarp = 1, kTcProducerWarp = 5;
+__device__ __forceinline__ int tc_epi_quadrant(int w) {
+  return w == 16 ? 0 : w == 13 ? 1 : w == 14 ? 2 : w == 15 ? 3 : -1;
+}
+__device__ __forceinline__ int tc_repack_index(int w) {
+  // warps 0,2,3,4,6,7,8,9,10,11,12,17 -> 0..11
+  return w == 17 ? 11 : (w == 1 || w == 5 || w >= 13) ? -1 : w == 0 ? 0 : w < 5 ? w - 1 : w - 2;
+}
+constexpr int kTcRawStages = 3, kTcCanStages = 2;
+constexpr int kTcChunk = 14;                         // K blocks (32 elements) per chunk
+constexpr int kTcBoxW = 256;                         // TMA box width (bytes): >= 14*17 + 14
+constexpr int kTcBoxRows = 16;                       // row groups per box (8 for half tiles)
+constexpr int kTcBoxBytes = kTcBoxW * kTcBoxRows;    // one row phase of a chunk
+constexpr int kTcRawBytes = 8 * kTcBoxBytes;         // 8 row phases
+constexpr int kTcCanA = 16 * kTcChunk * 128;         // 16 row groups x 14 blocks x 128 B
+constexpr int kTcCanSFA = 4 * 512;                   // 4 scale atoms of 4 blocks
+constexpr int kTcCanB = 16 * 128;                    // phase-2 B: 8 planes x 14 blocks (+pad)
+constexpr int kTcCanSFB = 4 * 512;
 constexpr int kTcCanBytes = kTcCanA + kTcCanSFA + kTcCanB + kTcCanSFB;
-constexpr int kTcTmemCols = 128;                     // D: 2 x 16 cols; SF: 3 stages x 16 cols
+constexpr int kTcDCols = 32;                         // D: gate planes at +0, up planes at +16
+constexpr int kTcTmemCols = 128;                     // D: 2 x 32 cols; SF: 2 stages x 32 cols
 constexpr int kTcMaxSegs = 8;                        // tiles one CTA touches
-constexpr int kTcMaxSplit = 16;                      // CTAs one tile is split over
-constexpr int kTcMaxTiles = 2048;
-constexpr int kTcWsHeader = 16384;                   // barrier word, counters
-constexpr int kTcOffCnt = 1024, kTcOffReady = 1024 + 4 * kTcMaxTiles, kTcOffCnt2 = kTcOffReady + 4 * 128;
+constexpr int kTcMaxSplit = 24;                      // CTAs one tile is split over
+constexpr int kTcMaxTiles = 1024;
+constexpr int kTcWsHeader = 8192;                    // barrier word, counters
+constexpr int kTcOffCnt = 1024, kTcOffReady = kTcOffCnt + 4 * kTcMaxTiles, kTcOffCnt2 = kTcOffReady + 4 * 128;
 constexpr int kTcMaxRowTiles = (kTcWsHeader - kTcOffCnt2) / 4;
 constexpr int kTcSmemBudget = 225 * 1024;
+constexpr int kTcGridMax = 160;                      // SMs the workspace is sized for
 
 struct MoeTcArgs {
-  CUtensorMap tm_gate, tm_up, tm_down;  // 8-row groups x 8*row_bytes bytes, box 160 x 8
+  // 8-row groups x 8*row_bytes bytes; box 256 x 16 (full tiles) and 256 x 8 (half tiles)
+  CUtensorMap tm_gate16, tm_gate8, tm_up16, tm_up8, tm_down16, tm_down8;
   ns_moe_layer_t p;
   int rb_h, rb_f, nb_h, nb_f;
   unsigned long long* bar;
   unsigned* cnt;     // per tile: segments finished
-  unsigned* ready;   // per slot: phase-1 slabs finished
+  unsigned* ready;   // per slot: phase-1 tiles finished
   unsigned* cnt2;    // per phase-2 row tile: pairs finished
   float* logits;     // T x E
-  float* partial;    // [G][2][T][128]
+  float* partial;    // per CTA: 2 phase-1 slots of 2*T*128 floats, then 2 phase-2 slots of 128
+  int part_floats;   // floats per CTA: (4*T + 2) * 128
   uint8_t* actimg;   // per pair: planes [nb_f][8][16] then scales [nb_f][8]
   float* yp;         // per pair: H fp32
   int img_bytes;
   int zero_tiles;    // counters to clear per launch
-  int off_raw, off_b1, off_sfb1, off_can, off_xchg, off_bars, off_shared;
+  int off_raw, off_b1, off_sfb1, off_can, off_bars, off_shared;
   int sfb1_atom;     // bytes between phase-1 scale atoms (128 * T)
   unsigned long long* trace;
 };
@@ -85,7 +109,8 @@ struct TcSeg {
   int nsplit;                  // CTAs sharing the tile
   short split_cta[kTcMaxSplit];
   char split_slot[kTcMaxSplit];
-  int my_slot;                 // this CTA's partial slot (0 first segment, 1 last)
+  int my_slot;                 // this CTA's partial slot: 2*phase + (0 first segment of the phase, 1 last)
+  int grp, sub;                // slot (phase 1) or pair (phase 2), and 128-row block within it
 };
 
 struct TcShared {
@@ -108,23 +133,40 @@ struct TcShared {
   int nseg;
   TcSeg seg[kTcMaxSegs];
   int fin;
-  int bnd[1025];  // CTA range boundaries in K blocks (grid <= 1024)
+  int win[2][64];  // range starts of CTAs c-31 .. c+32 in each phase (tile-major K blocks)
   __align__(16) float scratch[NS_MAX_EXPERTS];
 };
 
-// Geometry of the tile list: phase-1 slabs (slot-major), then phase-2 row tiles (pair-major).
+// Geometry: phase-1 tiles (slot-major, 128 neurons, K = gate nb_h blocks then up nb_h blocks),
+// then phase-2 tiles (pair-major, 128 down rows, K = nb_f blocks).
 struct TcGeom {
-  int T1, T2, ns1, nr2, nb_h, nb_f;
-  __device__ int64_t start(int i) const {
-    return i < T1 ? (int64_t)i * nb_h : (int64_t)T1 * nb_h + (int64_t)(i - T1) * nb_f;
+  int T1, T2, ns1, nr2, nb_h, nb_f, H, F;
+  __device__ int len(int ph) const { return ph == 0 ? 2 * nb_h : nb_f; }
+  // K blocks of the half that block kb belongs to, and the half's first block
+  __device__ void half_of(int ph, int kb, int* h0, int* hl) const {
+    if (ph == 0 && kb >= nb_h) { *h0 = nb_h; *hl = nb_h; }
+    else { *h0 = 0; *hl = ph == 0 ? nb_h : nb_f; }
   }
-  __device__ int len(int i) const { return i < T1 ? nb_h : nb_f; }
-  __device__ int tile_of(int64_t u) const {
-    const int64_t u1 = (int64_t)T1 * nb_h;
-    return u < u1 ? (int)(u / nb_h) : T1 + (int)((u - u1) / nb_f);
+  // nearest chunk start to tile-local block `off` (chunks restart at each half)
+  __device__ int snap(int ph, int off) const {
+    int h0, hl;
+    half_of(ph, off, &h0, &hl);
+    const int w = off - h0;
+    return h0 + min(hl, ((w + kTcChunk / 2) / kTcChunk) * kTcChunk);
   }
-  __device__ int64_t total() const { return (int64_t)T1 * nb_h + (int64_t)T2 * nb_f; }
+  // 8-row groups of a tile holding real rows (16, or 8 for a last half tile)
+  __device__ int groups(int tile) const {
+    const int rows = tile < T1 ? F - 128 * (tile % ns1) : H - 128 * ((tile - T1) % nr2);
+    return rows >= 128 ? 16 : rows / 8;
+  }
 };
+
+// Partial-sum slot `slot` (2*phase + first/last) of CTA `cta`.
+template <int NT>
+__device__ __forceinline__ float* tc_partial(float* base, int part_floats, int cta, int slot) {
+  float* b = base + (size_t)cta * part_floats;
+  return slot < 2 ? b + slot * (2 * NT * 128) : b + 2 * (2 * NT * 128) + (slot - 2) * 128;
+}
 
 __device__ __forceinline__ bool tc_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag) {
   if (mbar_try_wait(bar, parity)) return true;
@@ -193,6 +235,27 @@ __device__ __forceinline__ void halfwarp_block_planes(float v0, float v1, uint8_
     for (int p = 0; p < 8; ++p) sdst[p * sstride] = (uint8_t)plane_scale(p, e, nz);
 }
 
+// Phase-1 B operand: the digit planes of h = (x * r) * norm_w, built from L2 by 16 warps (32
+// half-warps, index hw) while the first weight chunks are in flight.  Token t's planes are rows
+// 8t..8t+7: core matrix (t, block b) at b1 + t*nb_h*128 + b*128; scale atom b/4 at
+// sfb1 + (b/4)*sfb1_atom, byte 16*(8t+p) + b%4.
+__device__ __forceinline__ void tc_build_b1(const ns_moe_layer_t& p, int T, int nb_h, const float* rscale, uint8_t* b1,
+                                            uint8_t* sfb1, int sfb1_atom, int hw, int lane) {
+  const int hl = lane & 15;
+  const unsigned mask = 0xFFFFu << (lane & 16);
+  for (int it = hw; it < T * nb_h; it += 32) {
+    const int t = it / nb_h, b = it - t * nb_h;
+    const int64_t i0 = (int64_t)t * p.H + 32 * b + hl;
+    float v0 = p.x[i0], v1 = p.x[i0 + 16];
+    if (p.norm_w) {
+      v0 = __fmul_rn(__fmul_rn(v0, rscale[t]), p.norm_w[32 * b + hl]);
+      v1 = __fmul_rn(__fmul_rn(v1, rscale[t]), p.norm_w[32 * b + hl + 16]);
+    }
+    halfwarp_block_planes(v0, v1, b1 + (size_t)t * nb_h * 128 + b * 128,
+                          sfb1 + (b >> 2) * sfb1_atom + 16 * (8 * t) + (b & 3), 16, hl, mask);
+  }
+}
+
 template <int NT>
 __global__ void __launch_bounds__(kTcThreads, 1) moe_tc_kernel(const __grid_constant__ MoeTcArgs a) {
   extern __shared__ __align__(1024) uint8_t smem[];
@@ -205,7 +268,6 @@ __global__ void __launch_bounds__(kTcThreads, 1) moe_tc_kernel(const __grid_cons
   uint8_t* b1 = smem + a.off_b1;
   uint8_t* sfb1 = smem + a.off_sfb1;
   uint8_t* can = smem + a.off_can;
-  float* xchg = reinterpret_cast<float*>(smem + a.off_xchg);
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + a.off_bars);
   uint64_t* full_raw = bars;
   uint64_t* empty_raw = full_raw + kTcRawStages;
@@ -214,6 +276,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) moe_tc_kernel(const __grid_cons
   uint64_t* full_d = empty_can + kTcCanStages;
   uint64_t* empty_d = full_d + 2;
   uint64_t* mma_done = empty_d + 2;
+  uint64_t* b1_ready = mma_done + 1;  // phase-1 activation planes built (16 builder warps)
   TcShared& S = *reinterpret_cast<TcShared*>(smem + a.off_shared);
   volatile int* abort_flag = &S.abort_flag;
 
@@ -232,15 +295,16 @@ __global__ void __launch_bounds__(kTcThreads, 1) moe_tc_kernel(const __grid_cons
       mbar_init(&empty_d[s], 4);
     }
     mbar_init(mma_done, 1);
+    mbar_init(b1_ready, kTcRepackWarps + 4);
     fence_mbar_init();
     // TMA boxes and operand tiles assume a 1024-byte aligned dynamic shared-memory base
     S.abort_flag = (smem_addr(smem) & 1023u) != 0;
     if (S.abort_flag) raise_device_error(NS_DEVERR_COPY_WAIT);
-    prefetch_tmap(&a.tm_gate);
-    prefetch_tmap(&a.tm_up);
-    prefetch_tmap(&a.tm_down);
+    prefetch_tmap(&a.tm_gate16);
+    prefetch_tmap(&a.tm_up16);
+    prefetch_tmap(&a.tm_down16);
   }
-  if (warp == 1) tmem_alloc(&S.tmem_base, kTcTmemCols);
+  if (warp == kTcMmaWarp) tmem_alloc(&S.tmem_base, kTcTmemCols);
   // counters of this launch (used only after the routing barrier)
   if (c == 0) {
     for (int i = tid; i < a.zero_tiles; i += kTcThreads) a.cnt[i] = 0u;
@@ -253,13 +317,25 @@ __global__ void __launch_bounds__(kTcThreads, 1) moe_tc_kernel(const __grid_cons
   const bool own_expert = c < E;
   for (int t = 0; t < T; ++t) {
     float ss = 0.f, dot = 0.f;
-    for (int i = tid; i < H; i += kTcThreads) {
-      const float xv = p.x[(int64_t)t * H + i];
-      const float wv = p.norm_w ? p.norm_w[i] : 1.0f;
-      const float rv = own_expert ? load_float(p.router_w, p.router_dtype, (int64_t)c * H + i) : 0.f;
-      h[t * H + i] = xv;
-      ss = fmaf(xv, xv, ss);
-      dot = fmaf(xv * wv, rv, dot);
+    for (int i0 = tid; i0 < H; i0 += 8 * kTcThreads) {  // 8 loads in flight per thread, then the sums in order
+      float xv[8], wv[8], rv[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        const int i = i0 + u * kTcThreads;
+        const bool ok = i < H;
+        xv[u] = ok ? p.x[(int64_t)t * H + i] : 0.f;
+        wv[u] = ok && p.norm_w ? p.norm_w[i] : 1.0f;
+        rv[u] = ok && own_expert ? load_float(p.router_w, p.router_dtype, (int64_t)c * H + i) : 0.f;
+      }
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        const int i = i0 + u * kTcThreads;
+        if (i < H) {
+          h[t * H + i] = xv[u];
+          ss = fmaf(xv[u], xv[u], ss);
+          dot = fmaf(xv[u] * wv[u], rv[u], dot);
+        }
+      }
     }
     ss = warp_sum(ss);
     dot = warp_sum(dot);
@@ -281,9 +357,16 @@ __global__ void __launch_bounds__(kTcThreads, 1) moe_tc_kernel(const __grid_cons
   }
   __syncthreads();
   if (p.norm_w)
-    for (int t = 0; t < T; ++t) {
-      const float r = S.rscale[t];
-      for (int i = tid; i < H; i += kTcThreads) h[t * H + i] = __fmul_rn(__fmul_rn(h[t * H + i], r), p.norm_w[i]);
+    for (int i0 = tid; i0 < H; i0 += 8 * kTcThreads) {
+      float wv[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) wv[u] = i0 + u * kTcThreads < H ? p.norm_w[i0 + u * kTcThreads] : 0.f;
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        const int i = i0 + u * kTcThreads;
+        if (i < H)
+          for (int t = 0; t < T; ++t) h[t * H + i] = __fmul_rn(__fmul_rn(h[t * H + i], S.rscale[t]), wv[u]);
+      }
     }
   __syncthreads();
   if (tid == 0) stamp(a.trace, kEvNorm);
@@ -310,26 +393,12 @@ __global__ void __launch_bounds__(kTcThreads, 1) moe_tc_kernel(const __grid_cons
     __syncthreads();
   }
 
-  // ---- 2. split-phase grid barrier around the build of the phase-1 activation planes
+  // ---- 2. grid barrier: every CTA's router logit is in the workspace
   if (tid == 0) {
     stamp(a.trace, kEvRouter);
     __threadfence();
     const unsigned long long old = atomicAdd(a.bar, 1ull);
     S.bar_target = (old / (unsigned)G + 1ull) * (unsigned)G;
-  }
-  {
-    // B1: token t's planes are rows 8t..8t+7; core matrix (t, block b) at t*nb_h*128 + b*128.
-    // SFB1: atom b/4 at (b/4)*sfb1_atom, byte 16*(8t+p) + b%4.
-    const int nb = a.nb_h;
-    const int half = (tid >> 4), hl = tid & 15;
-    const unsigned mask = 0xFFFFu << (lane & 16);
-    for (int it = half; it < T * nb; it += kTcThreads / 16) {
-      const int t = it / nb, b = it - t * nb;
-      const float* hv = h + t * H + 32 * b;
-      uint8_t* dst = b1 + (size_t)t * nb * 128 + b * 128;
-      uint8_t* sdst = sfb1 + (b >> 2) * a.sfb1_atom + 16 * (8 * t) + (b & 3);
-      halfwarp_block_planes(hv[hl], hv[hl + 16], dst, sdst, 16, hl, mask);
-    }
   }
   if (tid == 0) {
     S.ok = 1;
@@ -396,139 +465,179 @@ __global__ void __launch_bounds__(kTcThreads, 1) moe_tc_kernel(const __grid_cons
       }
     }
     __syncthreads();
-    if (warp == 0) {
-      const float v = lane < k ? S.topv[t][lane] : 0.f;
-      float wgt;
-      if (p.route_mode == NS_ROUTE_TOPK_SOFTMAX) {
-        // softmax over the k (neurostream/model/gpt_oss.py:119-120)
-        const float mx = S.topv[t][0];
-        const float ex = lane < k ? expf(v - mx) : 0.f;
-        wgt = ex / warp_sum(ex);
-      } else {
-        wgt = v / warp_sum(v);  // renormalise the top-k probabilities (router.py:66-68)
-      }
-      if (lane < k) S.w[t][lane] = wgt;
-    }
-    __syncthreads();
   }
   if (tid == 0) stamp(a.trace, kEvTopk);
 
-  // ---- 4. slots (distinct local experts, ascending) and pairs (slot-major, token ascending)
-  if (tid == 0) {
-    int n = 0;
-    for (int t = 0; t < T; ++t)
-      for (int j = 0; j < k; ++j) {
-        const int e = S.ids[t][j];
-        if (e < p.expert_lo || e >= p.expert_hi) continue;
-        bool seen = false;
-        for (int q = 0; q < n; ++q) seen |= S.slot_expert[q] == e;
-        if (!seen) S.slot_expert[n++] = e;
-      }
-    for (int i = 1; i < n; ++i) {  // insertion sort, n <= T*k
-      const int v = S.slot_expert[i];
-      int j = i - 1;
-      while (j >= 0 && S.slot_expert[j] > v) {
-        S.slot_expert[j + 1] = S.slot_expert[j];
-        --j;
-      }
-      S.slot_expert[j + 1] = v;
+  // ---- 4 + 5, in parallel: warp 0 finishes routing (weights, slots, pairs); warp 1 derives this
+  // CTA's work.  Lane l = t*k + j holds routed expert (t, j); T*k <= 32 for this kernel.
+  if (warp == 0 || warp == 1) {
+    const int nall = T * k;
+    const bool act = lane < nall;
+    const int t = (T == 2 && lane >= k) ? 1 : 0, j = lane - t * k;
+    const int e = act ? S.ids[t][j] : 0x7FFFFFFF;
+    const bool loc = act && e >= p.expert_lo && e < p.expert_hi;
+    int less_local = 0, same_before = 0;
+    for (int l2 = 0; l2 < nall; ++l2) {
+      const int e2 = __shfl_sync(0xffffffffu, e, l2);
+      if (e2 < p.expert_lo || e2 >= p.expert_hi) continue;
+      less_local += e2 < e;
+      same_before += (e2 == e && l2 < lane);
     }
-    int np = 0;
-    for (int s = 0; s < n; ++s) {
-      S.slot_pair0[s] = np;
-      for (int t = 0; t < T; ++t)
-        for (int j = 0; j < k; ++j)
-          if (S.ids[t][j] == S.slot_expert[s]) {
-            S.pair_token[np] = t;
-            S.pair_w[np] = S.w[t][j];
-            S.pair_slot[np] = s;
-            ++np;
-          }
-    }
-    S.slot_pair0[n] = np;
-    S.nslots = n;
-    S.npairs = np;
-  }
-  if (c == 0 && warp == 0)
-    for (int i = lane; i < T * k; i += 32) {
-      if (p.ids) p.ids[i] = S.ids[i / k][i % k];
-      if (p.weights) p.weights[i] = S.w[i / k][i % k];
-    }
-  __syncthreads();
-
-  TcGeom geo;
-  geo.ns1 = F / 64;
-  geo.nr2 = (H + 127) / 128;
-  geo.T1 = S.nslots * geo.ns1;
-  geo.T2 = S.npairs * geo.nr2;
-  geo.nb_h = a.nb_h;
-  geo.nb_f = a.nb_f;
-  const int64_t U = geo.total();
-
-  // ---- 5. CTA ranges (K blocks, snapped to chunk boundaries) and this CTA's segments
-  for (int j = tid; j <= G; j += kTcThreads) {
-    int64_t b;
-    if (j == G || U == 0) {
-      b = j == G ? U : 0;
-    } else {
-      const int64_t u = U * j / G;
-      const int i = geo.tile_of(u);
-      const int64_t s0 = geo.start(i);
-      const int L = geo.len(i);
-      const int off = (int)(u - s0);
-      b = s0 + min(L, ((off + kTcChunk / 2) / kTcChunk) * kTcChunk);
-    }
-    S.bnd[j] = (int)b;
-  }
-  __syncthreads();
-  if (tid == 0) {
-    int ns = 0;
-    int64_t u = S.bnd[c];
-    const int64_t uend = S.bnd[c + 1];
-    while (u < uend && ns < kTcMaxSegs) {
-      const int i = geo.tile_of(u);
-      const int64_t s0 = geo.start(i), e0 = s0 + geo.len(i);
-      TcSeg& sg = S.seg[ns];
-      sg.tile = i;
-      sg.k0 = (int)(u - s0);
-      sg.k1 = (int)(min(e0, uend) - s0);
-      sg.my_slot = ns == 0 ? 0 : 1;
-      // CTAs sharing tile i, ascending: first one whose range contains s0, then on while ranges start before e0
-      int lo = 0, hi = G - 1;
-      while (lo < hi) {  // largest cc with bnd[cc] <= s0
-        const int mid = (lo + hi + 1) >> 1;
-        if (S.bnd[mid] <= s0) lo = mid; else hi = mid - 1;
-      }
-      int nsp = 0;
-      for (int cc = lo; cc < G && S.bnd[cc] < e0; ++cc) {
-        if (S.bnd[cc + 1] <= S.bnd[cc] || S.bnd[cc + 1] <= s0) continue;  // empty or before the tile
-        if (nsp < kTcMaxSplit) {
-          sg.split_cta[nsp] = (short)cc;
-          sg.split_slot[nsp] = (char)(S.bnd[cc] >= s0 ? 0 : 1);
+    const bool first = loc && same_before == 0;
+    const unsigned first_mask = __ballot_sync(0xffffffffu, first);
+    const int npairs = __popc(__ballot_sync(0xffffffffu, loc)), nslots = __popc(first_mask);
+    if (warp == 0) {
+      // routing weights: GPT-OSS softmax over the k (neurostream/model/gpt_oss.py:119-120); Qwen3
+      // renormalised top-k probabilities (neurostream/moe/router.py:66-68)
+      const float v = act ? S.topv[t][j] : 0.f;
+      const float mx = __shfl_sync(0xffffffffu, v, t * k);
+      float wgt;
+      if (p.route_mode == NS_ROUTE_TOPK_SOFTMAX) {
+        const float ex = act ? expf(v - mx) : 0.f;
+        float sum = 0.f;
+        for (int l2 = 0; l2 < nall; ++l2) {  // per-token sum, fixed order
+          const float x2 = __shfl_sync(0xffffffffu, ex, l2);
+          if (l2 >= t * k && l2 < t * k + k) sum += x2;
         }
-        ++nsp;
+        wgt = ex / sum;
+      } else {
+        float sum = 0.f;
+        for (int l2 = 0; l2 < nall; ++l2) {
+          const float x2 = __shfl_sync(0xffffffffu, v, l2);
+          if (l2 >= t * k && l2 < t * k + k) sum += x2;
+        }
+        wgt = v / sum;
       }
-      sg.nsplit = nsp;
-      if (nsp > kTcMaxSplit) {
-        raise_device_error(NS_DEVERR_ROUTE);
-        S.abort_flag = 1;
+      if (act) S.w[t][j] = wgt;
+      int distinct_less = 0;
+      for (int l2 = 0; l2 < nall; ++l2) {
+        const int e2 = __shfl_sync(0xffffffffu, e, l2);
+        distinct_less += ((first_mask >> l2) & 1u) && e2 < e;
       }
-      u = e0 < uend ? e0 : uend;
-      ++ns;
+      if (loc) {
+        const int pidx = less_local + same_before;
+        S.pair_token[pidx] = t;
+        S.pair_w[pidx] = wgt;
+        S.pair_slot[pidx] = distinct_less;
+        if (first) {
+          S.slot_expert[distinct_less] = e;
+          S.slot_pair0[distinct_less] = less_local;
+        }
+      }
+      if (lane == 0) {
+        S.slot_pair0[nslots] = npairs;
+        S.nslots = nslots;
+        S.npairs = npairs;
+        stamp(a.trace, kEvImages);
+      }
+      if (c == 0 && act) {
+        if (p.ids) p.ids[lane] = e;
+        if (p.weights) p.weights[lane] = wgt;
+      }
+    } else {
+      // this CTA's segments: each phase's K blocks split evenly over the CTAs at chunk boundaries
+      TcGeom g;
+      g.ns1 = (F + 127) / 128;
+      g.nr2 = (H + 127) / 128;
+      g.T1 = nslots * g.ns1;
+      g.T2 = npairs * g.nr2;
+      g.nb_h = a.nb_h;
+      g.nb_f = a.nb_f;
+      g.H = H;
+      g.F = F;
+      auto bnd = [&](int ph, int jj) -> int {  // start of CTA jj's range in phase ph (tile-major blocks)
+        const int L = g.len(ph), Uph = (ph == 0 ? g.T1 : g.T2) * L;
+        if (jj <= 0) return 0;
+        if (jj >= G) return Uph;
+        const int u = (int)(((unsigned)Uph * (unsigned)jj) / (unsigned)G);  // Uph * G < 2^32 (host-checked)
+        const int i = (int)((unsigned)u / (unsigned)L);
+        return i * L + g.snap(ph, u - i * L);
+      };
+      // boundaries of CTAs c-31 .. c+32 (every CTA that can share a tile with this one), both phases
+      for (int ph = 0; ph < 2; ++ph) {
+        S.win[ph][lane] = bnd(ph, c - 31 + lane);
+        S.win[ph][lane + 32] = bnd(ph, c + 1 + lane);
+      }
+      __syncwarp();
+      int n[2];
+      for (int ph = 0; ph < 2; ++ph) {
+        const int L = g.len(ph), lo = S.win[ph][31], hi = S.win[ph][32];
+        n[ph] = hi > lo ? (hi - 1) / L - lo / L + 1 : 0;
+      }
+      const int ns = n[0] + n[1];
+      if (ns > kTcMaxSegs) {
+        if (lane == 0) {
+          raise_device_error(NS_DEVERR_ROUTE);
+          S.abort_flag = 1;
+        }
+      } else if (lane < ns) {
+        const int ph = lane < n[0] ? 0 : 1, li = ph == 0 ? lane : lane - n[0];
+        const int L = g.len(ph), lo = S.win[ph][31], hi = S.win[ph][32];
+        const int tl = lo / L + li;  // tile within the phase
+        const int s0 = tl * L, e0 = s0 + L;
+        TcSeg& sg = S.seg[lane];
+        sg.tile = ph == 0 ? tl : g.T1 + tl;
+        sg.k0 = max(lo, s0) - s0;
+        sg.k1 = min(hi, e0) - s0;
+        sg.my_slot = 2 * ph + (li == 0 ? 0 : 1);
+        sg.grp = ph == 0 ? tl / g.ns1 : tl / g.nr2;       // slot (phase 1) or pair (phase 2)
+        sg.sub = ph == 0 ? tl - sg.grp * g.ns1 : tl - sg.grp * g.nr2;  // 128-row block within it
+        int lo_w = 0, hi_w = 62;  // first window CTA whose range ends after s0 (window starts are sorted)
+        while (lo_w < hi_w) {
+          const int mid = (lo_w + hi_w) >> 1;
+          if (S.win[ph][mid + 1] <= s0) lo_w = mid + 1; else hi_w = mid;
+        }
+        int nsp = 0;
+        for (int w = lo_w; w < 63; ++w) {  // CTAs c-31+w sharing tile tl, ascending
+          const int cc = c - 31 + w;
+          if (cc < 0) continue;
+          if (cc >= G) break;
+          const int b0 = S.win[ph][w], b1 = S.win[ph][w + 1];
+          if (b0 >= e0) break;
+          if (b1 <= b0 || b1 <= s0) continue;  // empty, or ends before the tile
+          if (nsp < kTcMaxSplit) {
+            sg.split_cta[nsp] = (short)cc;
+            sg.split_slot[nsp] = (char)(2 * ph + (b0 >= s0 ? 0 : 1));
+          }
+          ++nsp;
+        }
+        sg.nsplit = nsp;
+        if (nsp > kTcMaxSplit) {
+          raise_device_error(NS_DEVERR_ROUTE);
+          S.abort_flag = 1;
+        }
+      }
+      if (lane == 0) {
+        S.nseg = ns > kTcMaxSegs ? 0 : ns;
+        stamp(a.trace, kEvRoute);
+      }
     }
-    if (u < uend) {
-      raise_device_error(NS_DEVERR_ROUTE);
-      S.abort_flag = 1;
-    }
-    S.nseg = ns;
-    stamp(a.trace, kEvRoute);
   }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
 
+  TcGeom geo;
+  geo.ns1 = (F + 127) / 128;
+  geo.nr2 = (H + 127) / 128;
+  geo.T1 = S.nslots * geo.ns1;
+  geo.T2 = S.npairs * geo.nr2;
+  geo.nb_h = a.nb_h;
+  geo.nb_f = a.nb_f;
+  geo.H = H;
+  geo.F = F;
+
   const int nseg = S.nseg;
   const uint32_t tbase = S.tmem_base;
+
+  // Chunks of a segment: [kb, kb + nbc) within one half of the tile (gate or up for phase 1).
+  auto chunk_of = [&](int ph, int kb, int k1, int* w, int* nbc, bool* up) {
+    int h0, hl;
+    geo.half_of(ph, kb, &h0, &hl);
+    *w = kb - h0;
+    *nbc = min(min(kTcChunk, hl - *w), k1 - kb);
+    *up = ph == 0 && h0 > 0;
+  };
 
   // ---- no routed local expert (expert parallel): this rank contributes zeros (+ residual)
   if (S.npairs == 0) {
@@ -537,47 +646,36 @@ __global__ void __launch_bounds__(kTcThreads, 1) moe_tc_kernel(const __grid_cons
       const int t = q / (r1 - r0), r = r0 + (q - t * (r1 - r0));
       p.out[(int64_t)t * H + r] = p.add_residual ? p.x[(int64_t)t * H + r] : 0.f;
     }
-  } else if (warp == 0) {
+  } else if (warp == kTcProducerWarp) {
     // ================================================================= producer (TMA)
     if (lane == 0) {
+      const uint64_t policy = l2_evict_first_policy();
       int n = 0;
       for (int sgi = 0; sgi < nseg && !*abort_flag; ++sgi) {
-        const TcSeg sg = S.seg[sgi];
-        const int i = sg.tile;
-        const bool ph1 = i < geo.T1;
-        const int rb = ph1 ? a.rb_h : a.rb_f;
-        int y0, nh;
-        const CUtensorMap *tm0, *tm1;
-        if (ph1) {
-          const int sl = i % geo.ns1, el = S.slot_expert[i / geo.ns1] - p.expert_lo;
-          y0 = (el * F + 64 * sl) / 8;
-          nh = 2;
-          tm0 = &a.tm_gate;
-          tm1 = &a.tm_up;
-        } else {
-          const int q = i - geo.T1, pp = q / geo.nr2, rt = q % geo.nr2;
-          const int el = S.slot_expert[S.pair_slot[pp]] - p.expert_lo;
-          y0 = (el * H + 128 * rt) / 8;
-          nh = (H - 128 * rt) >= 128 ? 2 : 1;
-          tm0 = &a.tm_down;
-          tm1 = &a.tm_down;
-        }
-        for (int kb = sg.k0; kb < sg.k1 && !*abort_flag; kb += kTcChunk, ++n) {
+        const TcSeg& sg = S.seg[sgi];
+        const int i = sg.tile, ph = i < geo.T1 ? 0 : 1, gv = geo.groups(i);
+        const int rb = ph == 0 ? a.rb_h : a.rb_f;
+        const int el = S.slot_expert[ph == 0 ? sg.grp : S.pair_slot[sg.grp]] - p.expert_lo;
+        const int y0 = ((ph == 0 ? el * F : el * H) + 128 * sg.sub) / 8;
+        const int k1 = sg.k1;
+        for (int kb = sg.k0; kb < k1 && !*abort_flag; ++n) {
+          int w, nbc;
+          bool up;
+          chunk_of(ph, kb, k1, &w, &nbc, &up);
+          const CUtensorMap* tm = ph == 1 ? (gv == 16 ? &a.tm_down16 : &a.tm_down8)
+                                          : up ? (gv == 16 ? &a.tm_up16 : &a.tm_up8)
+                                               : (gv == 16 ? &a.tm_gate16 : &a.tm_gate8);
           const int st = n % kTcRawStages;
           if (!tc_wait(&empty_raw[st], ((n / kTcRawStages) & 1) ^ 1, abort_flag)) break;
-          mbar_arrive_expect_tx(&full_raw[st], (uint32_t)(nh * 8 * kTcBoxBytes));
+          mbar_arrive_expect_tx(&full_raw[st], (uint32_t)(8 * gv * kTcBoxW));
           uint8_t* dst = raw + st * kTcRawBytes;
-          const int cc = kb / kTcChunk;
-          for (int hh = 0; hh < nh; ++hh) {
-            const CUtensorMap* tm = hh == 0 ? tm0 : tm1;
-            const int yy = ph1 ? y0 : y0 + 8 * hh;
 #pragma unroll 1
-            for (int j = 0; j < 8; ++j) {
-              const int x0 = (j * rb + cc * 136) & ~15;
-              tma_load_2d(dst + (hh * 8 + j) * kTcBoxBytes, tm, x0, yy, &full_raw[st]);
-            }
+          for (int j = 0; j < 8; ++j) {
+            const int x0 = (j * rb + 17 * w) & ~15;
+            tma_load_2d_hint(dst + j * kTcBoxBytes, tm, x0, y0, &full_raw[st], policy);
           }
           if (n == 0) stamp(a.trace, kEvProducerFirst);
+          kb += nbc;
         }
       }
       // let every issued load land before the CTA can exit
@@ -585,65 +683,114 @@ __global__ void __launch_bounds__(kTcThreads, 1) moe_tc_kernel(const __grid_cons
         mbar_wait_bounded(&full_raw[q % kTcRawStages], (q / kTcRawStages) & 1);
       stamp(a.trace, kEvProducerLast);
     }
-  } else if (warp == 1) {
+  } else if (warp == kTcMmaWarp) {
     // ================================================================= MMA issuer
     if (lane == 0) {
       int n = 0;
-      const uint32_t idesc_full1 = idesc_mxf4(128, 8 * NT, 0, 0);
-      const uint32_t idesc_full2 = idesc_mxf4(128, 8, 0, 0);
+      bool have_b1 = false;
       for (int sgi = 0; sgi < nseg && !*abort_flag; ++sgi) {
-        const TcSeg sg = S.seg[sgi];
-        const bool ph1 = sg.tile < geo.T1;
+        const TcSeg& sg = S.seg[sgi];
+        const int i = sg.tile, ph = i < geo.T1 ? 0 : 1;
         const int db = sgi & 1;
-        if (!tc_wait(&empty_d[db], ((sgi >> 1) & 1) ^ 1, abort_flag)) break;
-        const uint32_t tmem_d = tbase + 16 * db;
-        bool first = true;
-        for (int kb = sg.k0; kb < sg.k1; kb += kTcChunk, ++n) {
-          const int st = n % kTcCanStages;
-          if (!tc_wait(&full_can[st], (n / kTcCanStages) & 1, abort_flag)) break;
-          tc_fence_after();
-          const int nbc = min(kTcChunk, sg.k1 - kb), cc = kb / kTcChunk;
-          uint8_t* cs = can + st * kTcCanBytes;
-          const uint32_t sf_col = tbase + 32 + 16 * st;
-          for (int at = 0; at < (nbc + 3) / 4; ++at) {
-            tc_cp_sf(sf_col + 4 * at, umma_desc(smem_addr(cs + kTcCanA + at * 512), 128, 128));
-            const uint8_t* sfb_src = ph1 ? sfb1 + (2 * cc + at) * a.sfb1_atom : cs + kTcCanA + kTcCanSFA + kTcCanB + at * 512;
-            tc_cp_sf(sf_col + 8 + 4 * at, umma_desc(smem_addr(sfb_src), 128, 128));
-          }
-          for (int s = 0; s < nbc / 2; ++s) {
-            const uint64_t da = umma_desc(smem_addr(cs + 2 * s * 128), 128, kTcChunk * 128);
-            const uint64_t dbd = ph1 ? umma_desc(smem_addr(b1 + (size_t)(kb + 2 * s) * 128), 128, a.nb_h * 128)
-                                     : umma_desc(smem_addr(cs + kTcCanA + kTcCanSFA + 2 * s * 128), 128, 1024);
-            const uint32_t sfid = 2u * (s & 1);
-            const uint32_t id = (ph1 ? idesc_full1 : idesc_full2) | (sfid << 4) | (sfid << 29);
-            const uint32_t tsfa = (sf_col + 4 * (s >> 1)) | (sfid << 30);
-            const uint32_t tsfb = (sf_col + 8 + 4 * (s >> 1)) | (sfid << 30);
-            mma_mxf4(tmem_d, da, dbd, id, tsfa, tsfb, first ? 0u : 1u);
-            first = false;
-          }
-          tc_commit(&empty_can[st]);
+        if (ph == 0 && !have_b1) {
+          if (!tc_wait(b1_ready, 0, abort_flag)) break;
+          have_b1 = true;
         }
+        if (!tc_wait(&empty_d[db], ((sgi >> 1) & 1) ^ 1, abort_flag)) break;
+        const uint32_t tmem_d = tbase + kTcDCols * db;
+        const int N = ph == 0 ? 8 * NT : 8;
+        bool fresh_gate = true, fresh_up = true;  // accumulators not yet written in this segment
+        const int k1 = sg.k1;
+        bool ok = true;
+        for (int kb = sg.k0; kb < k1; ++n) {
+          int w, nbc;
+          bool up;
+          chunk_of(ph, kb, k1, &w, &nbc, &up);
+          const int st = n % kTcCanStages;
+          if (!tc_wait(&full_can[st], (n / kTcCanStages) & 1, abort_flag)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          uint8_t* cs = can + st * kTcCanBytes;
+          const uint32_t sf_col = tbase + 2 * kTcDCols + 32 * st;
+          const int na = (nbc + 3) / 4;
+          for (int at = 0; at < na; ++at)
+            tc_cp_sf(sf_col + 4 * at, umma_desc(smem_addr(cs + kTcCanA + at * 512), 128, 128));
+          const int ab0 = w >> 2;  // phase 1: first scale atom of the resident activation planes
+          if (ph == 0) {
+            const int nab = ((w + nbc - 1) >> 2) - ab0 + 1;
+            for (int at = 0; at < nab; ++at)
+              tc_cp_sf(sf_col + 16 + 4 * at, umma_desc(smem_addr(sfb1 + (ab0 + at) * a.sfb1_atom), 128, 128));
+          } else {
+            for (int at = 0; at < na; ++at)
+              tc_cp_sf(sf_col + 16 + 4 * at,
+                       umma_desc(smem_addr(cs + kTcCanA + kTcCanSFA + kTcCanB + at * 512), 128, 128));
+          }
+          const uint32_t dcol = tmem_d + (up ? 16 : 0);
+          // Descriptors advance by 256 bytes (2 blocks of 128 B) per MMA: +16 in the address field.
+          const uint32_t cs_addr = smem_addr(cs);
+          const uint64_t da0 = umma_desc(cs_addr, 128, kTcChunk * 128);
+          const uint64_t db0 = ph == 0 ? umma_desc(smem_addr(b1) + (uint32_t)w * 128u, 128, a.nb_h * 128)
+                                       : umma_desc(cs_addr + kTcCanA + kTcCanSFA, 128, 1024);
+          // activation scale atoms: phase 1 indexes the resident planes from block w (w even)
+          const int wm = ph == 0 ? (w >> 1) & 1 : 0;
+          const uint32_t idesc0 = idesc_mxf4(128, N, 0, 0);
+          bool acc = up ? !fresh_up : !fresh_gate;
+#pragma unroll
+          for (int s = 0; s < kTcChunk / 2; ++s) {
+            if (s < nbc / 2) {
+              const uint32_t sfa_id = 2u * (s & 1), sfb_id = 2u * ((s + wm) & 1);
+              const uint32_t tsfa = (sf_col + 4 * (s >> 1)) | (sfa_id << 30);
+              const uint32_t tsfb = (sf_col + 16 + 4 * ((s + wm) >> 1)) | (sfb_id << 30);
+              mma_mxf4(dcol, da0 + (uint64_t)(16 * s), db0 + (uint64_t)(16 * s), idesc0 | (sfb_id << 4) | (sfa_id << 29),
+                       tsfa, tsfb, acc ? 1u : 0u);
+              acc = true;
+            }
+          }
+          if (up) fresh_up = false; else fresh_gate = false;
+          tc_commit(&empty_can[st]);
+          kb += nbc;
+        }
+        if (!ok) break;
         tc_commit(&full_d[db]);
       }
+      stamp(a.trace, kEvPhase2Images);
       tc_commit(mma_done);
       mbar_wait_bounded(mma_done, 0);
     }
-  } else if (warp < kTcEpiWarp0) {
+  } else if (tc_repack_index(warp) >= 0) {
     // ================================================================= repack warps
-    const int rw = warp - kTcRepackWarp0;  // 0..7
+    const int rw = tc_repack_index(warp);  // 0..11
+    tc_build_b1(p, T, a.nb_h, S.rscale, b1, sfb1, a.sfb1_atom, 2 * rw + (lane >> 4), lane);
+    fence_proxy_async_smem();
+    __syncwarp();
+    if (lane == 0) mbar_arrive(b1_ready);
     const int j = lane & 7, qd = lane >> 3;
+    // this lane's items: row j of group G = item / 4, block b = (qd + 2j + 4t) mod 16, t = item % 4
+    constexpr int kItems = (64 + kTcRepackWarps - 1) / kTcRepackWarps;
+    int ibase[kItems], ib[kItems], isrc[kItems], idst[kItems], isfa[kItems];
+#pragma unroll
+    for (int it = 0; it < kItems; ++it) {
+      const int item = rw + kTcRepackWarps * it;
+      const int Gr = item >> 2, tt = item & 3;
+      const int b = (qd + 2 * j + 4 * tt) & 15;
+      const int r = 8 * Gr + j;
+      ibase[it] = item < 64 ? (Gr << 8) : -1;
+      ib[it] = b;
+      isrc[it] = j * kTcBoxBytes + Gr * kTcBoxW + 17 * b;
+      idst[it] = Gr * (kTcChunk * 128) + b * 128 + j * 16;
+      isfa[it] = (b >> 2) * 512 + 16 * (r & 31) + 4 * (r >> 5) + (b & 3);
+    }
     int n = 0;
     int ready_slot = -1;
     for (int sgi = 0; sgi < nseg && !*abort_flag; ++sgi) {
-      const TcSeg sg = S.seg[sgi];
-      const int i = sg.tile;
-      const bool ph1 = i < geo.T1;
-      const int rb = ph1 ? a.rb_h : a.rb_f;
-      int gvalid = 16, pp = 0;
-      if (!ph1) {
-        const int q = i - geo.T1, rt = q % geo.nr2;
-        pp = q / geo.nr2;
-        gvalid = (H - 128 * rt) >= 128 ? 16 : 8;
+      const TcSeg& sg = S.seg[sgi];
+      const int i = sg.tile, ph = i < geo.T1 ? 0 : 1, gv = geo.groups(i);
+      const int rb = ph == 0 ? a.rb_h : a.rb_f;
+      int pp = 0;
+      if (ph == 1) {
+        pp = (i - geo.T1) / geo.nr2;
         const int slot = S.pair_slot[pp];
         if (slot != ready_slot) {  // this pair's activation planes must be complete (every lane acquires)
           const unsigned target = (unsigned)geo.ns1;
@@ -661,53 +808,67 @@ __global__ void __launch_bounds__(kTcThreads, 1) moe_tc_kernel(const __grid_cons
           ready_slot = slot;
         }
       }
-      for (int kb = sg.k0; kb < sg.k1; kb += kTcChunk, ++n) {
+      const int k1 = sg.k1;
+      for (int kb = sg.k0; kb < k1 && !*abort_flag; ++n) {
+        int w, nbc;
+        bool up;
+        chunk_of(ph, kb, k1, &w, &nbc, &up);
         const int st = n % kTcRawStages, cst = n % kTcCanStages;
         if (!tc_wait(&full_raw[st], (n / kTcRawStages) & 1, abort_flag)) break;
+        if (n == 0 && rw == 0 && lane == 0) stamp(a.trace, kEvFirstTile);
         if (!tc_wait(&empty_can[cst], ((n / kTcCanStages) & 1) ^ 1, abort_flag)) break;
-        const int nbc = min(kTcChunk, sg.k1 - kb), cc = kb / kTcChunk;
         const uint8_t* rs = raw + st * kTcRawBytes;
         uint8_t* cs = can + cst * kTcCanBytes;
-        const int oj = (j * rb + cc * 136) & 15;
-        for (int item = rw; item < 32; item += kTcRepackWarps) {
-          const int Gr = item >> 1, tt = item & 1;
-          if (Gr >= gvalid) continue;
-          const int b = (qd + 2 * j + 4 * tt) & 7;
-          if (b >= nbc) continue;
-          const int hh = Gr >> 3, g = Gr & 7;
-          const uint8_t* src = rs + (hh * 8 + j) * kTcBoxBytes + g * kTcBoxW + oj + 17 * b;  // scale byte
-          const uint32_t* w = reinterpret_cast<const uint32_t*>(reinterpret_cast<uintptr_t>(src) & ~uintptr_t(3));
-          const uint32_t a0 = (uint32_t)(reinterpret_cast<uintptr_t>(src) & 3);
-          uint32_t wv[5];
-#pragma unroll
-          for (int q = 0; q < 5; ++q) wv[q] = w[q];
-          const uint32_t scale = (wv[0] >> (8 * a0)) & 0xFFu;
-          const uint32_t s1 = a0 + 1;  // payload offset from the first word, 1..4
-          uint4 pl;
-          if (s1 < 4) {
-            const uint32_t sh = 8 * s1;
-            pl.x = __funnelshift_r(wv[0], wv[1], sh);
-            pl.y = __funnelshift_r(wv[1], wv[2], sh);
-            pl.z = __funnelshift_r(wv[2], wv[3], sh);
-            pl.w = __funnelshift_r(wv[3], wv[4], sh);
-          } else {
-            pl = make_uint4(wv[1], wv[2], wv[3], wv[4]);
-          }
-          *reinterpret_cast<uint4*>(cs + Gr * (kTcChunk * 128) + b * 128 + j * 16) = pl;
-          const int r = 8 * Gr + j;
-          cs[kTcCanA + (b >> 2) * 512 + 16 * (r & 31) + 4 * (r >> 5) + (b & 3)] = (uint8_t)scale;
-        }
-        if (!ph1) {
-          // B: this pair's activation planes for blocks [kb, kb + nbc) and their scales
+        // B of phase 2 (this pair's activation planes, from L2): issue the loads before the repack
+        uint4 bv4 = make_uint4(0, 0, 0, 0);
+        uint8_t bsv = 0;
+        const int t2 = rw * 32 + lane;  // 0..383
+        if (ph == 1) {
           const uint8_t* img = a.actimg + (size_t)pp * a.img_bytes;
-          const int t2 = rw * 32 + lane;  // 0..255
           if (t2 < nbc * 8) {
-            const uint4 v = __ldcg(reinterpret_cast<const uint4*>(img + (size_t)kb * 128) + t2);
-            *reinterpret_cast<uint4*>(cs + kTcCanA + kTcCanSFA + t2 * 16) = v;
-          } else if (t2 >= 64 && t2 < 64 + nbc * 8) {
-            const int q = t2 - 64, bb = q >> 3, pl = q & 7;
-            const uint8_t sv = __ldcg(img + (size_t)a.nb_f * 128 + (size_t)(kb + bb) * 8 + pl);
-            cs[kTcCanA + kTcCanSFA + kTcCanB + (bb >> 2) * 512 + 16 * pl + (bb & 3)] = sv;
+            bv4 = __ldcg(reinterpret_cast<const uint4*>(img + (size_t)w * 128) + t2);
+          } else if (t2 >= 128 && t2 < 128 + nbc * 8) {
+            const int q = t2 - 128;
+            bsv = __ldcg(img + (size_t)a.nb_f * 128 + (size_t)(w + (q >> 3)) * 8 + (q & 7));
+          }
+        }
+        const int oj = (j * rb + 17 * w) & 15;
+        // 64 items (row group G, block quarter t) per chunk, up to 6 per warp: loads first, then stores.
+        // Lane (j, qd) takes row j of group G and block (qd + 2j + 4t) mod 16 (bank spread).
+        uint32_t wv[kItems][5];
+        bool valid[kItems];
+#pragma unroll
+        for (int it = 0; it < kItems; ++it) {
+          valid[it] = ibase[it] >= 0 && (ibase[it] >> 8) < gv && ib[it] < nbc;
+          const uintptr_t src = reinterpret_cast<uintptr_t>(rs) + (uint32_t)isrc[it] + (uint32_t)oj;
+          const uint32_t* wp = reinterpret_cast<const uint32_t*>(src & ~uintptr_t(3));
+#pragma unroll
+          for (int q = 0; q < 5; ++q) wv[it][q] = valid[it] ? wp[q] : 0u;
+        }
+#pragma unroll
+        for (int it = 0; it < kItems; ++it) {
+          if (!valid[it]) continue;
+          const uint32_t a0 = (uint32_t)((oj + 17 * ib[it]) & 3);  // the scale byte's offset in its word
+          const uint32_t scale = (wv[it][0] >> (8 * a0)) & 0xFFu;
+          uint4 pl;
+          if (a0 < 3) {  // payload starts inside word 0
+            const uint32_t sh = 8 * (a0 + 1);
+            pl.x = __funnelshift_r(wv[it][0], wv[it][1], sh);
+            pl.y = __funnelshift_r(wv[it][1], wv[it][2], sh);
+            pl.z = __funnelshift_r(wv[it][2], wv[it][3], sh);
+            pl.w = __funnelshift_r(wv[it][3], wv[it][4], sh);
+          } else {
+            pl = make_uint4(wv[it][1], wv[it][2], wv[it][3], wv[it][4]);
+          }
+          *reinterpret_cast<uint4*>(cs + idst[it]) = pl;
+          cs[kTcCanA + isfa[it]] = (uint8_t)scale;
+        }
+        if (ph == 1) {
+          if (t2 < nbc * 8) {
+            *reinterpret_cast<uint4*>(cs + kTcCanA + kTcCanSFA + t2 * 16) = bv4;
+          } else if (t2 >= 128 && t2 < 128 + nbc * 8) {
+            const int q = t2 - 128, bb = q >> 3, pl8 = q & 7;
+            cs[kTcCanA + kTcCanSFA + kTcCanB + (bb >> 2) * 512 + 16 * pl8 + (bb & 3)] = bsv;
           }
         }
         fence_proxy_async_smem();
@@ -715,33 +876,59 @@ __global__ void __launch_bounds__(kTcThreads, 1) moe_tc_kernel(const __grid_cons
         if (lane == 0) {
           mbar_arrive(&full_can[cst]);
           mbar_arrive(&empty_raw[st]);
+          if (rw == 0 && n == 2) stamp(a.trace, kEvPhase1End);
+          if (rw == 0 && n == 8) stamp(a.trace, kEvBarrier2);
         }
+        kb += nbc;
       }
     }
-  } else {
+  } else if (tc_epi_quadrant(warp) >= 0) {
     // ================================================================= epilogue warps
-    const int q = warp & 3;               // TMEM lane quadrant
+    const int q = tc_epi_quadrant(warp);  // TMEM lane quadrant (= warp % 4)
     const int row = 32 * q + lane;        // tile row
-    const int et = tid - kTcEpiWarp0 * 32;  // 0..127
+    const int et = row;                   // 0..127
+    tc_build_b1(p, T, a.nb_h, S.rscale, b1, sfb1, a.sfb1_atom, 2 * (kTcRepackWarps + q) + (lane >> 4), lane);
+    fence_proxy_async_smem();
+    __syncwarp();
+    if (lane == 0) mbar_arrive(b1_ready);
     for (int sgi = 0; sgi < nseg; ++sgi) {
-      const TcSeg sg = S.seg[sgi];
-      const int i = sg.tile;
-      const bool ph1 = i < geo.T1;
+      const TcSeg& sg = S.seg[sgi];
+      const int i = sg.tile, ph = i < geo.T1 ? 0 : 1;
       const int db = sgi & 1;
+      // this row's biases, fetched while the tile's MMAs run
+      float bias0 = 0.f, bias1 = 0.f;
+      if (ph == 0) {
+        const int el = S.slot_expert[i / geo.ns1] - p.expert_lo, n = 128 * (i % geo.ns1) + row;
+        if (n < F) {
+          if (p.gate_b) bias0 = p.gate_b[(int64_t)el * F + n];
+          if (p.up_b) bias1 = p.up_b[(int64_t)el * F + n];
+        }
+      } else {
+        const int qq = i - geo.T1, r = 128 * (qq % geo.nr2) + row;
+        const int el = S.slot_expert[S.pair_slot[qq / geo.nr2]] - p.expert_lo;
+        if (r < H && p.down_b) bias0 = p.down_b[(int64_t)el * H + r];
+      }
       if (!tc_wait(&full_d[db], (sgi >> 1) & 1, abort_flag)) break;
       tc_fence_after();
-      float y[NT];
-      const uint32_t ta = tbase + 16 * db + ((uint32_t)(32 * q) << 16);
-      if (ph1 && NT == 2) {
-        uint32_t v[16];
+      // vals: phase 1 gate[t] at t, up[t] at NT + t; phase 2 the down row at 0
+      float vals[2 * NT];
+      const uint32_t ta = tbase + kTcDCols * db + ((uint32_t)(32 * q) << 16);
+      if (ph == 0) {
+        uint32_t v[16], u[16];
         tmem_ld_x16(ta, v);
+        tmem_ld_x16(ta + 16, u);
         tmem_wait_ld();
+        const bool has_gate = sg.k0 < geo.nb_h, has_up = sg.k1 > geo.nb_h;
 #pragma unroll
         for (int t = 0; t < NT; ++t) {
-          float s = 0.f;
+          float sg_ = 0.f, su = 0.f;
 #pragma unroll
-          for (int pl = 0; pl < 8; ++pl) s += __uint_as_float(v[8 * t + pl]);
-          y[t] = s;
+          for (int pl = 0; pl < 8; ++pl) {
+            sg_ += __uint_as_float(v[8 * t + pl]);
+            su += __uint_as_float(u[8 * t + pl]);
+          }
+          vals[t] = has_gate ? sg_ : 0.f;
+          vals[NT + t] = has_up ? su : 0.f;
         }
       } else {
         uint32_t v[8];
@@ -750,54 +937,66 @@ __global__ void __launch_bounds__(kTcThreads, 1) moe_tc_kernel(const __grid_cons
         float s = 0.f;
 #pragma unroll
         for (int pl = 0; pl < 8; ++pl) s += __uint_as_float(v[pl]);
-        y[0] = s;
 #pragma unroll
-        for (int t = 1; t < NT; ++t) y[t] = 0.f;
+        for (int t = 0; t < 2 * NT; ++t) vals[t] = t == 0 ? s : 0.f;
       }
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&empty_d[db]);
-      const int ny = ph1 ? NT : 1;
+      const int nv = ph == 0 ? 2 * NT : 1;
 
       // ---- split tile: publish this segment's partial; the last CTA to arrive finishes the tile
       if (sg.nsplit > 1) {
-        float* part = a.partial + ((size_t)(c * 2 + sg.my_slot) * NT) * 128;
-        for (int t = 0; t < ny; ++t) __stcg(part + t * 128 + row, y[t]);
-        __threadfence();
+        float* part = tc_partial<NT>(a.partial, a.part_floats, c, sg.my_slot);
+#pragma unroll
+        for (int v = 0; v < 2 * NT; ++v)
+          if (v < nv) __stcg(part + v * 128 + row, vals[v]);
         named_sync(1, 128);
         if (et == 0) {
-          const unsigned old = atomicAdd(a.cnt + i, 1u);
+          const unsigned old = atom_add_acq_rel(a.cnt + i, 1u);
           S.fin = old == (unsigned)(sg.nsplit - 1);
         }
         named_sync(1, 128);
         if (!S.fin) continue;
-        __threadfence();
-        for (int t = 0; t < ny; ++t) {
-          float s = 0.f;
-          for (int g = 0; g < sg.nsplit; ++g) {
-            const float* pg = a.partial + ((size_t)(sg.split_cta[g] * 2 + sg.split_slot[g]) * NT) * 128;
-            s += __ldcg(pg + t * 128 + row);
+        // all partials loaded together (up to 4 segments at a time), then summed in segment order
+#pragma unroll
+        for (int v = 0; v < 2 * NT; ++v) vals[v] = 0.f;
+        for (int g0 = 0; g0 < sg.nsplit; g0 += 4) {
+          float pv[4][2 * NT];
+#pragma unroll
+          for (int g = 0; g < 4; ++g) {
+            const bool ok = g0 + g < sg.nsplit;
+            const float* pg = ok ? tc_partial<NT>(a.partial, a.part_floats, sg.split_cta[g0 + g], sg.split_slot[g0 + g])
+                                 : nullptr;
+#pragma unroll
+            for (int v = 0; v < 2 * NT; ++v) pv[g][v] = ok && v < nv ? __ldcg(pg + v * 128 + row) : 0.f;
           }
-          y[t] = s;
+#pragma unroll
+          for (int g = 0; g < 4; ++g)
+#pragma unroll
+            for (int v = 0; v < 2 * NT; ++v)
+              if (g0 + g < sg.nsplit) vals[v] += pv[g][v];
         }
       }
 
-      if (ph1) {
-        // ---- phase-1 tile: rows 0..63 gate, 64..127 up of neurons 64*sl ..; activation -> planes
+      if (ph == 0) {
+        // ---- phase-1 tile: neuron 128*sl + row; activation -> planes of block 4*sl + q (this warp)
         const int s = i / geo.ns1, sl = i % geo.ns1;
         const int el = S.slot_expert[s] - p.expert_lo;
-        for (int t = 0; t < NT; ++t) xchg[t * 128 + row] = y[t];
-        named_sync(1, 128);
-        if (row < 64) {
-          const int n = 64 * sl + row;
-          const float gb = p.gate_b ? p.gate_b[(int64_t)el * F + n] : 0.f;
-          const float ub = p.up_b ? p.up_b[(int64_t)el * F + n] : 0.f;
+        const int n = 128 * sl + row;
+        if (n < F) {  // whole warps: F is a multiple of 64
+          const float gb = bias0, ub = bias1;
           const int blk = n >> 5;
           for (int pp = S.slot_pair0[s]; pp < S.slot_pair0[s + 1]; ++pp) {
             const int t = S.pair_token[pp];
-            const float gv = xchg[t * 128 + row] + gb, uv = xchg[t * 128 + 64 + row] + ub;
-            const float av = activate(p.act_mode, gv, uv, p.alpha, p.limit);
-            // planes of the 32-value block `blk` (this warp): lanes 0..15 and 16..31 pair up
+            float gv_ = 0.f, uv_ = 0.f;
+#pragma unroll
+            for (int tt = 0; tt < NT; ++tt)
+              if (tt == t) {
+                gv_ = vals[tt];
+                uv_ = vals[NT + tt];
+              }
+            const float av = activate(p.act_mode, gv_ + gb, uv_ + ub, p.alpha, p.limit);
             float m = fabsf(av);
 #pragma unroll
             for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
@@ -818,27 +1017,20 @@ __global__ void __launch_bounds__(kTcThreads, 1) moe_tc_kernel(const __grid_cons
             }
           }
         }
-        __threadfence();
         named_sync(1, 128);
-        if (et == 0) atomicAdd(a.ready + s, 1u);
+        if (et == 0) red_add_release(a.ready + s, 1u);
       } else {
         // ---- phase-2 tile: down rows of one pair; the last pair of a row block combines it
         const int qq = i - geo.T1, pp = qq / geo.nr2, rt = qq % geo.nr2;
-        const int el = S.slot_expert[S.pair_slot[pp]] - p.expert_lo;
         const int r = 128 * rt + row;
-        if (r < H) {
-          const float v = y[0] + (p.down_b ? p.down_b[(int64_t)el * H + r] : 0.f);
-          __stcg(a.yp + (size_t)pp * H + r, v);
-        }
-        __threadfence();
+        if (r < H) __stcg(a.yp + (size_t)pp * H + r, vals[0] + bias0);
         named_sync(1, 128);
         if (et == 0) {
-          const unsigned old = atomicAdd(a.cnt2 + rt, 1u);
+          const unsigned old = atom_add_acq_rel(a.cnt2 + rt, 1u);
           S.fin = old == (unsigned)(S.npairs - 1);
         }
         named_sync(1, 128);
         if (S.fin) {
-          __threadfence();
           if (r < H)
             for (int t = 0; t < T; ++t) {
               float o = 0.f;
@@ -854,7 +1046,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) moe_tc_kernel(const __grid_cons
 
   tc_fence_before();
   __syncthreads();
-  if (warp == 1) {
+  if (warp == kTcMmaWarp) {
     tc_fence_after();
     tmem_dealloc(tbase, kTcTmemCols);
   }
@@ -866,18 +1058,25 @@ __global__ void __launch_bounds__(kTcThreads, 1) moe_tc_kernel(const __grid_cons
 struct TcPlan {
   size_t ws_total;
   size_t off_logits, off_partial, off_img, off_yp;
-  int img_bytes, max_tiles, grid;
+  int img_bytes, max_tiles, grid, part_floats;
 };
 
-// Layers the tensor-core kernel takes: MXFP4 experts, T <= 2, H and F multiples of 64 with at
-// most 16 chunks per row, 16-byte aligned expert tensors.
+// Layers the tensor-core kernel takes: MXFP4 experts, T <= 2, H and F multiples of 64, tiles of
+// a phase split over at most kTcMaxSplit CTAs, 16-byte aligned expert tensors (moe_tc_aligned).
 static bool moe_tc_eligible(const ns_moe_layer_t* p) {
   if (p->ggml_type != NS_GGML_MXFP4 || p->T > 2) return false;
-  if (p->H % 64 || p->F % 64 || p->H / 32 > kTcChunk * kTcMaxSplit || p->F / 32 > kTcChunk * kTcMaxSplit) return false;
-  if (p->T * p->k > kMaxPairs) return false;
+  if (p->H % 64 || p->F % 64) return false;
+  // a tile is shared by at most one CTA per chunk
+  const int ch1 = 2 * ((p->H / 32 + kTcChunk - 1) / kTcChunk), ch2 = (p->F / 32 + kTcChunk - 1) / kTcChunk;
+  if (ch1 > kTcMaxSplit || ch2 > kTcMaxSplit) return false;
+  if (p->T * p->k > kMaxPairs || p->T * p->k > 32) return false;
   const int pairs = p->T * p->k;
-  const int64_t tiles = (int64_t)pairs * (p->F / 64) + (int64_t)pairs * ((p->H + 127) / 128);
+  const int64_t tiles = (int64_t)pairs * ((p->F + 127) / 128) + (int64_t)pairs * ((p->H + 127) / 128);
   if (tiles > kTcMaxTiles || (p->H + 127) / 128 > kTcMaxRowTiles) return false;
+  // per-phase K blocks times the grid must fit 32 bits (the kernel's range arithmetic)
+  const int64_t u1 = (int64_t)pairs * ((p->F + 127) / 128) * 2 * (p->H / 32);
+  const int64_t u2 = (int64_t)pairs * ((p->H + 127) / 128) * (p->F / 32);
+  if (std::max(u1, u2) * kTcGridMax >= ((int64_t)1 << 32)) return false;
   return true;
 }
 
@@ -890,13 +1089,14 @@ static void moe_tc_plan(const ns_moe_layer_t* p, int grid, TcPlan* t) {
   const int pairs = p->T * p->k;
   const int nb_f = p->F / 32;
   t->grid = grid;
+  t->part_floats = (4 * p->T + 2) * 128;
   t->img_bytes = (int)align_up((size_t)nb_f * 128 + (size_t)nb_f * 8, 256);
-  t->max_tiles = pairs * (p->F / 64) + pairs * ((p->H + 127) / 128);
+  t->max_tiles = pairs * ((p->F + 127) / 128) + pairs * ((p->H + 127) / 128);
   size_t off = kTcWsHeader;
   t->off_logits = off;
   off += align_up((size_t)p->T * p->n_expert * 4, 256);
   t->off_partial = off;
-  off += align_up((size_t)grid * 2 * p->T * 128 * 4, 256);
+  off += align_up((size_t)grid * t->part_floats * 4, 256);
   t->off_img = off;
   off += (size_t)pairs * t->img_bytes;
   t->off_yp = off;
@@ -906,9 +1106,8 @@ static void moe_tc_plan(const ns_moe_layer_t* p, int grid, TcPlan* t) {
 
 static size_t moe_tc_smem(const ns_moe_layer_t* p, MoeTcArgs* a) {
   const int nb_h = p->H / 32;
-  size_t off = 0;
   a->off_raw = 0;
-  off = std::max((size_t)kTcRawStages * kTcRawBytes, align_up((size_t)p->T * p->H * 4, 1024));
+  size_t off = std::max((size_t)kTcRawStages * kTcRawBytes, align_up((size_t)p->T * p->H * 4, 1024));
   off = align_up(off, 1024);
   a->off_b1 = (int)off;
   off += (size_t)p->T * nb_h * 128;
@@ -919,8 +1118,6 @@ static size_t moe_tc_smem(const ns_moe_layer_t* p, MoeTcArgs* a) {
   off = align_up(off, 1024);
   a->off_can = (int)off;
   off += (size_t)kTcCanStages * kTcCanBytes;
-  a->off_xchg = (int)off;
-  off += 2 * 128 * 4;
   off = align_up(off, 64);
   a->off_bars = (int)off;
   off += 32 * 8;
@@ -950,14 +1147,15 @@ static int get_encode_fn(EncodeTiledFn* out) {
   return NS_OK;
 }
 
-// Tensor map over `rows` GGUF rows of `rb` bytes viewed as (rows/8) groups of 8*rb bytes.
-static int make_row_group_map(CUtensorMap* m, const uint8_t* base, int64_t rows, int rb) {
+// Tensor map over `rows` GGUF rows of `rb` bytes viewed as (rows/8) groups of 8*rb bytes; the box
+// is 256 bytes of `box_groups` consecutive groups.
+static int make_row_group_map(CUtensorMap* m, const uint8_t* base, int64_t rows, int rb, int box_groups) {
   EncodeTiledFn fn;
   int st = get_encode_fn(&fn);
   if (st) return st;
   const cuuint64_t dims[2] = {(cuuint64_t)8 * rb, (cuuint64_t)(rows / 8)};
   const cuuint64_t strides[1] = {(cuuint64_t)8 * rb};
-  const cuuint32_t box[2] = {(cuuint32_t)kTcBoxW, 8};
+  const cuuint32_t box[2] = {(cuuint32_t)kTcBoxW, (cuuint32_t)box_groups};
   const cuuint32_t estr[2] = {1, 1};
   CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<uint8_t*>(base), dims, strides, box, estr,
                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
@@ -996,9 +1194,13 @@ static int moe_tc_launch(const ns_moe_layer_t* p, const TcPlan& tp, uint8_t* ws,
   a.nb_h = p->H / 32;
   a.nb_f = p->F / 32;
   const int n_local = p->expert_hi - p->expert_lo;
-  int st = make_row_group_map(&a.tm_gate, p->gate_w, (int64_t)n_local * p->F, a.rb_h);
-  if (!st) st = make_row_group_map(&a.tm_up, p->up_w, (int64_t)n_local * p->F, a.rb_h);
-  if (!st) st = make_row_group_map(&a.tm_down, p->down_w, (int64_t)n_local * p->H, a.rb_f);
+  const int64_t rows_gu = (int64_t)n_local * p->F, rows_d = (int64_t)n_local * p->H;
+  int st = make_row_group_map(&a.tm_gate16, p->gate_w, rows_gu, a.rb_h, 16);
+  if (!st) st = make_row_group_map(&a.tm_gate8, p->gate_w, rows_gu, a.rb_h, 8);
+  if (!st) st = make_row_group_map(&a.tm_up16, p->up_w, rows_gu, a.rb_h, 16);
+  if (!st) st = make_row_group_map(&a.tm_up8, p->up_w, rows_gu, a.rb_h, 8);
+  if (!st) st = make_row_group_map(&a.tm_down16, p->down_w, rows_d, a.rb_f, 16);
+  if (!st) st = make_row_group_map(&a.tm_down8, p->down_w, rows_d, a.rb_f, 8);
   if (st) return st;
   a.bar = reinterpret_cast<unsigned long long*>(ws);
   a.cnt = reinterpret_cast<unsigned*>(ws + kTcOffCnt);
@@ -1006,6 +1208,7 @@ static int moe_tc_launch(const ns_moe_layer_t* p, const TcPlan& tp, uint8_t* ws,
   a.cnt2 = reinterpret_cast<unsigned*>(ws + kTcOffCnt2);
   a.logits = reinterpret_cast<float*>(ws + tp.off_logits);
   a.partial = reinterpret_cast<float*>(ws + tp.off_partial);
+  a.part_floats = tp.part_floats;
   a.actimg = ws + tp.off_img;
   a.yp = reinterpret_cast<float*>(ws + tp.off_yp);
   a.img_bytes = tp.img_bytes;
@@ -1014,7 +1217,7 @@ static int moe_tc_launch(const ns_moe_layer_t* p, const TcPlan& tp, uint8_t* ws,
   const size_t smem = moe_tc_smem(p, &a);
   if (smem > (size_t)kTcSmemBudget)
     return fail(NS_ERR_UNSUPPORTED, "ns_moe_decode_layer: tensor-core layout needs %zu bytes of shared memory", smem);
-  if (tp.grid > 1024) return fail(NS_ERR_UNSUPPORTED, "ns_moe_decode_layer: more than 1024 SMs");
+  if (tp.grid > kTcGridMax) return fail(NS_ERR_UNSUPPORTED, "ns_moe_decode_layer: more than %d SMs", kTcGridMax);
   return p->T == 1 ? launch_moe_tc<1>(a, tp.grid, smem, s) : launch_moe_tc<2>(a, tp.grid, smem, s);
 }
 
