@@ -50,30 +50,51 @@ namespace ns {
 constexpr int kTcWarps = 18;
 constexpr int kTcThreads = kTcWarps * 32;
 constexpr int kTcRepackWarps = 12;
-// Warp roles.  Warp w issues from SM sub-partition w % 4; the MMA issuer (1) shares its
-// sub-partition only with the producer (5), one epilogue warp (13) and two repack warps, so its
-// instruction stream is not starved.  The epilogue has one warp per TMEM lane quadrant (w % 4).
-constexpr int kTcMmaWarp = 1, kTcProducerWarp = 5;
+// Warp roles.  Warp w issues from SM sub-partition w % 4 and can reach TMEM lanes 32*(w % 4) ..
+// +31.  Producer 0, MMA issuer 1; one epilogue warp and three repack warps per lane quadrant:
+// epilogue 16, 13, 14, 15 (quadrants 0..3), repack {4, 8, 12}, {5, 9, 17}, {2, 6, 10}, {3, 7, 11}.
+constexpr int kTcMmaWarp = 1, kTcProducerWarp = 0;
 __device__ __forceinline__ int tc_epi_quadrant(int w) {
   return w == 16 ? 0 : w == 13 ? 1 : w == 14 ? 2 : w == 15 ? 3 : -1;
 }
+// Repack index 3*quadrant + (0..2), or -1.
 __device__ __forceinline__ int tc_repack_index(int w) {
-  // warps 0,2,3,4,6,7,8,9,10,11,12,17 -> 0..11
-  return w == 17 ? 11 : (w == 1 || w == 5 || w >= 13) ? -1 : w == 0 ? 0 : w < 5 ? w - 1 : w - 2;
+  if (w < 2 || w == 13 || w == 14 || w == 15 || w == 16) return -1;
+  const int q = w & 3;
+  const int wi = w == 17 ? 2 : (w >> 2) - (q <= 1 ? 1 : 0);
+  return 3 * q + wi;
 }
-constexpr int kTcRawStages = 3, kTcCanStages = 2;
+// M-row (TMEM lane) m = 32q + i of a tile holds tile row 8G + j, G = 8*(q/2) + i%8,
+// j = 2*(i/8) + q%2: the 32 rows a quadrant's repack warps read sit in distinct banks of the
+// staged boxes (8 row groups 4 banks apart x 4 row phases a quarter-quad apart when 8 GGUF rows
+// are an odd multiple of 2 mod 16 bytes, as for 2880-wide rows).
+__device__ __forceinline__ int tc_row_of(int m) {
+  const int q = m >> 5, i = m & 31;
+  return 8 * (8 * (q >> 1) + (i & 7)) + 2 * (i >> 3) + (q & 1);
+}
+constexpr int kTcCanStages = 2;
+// Raw (TMA) stages: enough bytes in flight to cover the load latency; one fewer for T = 2, whose
+// resident activation planes take the room.
+template <int NT>
+struct TcRaw {
+  static constexpr int kStages = NT == 1 ? 5 : 4;
+};
 constexpr int kTcChunk = 14;                         // K blocks (32 elements) per chunk
-constexpr int kTcBoxW = 256;                         // TMA box width (bytes): >= 14*17 + 14
+constexpr int kTcBoxW = 272;                         // TMA box row (bytes, 136 u16): >= 14*17 + 14; rows of
+                                                     // a box land 68 words apart (4 banks)
 constexpr int kTcBoxRows = 16;                       // row groups per box (8 for half tiles)
 constexpr int kTcBoxBytes = kTcBoxW * kTcBoxRows;    // one row phase of a chunk
 constexpr int kTcRawBytes = 8 * kTcBoxBytes;         // 8 row phases
-constexpr int kTcCanA = 16 * kTcChunk * 128;         // 16 row groups x 14 blocks x 128 B
-constexpr int kTcCanSFA = 4 * 512;                   // 4 scale atoms of 4 blocks
+constexpr int kTcCanSFA = 4 * 512;                   // per operand stage: weight scale atoms (4 x 4 blocks)
 constexpr int kTcCanB = 16 * 128;                    // phase-2 B: 8 planes x 14 blocks (+pad)
-constexpr int kTcCanSFB = 4 * 512;
-constexpr int kTcCanBytes = kTcCanA + kTcCanSFA + kTcCanB + kTcCanSFB;
+constexpr int kTcCanSFB = 4 * 512;                   // phase-2 B scale atoms
+constexpr int kTcCanBytes = kTcCanSFA + kTcCanB + kTcCanSFB;
 constexpr int kTcDCols = 32;                         // D: gate planes at +0, up planes at +16
-constexpr int kTcTmemCols = 128;                     // D: 2 x 32 cols; SF: 2 stages x 32 cols
+// TMEM columns: D buffers [0, 64); weight scales (SFA) [64, 96) and phase-2 activation scales
+// (SFB) [96, 128), 2 stages x 16 each; weights (A) [128, 256), 2 stages x 64 (14 blocks x 4 used);
+// phase-1 activation scales, resident for the whole K, [256, 384) (4 columns per 4-block atom).
+constexpr int kTcTmemSfa = 64, kTcTmemSfb = 96, kTcTmemA = 128, kTcTmemAStage = 64, kTcTmemSfb1 = 256;
+constexpr int kTcTmemCols = 512;
 constexpr int kTcMaxSegs = 8;                        // tiles one CTA touches
 constexpr int kTcMaxSplit = 24;                      // CTAs one tile is split over
 constexpr int kTcMaxTiles = 1024;
@@ -99,7 +120,7 @@ struct MoeTcArgs {
   float* yp;         // per pair: H fp32
   int img_bytes;
   int zero_tiles;    // counters to clear per launch
-  int off_raw, off_b1, off_sfb1, off_can, off_bars, off_shared;
+  int off_raw, off_b1, off_sfb1, off_can, off_xchg, off_bars, off_shared;
   int sfb1_atom;     // bytes between phase-1 scale atoms (128 * T)
   unsigned long long* trace;
 };
@@ -182,37 +203,33 @@ __device__ __forceinline__ bool tc_wait(uint64_t* bar, uint32_t parity, volatile
   return true;
 }
 
-// e2m1 code of digit d in [-4, 4] (value d/2): magnitude |d| is the code, bit 3 the sign.
-__device__ __forceinline__ uint32_t digit_code(int d) { return (uint32_t)(d < 0 ? (8 - d) : d); }
+// Block exponent of a 32-value block with max |v| = m: be = biased fp32 exponent of m, so that
+// max |v| < 2^e with e = be - 126.  Blocks below 2^-105 (or all zero) return 0 and are encoded as
+// zeros.
+__device__ __forceinline__ int block_be(float m) {
+  const int be = (int)((__float_as_uint(m) >> 23) & 255u);
+  return be >= 22 ? be : 0;
+}
 
-// Balanced radix-8 split of one value given its block exponent e (max|v| < 2^e):
-// nibble codes of the 8 planes packed in a 32-bit word (plane p in bits 4p..4p+3).
-__device__ __forceinline__ uint32_t digit_planes(float v, int e) {
-  int X = (int)rintf(ldexpf(v, 23 - e));
+// Balanced radix-8 digit planes of one value: X = round(v * 2^(23-e)), |X| <= 2^23, written as
+// X = sum_{p<7} d_p 8^p + d_7 8^7 with d_p in [-4, 3] and d_7 in [-4, 4].  Adding
+// c = 4 * (8^7 - 1) / 7 makes the seven low digits plain 3-bit fields of X + c (no carries), so all
+// planes come out in parallel.  Returns the e2m1 nibble codes (digit d -> value d/2: code |d|,
+// bit 3 = sign), plane p in bits 4p..4p+3.
+__device__ __forceinline__ uint32_t digit_planes(float v, int be) {
+  if (be == 0) return 0u;
+  const int X = __float2int_rn(v * __uint_as_float((uint32_t)(276 - be) << 23));  // v * 2^(149-be), exact
+  const int Y = X + 1198372;
   uint32_t codes = 0;
 #pragma unroll
-  for (int p = 0; p < 7; ++p) {
-    int d = X & 7;
-    d = d > 4 ? d - 8 : d;
-    X = (X - d) >> 3;
-    codes |= digit_code(d) << (4 * p);
-  }
-  return codes | (digit_code(X) << 28);
+  for (int p = 0; p < 7; ++p)  // field u = d + 4: code 12-u for u < 4 (negative d), u-4 otherwise
+    codes |= ((0x32109ABCu >> (4 * ((Y >> (3 * p)) & 7))) & 15u) << (4 * p);
+  const int Q = Y >> 21;  // d_7 in [-4, 4]
+  return codes | ((uint32_t)(Q < 0 ? 8 - Q : Q) << 28);
 }
 
-// E8M0 scale byte of plane p for block exponent e (block all zero: any scale).
-__device__ __forceinline__ uint32_t plane_scale(int p, int e, bool nonzero) {
-  if (!nonzero) return 127u;
-  const int s = 3 * p + e + 105;
-  return (uint32_t)(s < 0 ? 0 : (s > 254 ? 254 : s));
-}
-
-// Block exponent: max|v| < 2^e.
-__device__ __forceinline__ int block_exp(float m) {
-  int e = 0;
-  if (m > 0.f) frexpf(m, &e);
-  return e;
-}
+// UE8M0 scale of plane p: 2^(3p + e - 22) with bias 127 -> 3p + be - 21 (1..254 for be in 22..254).
+__device__ __forceinline__ uint32_t plane_scale(int p, int be) { return be ? (uint32_t)(3 * p + be - 21) : 127u; }
 
 // One half-warp (16 lanes, lane j holds block values v[j] and v[j+16]) writes the
 // 8 planes of one block: plane p byte j = code(v[j]) | code(v[j+16]) << 4, to
@@ -222,9 +239,8 @@ __device__ __forceinline__ void halfwarp_block_planes(float v0, float v1, uint8_
   float m = fmaxf(fabsf(v0), fabsf(v1));
 #pragma unroll
   for (int o = 8; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(mask, m, o, 16));
-  const int e = block_exp(m);
-  const bool nz = m > 0.f;
-  const uint32_t c0 = nz ? digit_planes(v0, e) : 0u, c1 = nz ? digit_planes(v1, e) : 0u;
+  const int be = block_be(m);
+  const uint32_t c0 = digit_planes(v0, be), c1 = digit_planes(v1, be);
 #pragma unroll
   for (int p = 0; p < 8; ++p) {
     const uint32_t b = ((c0 >> (4 * p)) & 15u) | (((c1 >> (4 * p)) & 15u) << 4);
@@ -232,7 +248,7 @@ __device__ __forceinline__ void halfwarp_block_planes(float v0, float v1, uint8_
   }
   if (hl == 0)
 #pragma unroll
-    for (int p = 0; p < 8; ++p) sdst[p * sstride] = (uint8_t)plane_scale(p, e, nz);
+    for (int p = 0; p < 8; ++p) sdst[p * sstride] = (uint8_t)plane_scale(p, be);
 }
 
 // Phase-1 B operand: the digit planes of h = (x * r) * norm_w, built from L2 by 16 warps (32
@@ -243,16 +259,32 @@ __device__ __forceinline__ void tc_build_b1(const ns_moe_layer_t& p, int T, int 
                                             uint8_t* sfb1, int sfb1_atom, int hw, int lane) {
   const int hl = lane & 15;
   const unsigned mask = 0xFFFFu << (lane & 16);
-  for (int it = hw; it < T * nb_h; it += 32) {
-    const int t = it / nb_h, b = it - t * nb_h;
-    const int64_t i0 = (int64_t)t * p.H + 32 * b + hl;
-    float v0 = p.x[i0], v1 = p.x[i0 + 16];
-    if (p.norm_w) {
-      v0 = __fmul_rn(__fmul_rn(v0, rscale[t]), p.norm_w[32 * b + hl]);
-      v1 = __fmul_rn(__fmul_rn(v1, rscale[t]), p.norm_w[32 * b + hl + 16]);
+  const int nit = T * nb_h;
+  for (int it0 = hw; it0 < nit; it0 += 4 * 32) {  // up to 4 blocks per half-warp: all loads first
+    float v[4][2], w[4][2];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int it = it0 + 32 * u;
+      const int t = it < nit ? it / nb_h : 0, b = it < nit ? it - t * nb_h : 0;
+      const int64_t i0 = (int64_t)t * p.H + 32 * b + hl;
+      v[u][0] = it < nit ? p.x[i0] : 0.f;
+      v[u][1] = it < nit ? p.x[i0 + 16] : 0.f;
+      w[u][0] = it < nit && p.norm_w ? p.norm_w[32 * b + hl] : 1.f;
+      w[u][1] = it < nit && p.norm_w ? p.norm_w[32 * b + hl + 16] : 1.f;
     }
-    halfwarp_block_planes(v0, v1, b1 + (size_t)t * nb_h * 128 + b * 128,
-                          sfb1 + (b >> 2) * sfb1_atom + 16 * (8 * t) + (b & 3), 16, hl, mask);
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int it = it0 + 32 * u;
+      if (it >= nit) break;
+      const int t = it / nb_h, b = it - t * nb_h;
+      float v0 = v[u][0], v1 = v[u][1];
+      if (p.norm_w) {
+        v0 = __fmul_rn(__fmul_rn(v0, rscale[t]), w[u][0]);
+        v1 = __fmul_rn(__fmul_rn(v1, rscale[t]), w[u][1]);
+      }
+      halfwarp_block_planes(v0, v1, b1 + (size_t)t * nb_h * 128 + b * 128,
+                            sfb1 + (b >> 2) * sfb1_atom + 16 * (8 * t) + (b & 3), 16, hl, mask);
+    }
   }
 }
 
@@ -270,8 +302,8 @@ __global__ void __launch_bounds__(kTcThreads, 1) moe_tc_kernel(const __grid_cons
   uint8_t* can = smem + a.off_can;
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + a.off_bars);
   uint64_t* full_raw = bars;
-  uint64_t* empty_raw = full_raw + kTcRawStages;
-  uint64_t* full_can = empty_raw + kTcRawStages;
+  uint64_t* empty_raw = full_raw + TcRaw<NT>::kStages;
+  uint64_t* full_can = empty_raw + TcRaw<NT>::kStages;
   uint64_t* empty_can = full_can + kTcCanStages;
   uint64_t* full_d = empty_can + kTcCanStages;
   uint64_t* empty_d = full_d + 2;
@@ -282,7 +314,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) moe_tc_kernel(const __grid_cons
 
   if (tid == 0) {
     stamp(a.trace, kEvStart);
-    for (int s = 0; s < kTcRawStages; ++s) {
+    for (int s = 0; s < TcRaw<NT>::kStages; ++s) {
       mbar_init(&full_raw[s], 1);
       mbar_init(&empty_raw[s], kTcRepackWarps);
     }
@@ -665,13 +697,13 @@ __global__ void __launch_bounds__(kTcThreads, 1) moe_tc_kernel(const __grid_cons
           const CUtensorMap* tm = ph == 1 ? (gv == 16 ? &a.tm_down16 : &a.tm_down8)
                                           : up ? (gv == 16 ? &a.tm_up16 : &a.tm_up8)
                                                : (gv == 16 ? &a.tm_gate16 : &a.tm_gate8);
-          const int st = n % kTcRawStages;
-          if (!tc_wait(&empty_raw[st], ((n / kTcRawStages) & 1) ^ 1, abort_flag)) break;
+          const int st = n % TcRaw<NT>::kStages;
+          if (!tc_wait(&empty_raw[st], ((n / TcRaw<NT>::kStages) & 1) ^ 1, abort_flag)) break;
           mbar_arrive_expect_tx(&full_raw[st], (uint32_t)(8 * gv * kTcBoxW));
           uint8_t* dst = raw + st * kTcRawBytes;
 #pragma unroll 1
           for (int j = 0; j < 8; ++j) {
-            const int x0 = (j * rb + 17 * w) & ~15;
+            const int x0 = ((j * rb + 17 * w) & ~15) >> 1;  // u16 elements
             tma_load_2d_hint(dst + j * kTcBoxBytes, tm, x0, y0, &full_raw[st], policy);
           }
           if (n == 0) stamp(a.trace, kEvProducerFirst);
@@ -679,8 +711,8 @@ __global__ void __launch_bounds__(kTcThreads, 1) moe_tc_kernel(const __grid_cons
         }
       }
       // let every issued load land before the CTA can exit
-      for (int q = max(0, n - kTcRawStages); q < n; ++q)
-        mbar_wait_bounded(&full_raw[q % kTcRawStages], (q / kTcRawStages) & 1);
+      for (int q = max(0, n - TcRaw<NT>::kStages); q < n; ++q)
+        mbar_wait_bounded(&full_raw[q % TcRaw<NT>::kStages], (q / TcRaw<NT>::kStages) & 1);
       stamp(a.trace, kEvProducerLast);
     }
   } else if (warp == kTcMmaWarp) {
@@ -694,6 +726,9 @@ __global__ void __launch_bounds__(kTcThreads, 1) moe_tc_kernel(const __grid_cons
         const int db = sgi & 1;
         if (ph == 0 && !have_b1) {
           if (!tc_wait(b1_ready, 0, abort_flag)) break;
+          tc_fence_after();
+          for (int at = 0; at < (a.nb_h + 3) / 4; ++at)  // phase-1 activation scales, once per launch
+            tc_cp_sf(tbase + kTcTmemSfb1 + 4 * at, umma_desc(smem_addr(sfb1 + at * a.sfb1_atom), 128, 128));
           have_b1 = true;
         }
         if (!tc_wait(&empty_d[db], ((sgi >> 1) & 1) ^ 1, abort_flag)) break;
@@ -713,38 +748,31 @@ __global__ void __launch_bounds__(kTcThreads, 1) moe_tc_kernel(const __grid_cons
           }
           tc_fence_after();
           uint8_t* cs = can + st * kTcCanBytes;
-          const uint32_t sf_col = tbase + 2 * kTcDCols + 32 * st;
-          const int na = (nbc + 3) / 4;
-          for (int at = 0; at < na; ++at)
-            tc_cp_sf(sf_col + 4 * at, umma_desc(smem_addr(cs + kTcCanA + at * 512), 128, 128));
-          const int ab0 = w >> 2;  // phase 1: first scale atom of the resident activation planes
-          if (ph == 0) {
-            const int nab = ((w + nbc - 1) >> 2) - ab0 + 1;
-            for (int at = 0; at < nab; ++at)
-              tc_cp_sf(sf_col + 16 + 4 * at, umma_desc(smem_addr(sfb1 + (ab0 + at) * a.sfb1_atom), 128, 128));
-          } else {
-            for (int at = 0; at < na; ++at)
-              tc_cp_sf(sf_col + 16 + 4 * at,
-                       umma_desc(smem_addr(cs + kTcCanA + kTcCanSFA + kTcCanB + at * 512), 128, 128));
-          }
+          const uint32_t sfa_col = tbase + kTcTmemSfa + 16 * st;  // written by the repack warps
+          const uint32_t sfb_col = tbase + kTcTmemSfb + 16 * st;
+          const uint32_t a_col = tbase + kTcTmemA + kTcTmemAStage * st;
+          if (ph == 1)  // phase 2: this chunk's activation scales (phase 1 uses the resident copy)
+            for (int at = 0; at < (nbc + 3) / 4; ++at)
+              tc_cp_sf(sfb_col + 4 * at, umma_desc(smem_addr(cs + kTcCanSFA + kTcCanB + at * 512), 128, 128));
           const uint32_t dcol = tmem_d + (up ? 16 : 0);
           // Descriptors advance by 256 bytes (2 blocks of 128 B) per MMA: +16 in the address field.
           const uint32_t cs_addr = smem_addr(cs);
-          const uint64_t da0 = umma_desc(cs_addr, 128, kTcChunk * 128);
           const uint64_t db0 = ph == 0 ? umma_desc(smem_addr(b1) + (uint32_t)w * 128u, 128, a.nb_h * 128)
-                                       : umma_desc(cs_addr + kTcCanA + kTcCanSFA, 128, 1024);
-          // activation scale atoms: phase 1 indexes the resident planes from block w (w even)
-          const int wm = ph == 0 ? (w >> 1) & 1 : 0;
+                                       : umma_desc(cs_addr + kTcCanSFA, 128, 1024);
           const uint32_t idesc0 = idesc_mxf4(128, N, 0, 0);
           bool acc = up ? !fresh_up : !fresh_gate;
 #pragma unroll
           for (int s = 0; s < kTcChunk / 2; ++s) {
             if (s < nbc / 2) {
-              const uint32_t sfa_id = 2u * (s & 1), sfb_id = 2u * ((s + wm) & 1);
-              const uint32_t tsfa = (sf_col + 4 * (s >> 1)) | (sfa_id << 30);
-              const uint32_t tsfb = (sf_col + 16 + 4 * ((s + wm) >> 1)) | (sfb_id << 30);
-              mma_mxf4(dcol, da0 + (uint64_t)(16 * s), db0 + (uint64_t)(16 * s), idesc0 | (sfb_id << 4) | (sfa_id << 29),
-                       tsfa, tsfb, acc ? 1u : 0u);
+              // weight scales: atom s/2 of the chunk; activation scales: phase 1 the resident atom of
+              // block w + 2s (w even), phase 2 atom s/2 of the chunk
+              const uint32_t sfa_id = 2u * (s & 1);
+              const int blk = w + 2 * s;
+              const uint32_t sfb_id = ph == 0 ? (uint32_t)(blk & 3) : sfa_id;
+              const uint32_t tsfa = (sfa_col + 4 * (s >> 1)) | (sfa_id << 30);
+              const uint32_t tsfb = (ph == 0 ? tbase + kTcTmemSfb1 + 4 * (blk >> 2) : sfb_col + 4 * (s >> 1)) | (sfb_id << 30);
+              mma_mxf4_ts(dcol, a_col + 8 * s, db0 + (uint64_t)(16 * s), idesc0 | (sfb_id << 4) | (sfa_id << 29),
+                          tsfa, tsfb, acc ? 1u : 0u);
               acc = true;
             }
           }
@@ -761,36 +789,30 @@ __global__ void __launch_bounds__(kTcThreads, 1) moe_tc_kernel(const __grid_cons
     }
   } else if (tc_repack_index(warp) >= 0) {
     // ================================================================= repack warps
+    // Quadrant q's three warps own M-rows 32q .. 32q+31 (this lane: M-row m, tile row (G, j)) and
+    // split a chunk's 14 blocks on scale-atom boundaries: {0-3, 12-13}, {4-7}, {8-11}.  Each
+    // block: 5 word loads of the staged row, the 16 payload bytes to 4 TMEM columns of row m; the
+    // E8M0 bytes of a 4-block atom form one TMEM word of row m (lane m, column 4*atom + m/32).
     const int rw = tc_repack_index(warp);  // 0..11
     tc_build_b1(p, T, a.nb_h, S.rscale, b1, sfb1, a.sfb1_atom, 2 * rw + (lane >> 4), lane);
     fence_proxy_async_smem();
     __syncwarp();
     if (lane == 0) mbar_arrive(b1_ready);
-    const int j = lane & 7, qd = lane >> 3;
-    // this lane's items: row j of group G = item / 4, block b = (qd + 2j + 4t) mod 16, t = item % 4
-    constexpr int kItems = (64 + kTcRepackWarps - 1) / kTcRepackWarps;
-    int ibase[kItems], ib[kItems], isrc[kItems], idst[kItems], isfa[kItems];
-#pragma unroll
-    for (int it = 0; it < kItems; ++it) {
-      const int item = rw + kTcRepackWarps * it;
-      const int Gr = item >> 2, tt = item & 3;
-      const int b = (qd + 2 * j + 4 * tt) & 15;
-      const int r = 8 * Gr + j;
-      ibase[it] = item < 64 ? (Gr << 8) : -1;
-      ib[it] = b;
-      isrc[it] = j * kTcBoxBytes + Gr * kTcBoxW + 17 * b;
-      idst[it] = Gr * (kTcChunk * 128) + b * 128 + j * 16;
-      isfa[it] = (b >> 2) * 512 + 16 * (r & 31) + 4 * (r >> 5) + (b & 3);
-    }
+    const int q = rw / 3, wi = rw - 3 * q;
+    const int m = 32 * q + lane;
+    const int Gr = 8 * (q >> 1) + (lane & 7), j = 2 * (lane >> 3) + (q & 1);
+    const uint32_t taddr_lane = (uint32_t)(32 * q) << 16;
+    (void)m;
     int n = 0;
     int ready_slot = -1;
     for (int sgi = 0; sgi < nseg && !*abort_flag; ++sgi) {
       const TcSeg& sg = S.seg[sgi];
       const int i = sg.tile, ph = i < geo.T1 ? 0 : 1, gv = geo.groups(i);
       const int rb = ph == 0 ? a.rb_h : a.rb_f;
+      const bool row_ok = Gr < gv;
       int pp = 0;
       if (ph == 1) {
-        pp = (i - geo.T1) / geo.nr2;
+        pp = sg.grp;
         const int slot = S.pair_slot[pp];
         if (slot != ready_slot) {  // this pair's activation planes must be complete (every lane acquires)
           const unsigned target = (unsigned)geo.ns1;
@@ -813,12 +835,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) moe_tc_kernel(const __grid_cons
         int w, nbc;
         bool up;
         chunk_of(ph, kb, k1, &w, &nbc, &up);
-        const int st = n % kTcRawStages, cst = n % kTcCanStages;
-        if (!tc_wait(&full_raw[st], (n / kTcRawStages) & 1, abort_flag)) break;
-        if (n == 0 && rw == 0 && lane == 0) stamp(a.trace, kEvFirstTile);
-        if (!tc_wait(&empty_can[cst], ((n / kTcCanStages) & 1) ^ 1, abort_flag)) break;
-        const uint8_t* rs = raw + st * kTcRawBytes;
-        uint8_t* cs = can + cst * kTcCanBytes;
+        const int st = n % TcRaw<NT>::kStages, cst = n % kTcCanStages;
         // B of phase 2 (this pair's activation planes, from L2): issue the loads before the repack
         uint4 bv4 = make_uint4(0, 0, 0, 0);
         uint8_t bsv = 0;
@@ -828,54 +845,73 @@ __global__ void __launch_bounds__(kTcThreads, 1) moe_tc_kernel(const __grid_cons
           if (t2 < nbc * 8) {
             bv4 = __ldcg(reinterpret_cast<const uint4*>(img + (size_t)w * 128) + t2);
           } else if (t2 >= 128 && t2 < 128 + nbc * 8) {
-            const int q = t2 - 128;
-            bsv = __ldcg(img + (size_t)a.nb_f * 128 + (size_t)(w + (q >> 3)) * 8 + (q & 7));
+            const int qq = t2 - 128;
+            bsv = __ldcg(img + (size_t)a.nb_f * 128 + (size_t)(w + (qq >> 3)) * 8 + (qq & 7));
           }
         }
-        const int oj = (j * rb + 17 * w) & 15;
-        // 64 items (row group G, block quarter t) per chunk, up to 6 per warp: loads first, then stores.
-        // Lane (j, qd) takes row j of group G and block (qd + 2j + 4t) mod 16 (bank spread).
-        uint32_t wv[kItems][5];
-        bool valid[kItems];
+        if (!tc_wait(&full_raw[st], (n / TcRaw<NT>::kStages) & 1, abort_flag)) break;
+        if (n == 0 && rw == 0 && lane == 0) stamp(a.trace, kEvFirstTile);
+        const uint8_t* rs = raw + st * kTcRawBytes + j * kTcBoxBytes + Gr * kTcBoxW + ((j * rb + 17 * w) & 15);
+        // this warp's blocks: u -> b = u (u < 4) or u + 8 for warp 0, 4*wi + u otherwise
+        constexpr int kU = 6;
+        uint32_t wv[kU][5];
 #pragma unroll
-        for (int it = 0; it < kItems; ++it) {
-          valid[it] = ibase[it] >= 0 && (ibase[it] >> 8) < gv && ib[it] < nbc;
-          const uintptr_t src = reinterpret_cast<uintptr_t>(rs) + (uint32_t)isrc[it] + (uint32_t)oj;
+        for (int u = 0; u < kU; ++u) {  // all loads first
+          const int b = wi == 0 ? (u < 4 ? u : u + 8) : 4 * wi + u;
+          const bool ok = row_ok && (wi == 0 || u < 4) && b < nbc;
+          const uintptr_t src = reinterpret_cast<uintptr_t>(rs + 17 * b);
           const uint32_t* wp = reinterpret_cast<const uint32_t*>(src & ~uintptr_t(3));
 #pragma unroll
-          for (int q = 0; q < 5; ++q) wv[it][q] = valid[it] ? wp[q] : 0u;
+          for (int k = 0; k < 5; ++k) wv[u][k] = ok ? wp[k] : 0u;
         }
+        uint32_t pay[4 * kU], sw[2] = {0u, 0u};
 #pragma unroll
-        for (int it = 0; it < kItems; ++it) {
-          if (!valid[it]) continue;
-          const uint32_t a0 = (uint32_t)((oj + 17 * ib[it]) & 3);  // the scale byte's offset in its word
-          const uint32_t scale = (wv[it][0] >> (8 * a0)) & 0xFFu;
-          uint4 pl;
-          if (a0 < 3) {  // payload starts inside word 0
-            const uint32_t sh = 8 * (a0 + 1);
-            pl.x = __funnelshift_r(wv[it][0], wv[it][1], sh);
-            pl.y = __funnelshift_r(wv[it][1], wv[it][2], sh);
-            pl.z = __funnelshift_r(wv[it][2], wv[it][3], sh);
-            pl.w = __funnelshift_r(wv[it][3], wv[it][4], sh);
-          } else {
-            pl = make_uint4(wv[it][1], wv[it][2], wv[it][3], wv[it][4]);
+        for (int u = 0; u < kU; ++u) {
+          const int b = wi == 0 ? (u < 4 ? u : u + 8) : 4 * wi + u;
+          const uint32_t a0 = (uint32_t)(reinterpret_cast<uintptr_t>(rs + 17 * b) & 3);  // scale byte's offset
+          const uint32_t sh = 8 * ((a0 + 1) & 3);
+          const bool whole = a0 == 3;  // payload is word-aligned: words 1..4
+#pragma unroll
+          for (int k = 0; k < 4; ++k)
+            pay[4 * u + k] = whole ? wv[u][k + 1] : __funnelshift_r(wv[u][k], wv[u][k + 1], sh);
+          sw[u >> 2] |= ((wv[u][0] >> (8 * a0)) & 0xFFu) << (8 * (u & 3));
+        }
+        __syncwarp();  // every lane has consumed its staged words: the raw stage can be refilled
+        if (lane == 0) mbar_arrive(&empty_raw[st]);
+        // the operand stage (TMEM columns, phase-2 B) must have been consumed by its earlier MMAs
+        if (!tc_wait(&empty_can[cst], ((n / kTcCanStages) & 1) ^ 1, abort_flag)) break;
+        tc_fence_after();
+        uint8_t* cs = can + cst * kTcCanBytes;
+        const uint32_t acol = tbase + kTcTmemA + kTcTmemAStage * cst + taddr_lane;
+        const uint32_t scol = tbase + kTcTmemSfa + 16 * cst + q + taddr_lane;  // column 4*atom + m/32
+        {
+          uint32_t v16[16];
+#pragma unroll
+          for (int k = 0; k < 16; ++k) v16[k] = pay[k];
+          tmem_st_x16(acol + 16 * wi, v16);                // blocks 4wi .. 4wi+3
+          tmem_st_x1(scol + 4 * wi, sw[0]);                 // their scale atom
+          if (wi == 0) {
+            uint32_t v8[8];
+#pragma unroll
+            for (int k = 0; k < 8; ++k) v8[k] = pay[16 + k];
+            tmem_st_x8(acol + 48, v8);                      // blocks 12, 13
+            tmem_st_x1(scol + 12, sw[1]);
           }
-          *reinterpret_cast<uint4*>(cs + idst[it]) = pl;
-          cs[kTcCanA + isfa[it]] = (uint8_t)scale;
         }
         if (ph == 1) {
           if (t2 < nbc * 8) {
-            *reinterpret_cast<uint4*>(cs + kTcCanA + kTcCanSFA + t2 * 16) = bv4;
+            *reinterpret_cast<uint4*>(cs + kTcCanSFA + t2 * 16) = bv4;
           } else if (t2 >= 128 && t2 < 128 + nbc * 8) {
-            const int q = t2 - 128, bb = q >> 3, pl8 = q & 7;
-            cs[kTcCanA + kTcCanSFA + kTcCanB + (bb >> 2) * 512 + 16 * pl8 + (bb & 3)] = bsv;
+            const int qq = t2 - 128, bb = qq >> 3, pl8 = qq & 7;
+            cs[kTcCanSFA + kTcCanB + (bb >> 2) * 512 + 16 * pl8 + (bb & 3)] = bsv;
           }
         }
+        tmem_wait_st();
         fence_proxy_async_smem();
+        tc_fence_before();
         __syncwarp();
         if (lane == 0) {
           mbar_arrive(&full_can[cst]);
-          mbar_arrive(&empty_raw[st]);
           if (rw == 0 && n == 2) stamp(a.trace, kEvPhase1End);
           if (rw == 0 && n == 8) stamp(a.trace, kEvBarrier2);
         }
@@ -885,8 +921,10 @@ __global__ void __launch_bounds__(kTcThreads, 1) moe_tc_kernel(const __grid_cons
   } else if (tc_epi_quadrant(warp) >= 0) {
     // ================================================================= epilogue warps
     const int q = tc_epi_quadrant(warp);  // TMEM lane quadrant (= warp % 4)
-    const int row = 32 * q + lane;        // tile row
-    const int et = row;                   // 0..127
+    const int mrow = 32 * q + lane;       // M-row (TMEM lane) of this thread
+    const int row = tc_row_of(mrow);      // the tile row it holds
+    const int et = mrow;                  // 0..127
+    float* xchg = reinterpret_cast<float*>(smem + a.off_xchg);
     tc_build_b1(p, T, a.nb_h, S.rscale, b1, sfb1, a.sfb1_atom, 2 * (kTcRepackWarps + q) + (lane >> 4), lane);
     fence_proxy_async_smem();
     __syncwarp();
@@ -950,7 +988,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) moe_tc_kernel(const __grid_cons
         float* part = tc_partial<NT>(a.partial, a.part_floats, c, sg.my_slot);
 #pragma unroll
         for (int v = 0; v < 2 * NT; ++v)
-          if (v < nv) __stcg(part + v * 128 + row, vals[v]);
+          if (v < nv) __stcg(part + v * 128 + mrow, vals[v]);
         named_sync(1, 128);
         if (et == 0) {
           const unsigned old = atom_add_acq_rel(a.cnt + i, 1u);
@@ -969,7 +1007,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) moe_tc_kernel(const __grid_cons
             const float* pg = ok ? tc_partial<NT>(a.partial, a.part_floats, sg.split_cta[g0 + g], sg.split_slot[g0 + g])
                                  : nullptr;
 #pragma unroll
-            for (int v = 0; v < 2 * NT; ++v) pv[g][v] = ok && v < nv ? __ldcg(pg + v * 128 + row) : 0.f;
+            for (int v = 0; v < 2 * NT; ++v) pv[g][v] = ok && v < nv ? __ldcg(pg + v * 128 + mrow) : 0.f;
           }
 #pragma unroll
           for (int g = 0; g < 4; ++g)
@@ -980,29 +1018,29 @@ __global__ void __launch_bounds__(kTcThreads, 1) moe_tc_kernel(const __grid_cons
       }
 
       if (ph == 0) {
-        // ---- phase-1 tile: neuron 128*sl + row; activation -> planes of block 4*sl + q (this warp)
+        // ---- phase-1 tile: neuron 128*sl + row; activations regrouped through shared memory so
+        // that warp q writes the planes of neurons 32q .. 32q+31 (block 4*sl + q)
         const int s = i / geo.ns1, sl = i % geo.ns1;
-        const int el = S.slot_expert[s] - p.expert_lo;
         const int n = 128 * sl + row;
-        if (n < F) {  // whole warps: F is a multiple of 64
-          const float gb = bias0, ub = bias1;
-          const int blk = n >> 5;
-          for (int pp = S.slot_pair0[s]; pp < S.slot_pair0[s + 1]; ++pp) {
-            const int t = S.pair_token[pp];
-            float gv_ = 0.f, uv_ = 0.f;
+        const int blk = 4 * sl + q;
+        for (int pp = S.slot_pair0[s]; pp < S.slot_pair0[s + 1]; ++pp) {
+          const int t = S.pair_token[pp];
+          float gv_ = 0.f, uv_ = 0.f;
 #pragma unroll
-            for (int tt = 0; tt < NT; ++tt)
-              if (tt == t) {
-                gv_ = vals[tt];
-                uv_ = vals[NT + tt];
-              }
-            const float av = activate(p.act_mode, gv_ + gb, uv_ + ub, p.alpha, p.limit);
+          for (int tt = 0; tt < NT; ++tt)
+            if (tt == t) {
+              gv_ = vals[tt];
+              uv_ = vals[NT + tt];
+            }
+          xchg[row] = n < F ? activate(p.act_mode, gv_ + bias0, uv_ + bias1, p.alpha, p.limit) : 0.f;
+          named_sync(1, 128);
+          if (32 * blk < F) {  // whole warps: F is a multiple of 64
+            const float av = xchg[32 * q + lane];
             float m = fabsf(av);
 #pragma unroll
             for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-            const int e = block_exp(m);
-            const bool nz = m > 0.f;
-            const uint32_t cd = nz ? digit_planes(av, e) : 0u;
+            const int be = block_be(m);
+            const uint32_t cd = digit_planes(av, be);
             const uint32_t hi = __shfl_down_sync(0xffffffffu, cd, 16);
             uint8_t* img = a.actimg + (size_t)pp * a.img_bytes;
             if (lane < 16) {
@@ -1013,9 +1051,10 @@ __global__ void __launch_bounds__(kTcThreads, 1) moe_tc_kernel(const __grid_cons
               }
             } else if (lane < 24) {
               const int pl = lane - 16;
-              img[(size_t)a.nb_f * 128 + (size_t)blk * 8 + pl] = (uint8_t)plane_scale(pl, e, nz);
+              img[(size_t)a.nb_f * 128 + (size_t)blk * 8 + pl] = (uint8_t)plane_scale(pl, be);
             }
           }
+          named_sync(1, 128);  // xchg is reused by the next pair
         }
         named_sync(1, 128);
         if (et == 0) red_add_release(a.ready + s, 1u);
@@ -1066,6 +1105,7 @@ struct TcPlan {
 static bool moe_tc_eligible(const ns_moe_layer_t* p) {
   if (p->ggml_type != NS_GGML_MXFP4 || p->T > 2) return false;
   if (p->H % 64 || p->F % 64) return false;
+  if (p->H / 32 > 128) return false;  // resident phase-1 activation scales: 4 TMEM columns per 4 blocks
   // a tile is shared by at most one CTA per chunk
   const int ch1 = 2 * ((p->H / 32 + kTcChunk - 1) / kTcChunk), ch2 = (p->F / 32 + kTcChunk - 1) / kTcChunk;
   if (ch1 > kTcMaxSplit || ch2 > kTcMaxSplit) return false;
@@ -1107,7 +1147,8 @@ static void moe_tc_plan(const ns_moe_layer_t* p, int grid, TcPlan* t) {
 static size_t moe_tc_smem(const ns_moe_layer_t* p, MoeTcArgs* a) {
   const int nb_h = p->H / 32;
   a->off_raw = 0;
-  size_t off = std::max((size_t)kTcRawStages * kTcRawBytes, align_up((size_t)p->T * p->H * 4, 1024));
+  const int raw_stages = p->T == 1 ? TcRaw<1>::kStages : TcRaw<2>::kStages;
+  size_t off = std::max((size_t)raw_stages * kTcRawBytes, align_up((size_t)p->T * p->H * 4, 1024));
   off = align_up(off, 1024);
   a->off_b1 = (int)off;
   off += (size_t)p->T * nb_h * 128;
@@ -1118,6 +1159,8 @@ static size_t moe_tc_smem(const ns_moe_layer_t* p, MoeTcArgs* a) {
   off = align_up(off, 1024);
   a->off_can = (int)off;
   off += (size_t)kTcCanStages * kTcCanBytes;
+  a->off_xchg = (int)off;
+  off += 128 * 4;
   off = align_up(off, 64);
   a->off_bars = (int)off;
   off += 32 * 8;
@@ -1147,17 +1190,17 @@ static int get_encode_fn(EncodeTiledFn* out) {
   return NS_OK;
 }
 
-// Tensor map over `rows` GGUF rows of `rb` bytes viewed as (rows/8) groups of 8*rb bytes; the box
-// is 256 bytes of `box_groups` consecutive groups.
+// Tensor map over `rows` GGUF rows of `rb` bytes viewed as (rows/8) groups of 8*rb bytes (16-bit
+// elements); the box is 272 bytes of `box_groups` consecutive groups.
 static int make_row_group_map(CUtensorMap* m, const uint8_t* base, int64_t rows, int rb, int box_groups) {
   EncodeTiledFn fn;
   int st = get_encode_fn(&fn);
   if (st) return st;
-  const cuuint64_t dims[2] = {(cuuint64_t)8 * rb, (cuuint64_t)(rows / 8)};
+  const cuuint64_t dims[2] = {(cuuint64_t)4 * rb, (cuuint64_t)(rows / 8)};  // u16 elements (rb is even)
   const cuuint64_t strides[1] = {(cuuint64_t)8 * rb};
-  const cuuint32_t box[2] = {(cuuint32_t)kTcBoxW, (cuuint32_t)box_groups};
+  const cuuint32_t box[2] = {(cuuint32_t)(kTcBoxW / 2), (cuuint32_t)box_groups};
   const cuuint32_t estr[2] = {1, 1};
-  CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<uint8_t*>(base), dims, strides, box, estr,
+  CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, const_cast<uint8_t*>(base), dims, strides, box, estr,
                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return fail(NS_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
