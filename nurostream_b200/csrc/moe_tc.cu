@@ -154,7 +154,6 @@ struct TcShared {
   int nseg;
   TcSeg seg[kTcMaxSegs];
   int fin;
-  int win[2][64];  // range starts of CTAs c-31 .. c+32 in each phase (tile-major K blocks)
   __align__(16) float scratch[NS_MAX_EXPERTS];
 };
 
@@ -585,16 +584,23 @@ __global__ void __launch_bounds__(kTcThreads, 1) moe_tc_kernel(const __grid_cons
         const int i = (int)((unsigned)u / (unsigned)L);
         return i * L + g.snap(ph, u - i * L);
       };
-      // boundaries of CTAs c-31 .. c+32 (every CTA that can share a tile with this one), both phases
+      // CTA owning the chunk that starts at tile-local block sl of tile tl: the last jj with
+      // bnd(jj) <= tl*L + sl.  snap(u) passes sl once u reaches sl + 7 (or the end of sl's half),
+      // so that jj is the last one with floor(Uph*jj/G) < u_t, i.e. ceil(u_t*G/Uph) - 1.
+      auto owner = [&](int ph, int tl, int sl) -> int {
+        const int L = g.len(ph), Uph = (ph == 0 ? g.T1 : g.T2) * L;
+        int h0, hl;
+        g.half_of(ph, sl, &h0, &hl);
+        const unsigned ut = (unsigned)(tl * L + min(sl + kTcChunk / 2, h0 + hl));
+        const int jj = (int)((ut * (unsigned)G + (unsigned)Uph - 1u) / (unsigned)Uph) - 1;
+        return min(max(jj, 0), G - 1);
+      };
+      int n[2], lo[2], hi[2];
       for (int ph = 0; ph < 2; ++ph) {
-        S.win[ph][lane] = bnd(ph, c - 31 + lane);
-        S.win[ph][lane + 32] = bnd(ph, c + 1 + lane);
-      }
-      __syncwarp();
-      int n[2];
-      for (int ph = 0; ph < 2; ++ph) {
-        const int L = g.len(ph), lo = S.win[ph][31], hi = S.win[ph][32];
-        n[ph] = hi > lo ? (hi - 1) / L - lo / L + 1 : 0;
+        const int L = g.len(ph);
+        lo[ph] = bnd(ph, c);
+        hi[ph] = bnd(ph, c + 1);
+        n[ph] = hi[ph] > lo[ph] ? (hi[ph] - 1) / L - lo[ph] / L + 1 : 0;
       }
       const int ns = n[0] + n[1];
       if (ns > kTcMaxSegs) {
@@ -604,34 +610,33 @@ __global__ void __launch_bounds__(kTcThreads, 1) moe_tc_kernel(const __grid_cons
         }
       } else if (lane < ns) {
         const int ph = lane < n[0] ? 0 : 1, li = ph == 0 ? lane : lane - n[0];
-        const int L = g.len(ph), lo = S.win[ph][31], hi = S.win[ph][32];
-        const int tl = lo / L + li;  // tile within the phase
+        const int L = g.len(ph);
+        const int tl = lo[ph] / L + li;  // tile within the phase
         const int s0 = tl * L, e0 = s0 + L;
         TcSeg& sg = S.seg[lane];
         sg.tile = ph == 0 ? tl : g.T1 + tl;
-        sg.k0 = max(lo, s0) - s0;
-        sg.k1 = min(hi, e0) - s0;
+        sg.k0 = max(lo[ph], s0) - s0;
+        sg.k1 = min(hi[ph], e0) - s0;
         sg.my_slot = 2 * ph + (li == 0 ? 0 : 1);
         sg.grp = ph == 0 ? tl / g.ns1 : tl / g.nr2;       // slot (phase 1) or pair (phase 2)
         sg.sub = ph == 0 ? tl - sg.grp * g.ns1 : tl - sg.grp * g.nr2;  // 128-row block within it
-        int lo_w = 0, hi_w = 62;  // first window CTA whose range ends after s0 (window starts are sorted)
-        while (lo_w < hi_w) {
-          const int mid = (lo_w + hi_w) >> 1;
-          if (S.win[ph][mid + 1] <= s0) lo_w = mid + 1; else hi_w = mid;
-        }
-        int nsp = 0;
-        for (int w = lo_w; w < 63; ++w) {  // CTAs c-31+w sharing tile tl, ascending
-          const int cc = c - 31 + w;
-          if (cc < 0) continue;
-          if (cc >= G) break;
-          const int b0 = S.win[ph][w], b1 = S.win[ph][w + 1];
-          if (b0 >= e0) break;
-          if (b1 <= b0 || b1 <= s0) continue;  // empty, or ends before the tile
-          if (nsp < kTcMaxSplit) {
-            sg.split_cta[nsp] = (short)cc;
-            sg.split_slot[nsp] = (char)(2 * ph + (b0 >= s0 ? 0 : 1));
+        // the CTAs sharing the tile, ascending: the owners of its chunks (chunks restart at each half).
+        // A sharer whose range starts inside the tile holds it as its first tile (slot 0), any other
+        // as its last (slot 1).
+        int nsp = 0, prev = -1;
+        for (int sl = 0; sl < L;) {
+          int h0, hl;
+          g.half_of(ph, sl, &h0, &hl);
+          const int cc = owner(ph, tl, sl);
+          if (cc != prev) {
+            if (nsp < kTcMaxSplit) {
+              sg.split_cta[nsp] = (short)cc;
+              sg.split_slot[nsp] = (char)(2 * ph + (bnd(ph, cc) >= s0 ? 0 : 1));
+            }
+            ++nsp;
+            prev = cc;
           }
-          ++nsp;
+          sl = min(sl + kTcChunk, h0 + hl);
         }
         sg.nsplit = nsp;
         if (nsp > kTcMaxSplit) {

@@ -56,6 +56,8 @@ def test_tc_layer_matches_reference_golden(path):
     dict(E=16, k=4, T=2, H=512, F=768, seed=8),
     dict(arch="qwen3moe", E=32, k=8, H=1024, F=512, bias=False, norm=None, T=2, seed=9),
     dict(E=4, k=1, H=2880, F=2880, seed=10),                   # one expert: tiles split over many CTAs
+    dict(E=4, k=1, H=64, F=64, seed=11),                       # 4 K blocks: the sharers of a tile lie far apart
+    dict(E=8, k=2, T=2, H=128, F=192, seed=12),
 ])
 def test_tc_layer_matches_oracle_and_cuda_core_kernel(path, kw):
     L = goldens.SynthLayer(_cfg(**kw))
