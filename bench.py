@@ -32,7 +32,7 @@ sys.path.insert(0, str(ROOT))
 
 METRIC = "decode tok/s at batch 1 (GPT-OSS-120B shape); dequant-GEMV HBM GB/s vs 8 TB/s"
 UNIT = "tok/s"
-KERNEL = "moe_layer_kernel"
+KERNEL = "moe_tc_kernel"
 
 
 def workload_config(shape, world):
@@ -279,11 +279,13 @@ def run_ours(args, rank, world, local_rank, group):
                      "frac": round(achieved / (peak * (1 if world == 1 else world)), 4),
                      "traffic": None, "peak_kind": peak_kind, "kernel": KERNEL,
                      "algorithmic_bytes_per_launch": bytes_layer,
-                     "launch_ms": round(per_launch_s * 1000, 5)},
+                     "launch_ms": round(per_launch_s * 1000, 5),
+                     "launch_ms_from": "CUDA events over the timed region / layer launches in it (one kernel "
+                                       "per layer, back to back in the graph)"},
         "cuda_graph": graphed,
         "routing_identical_on_all_ranks": ids_ok,
     }
-    traffic = ROOT / "profiles" / "moe_layer_traffic.json"
+    traffic = ROOT / "profiles" / "moe_tc_kernel_traffic.json"
     if traffic.exists():
         try:
             line["roofline"]["traffic"] = json.loads(traffic.read_text()).get("dram_bytes_per_launch")

@@ -115,7 +115,7 @@ struct MoeTcArgs {
   unsigned* cnt2;    // per phase-2 row tile: pairs finished
   float* logits;     // T x E
   float* partial;    // per CTA: 2 phase-1 slots of 2*T*128 floats, then 2 phase-2 slots of 128
-  int part_floats;   // floats per CTA: (4*T + 2) * 128
+  int part_floats;   // floats per CTA: (2*T + 1) * 128
   uint8_t* actimg;   // per pair: planes [nb_f][8][16] then scales [nb_f][8]
   float* yp;         // per pair: H fp32
   int img_bytes;
@@ -125,12 +125,11 @@ struct MoeTcArgs {
   unsigned long long* trace;
 };
 
+// A segment: K blocks [k0, k1) of one tile.  A tile split over CTAs is finished by the CTA that
+// holds its first chunk (k0 == 0): the tile ends that CTA's range, so it is the last to get there.
+// Every other sharer meets the tile at the start of its range (k0 > 0) and only publishes.
 struct TcSeg {
-  int tile, k0, k1;            // K blocks [k0, k1) of the tile
-  int nsplit;                  // CTAs sharing the tile
-  short split_cta[kTcMaxSplit];
-  char split_slot[kTcMaxSplit];
-  int my_slot;                 // this CTA's partial slot: 2*phase + (0 first segment of the phase, 1 last)
+  int tile, k0, k1;
   int grp, sub;                // slot (phase 1) or pair (phase 2), and 128-row block within it
 };
 
@@ -154,6 +153,8 @@ struct TcShared {
   int nseg;
   TcSeg seg[kTcMaxSegs];
   int fin;
+  int nsh;                     // sharers of the tile being finished, other than this CTA
+  short sh_cta[kTcMaxSplit];   // ... in ascending order
   __align__(16) float scratch[NS_MAX_EXPERTS];
 };
 
@@ -174,6 +175,35 @@ struct TcGeom {
     const int w = off - h0;
     return h0 + min(hl, ((w + kTcChunk / 2) / kTcChunk) * kTcChunk);
   }
+  // chunks of a tile and the tile-local block each starts at (chunks restart at each half)
+  __device__ int nchunks(int ph) const {
+    return ph == 0 ? 2 * ((nb_h + kTcChunk - 1) / kTcChunk) : (nb_f + kTcChunk - 1) / kTcChunk;
+  }
+  __device__ int chunk_start(int ph, int q) const {
+    const int c0 = (nb_h + kTcChunk - 1) / kTcChunk;
+    return ph == 0 && q >= c0 ? nb_h + kTcChunk * (q - c0) : kTcChunk * q;
+  }
+  // Each phase's K blocks (tile-major) are split evenly over the G CTAs at chunk boundaries:
+  // CTA jj streams [bnd(jj), bnd(jj+1)).
+  __device__ int bnd(int ph, int jj, int G) const {
+    const int L = len(ph), U = (ph == 0 ? T1 : T2) * L;
+    if (jj <= 0) return 0;
+    if (jj >= G) return U;
+    const int u = (int)(((unsigned)U * (unsigned)jj) / (unsigned)G);  // U * G < 2^32 (host-checked)
+    const int i = (int)((unsigned)u / (unsigned)L);
+    return i * L + snap(ph, u - i * L);
+  }
+  // CTA holding the chunk that starts at tile-local block sl of tile tl: the last jj with
+  // bnd(jj) <= tl*L + sl.  snap(u) passes sl once u reaches sl + 7 (or the end of sl's half), so
+  // that jj is the last one with floor(U*jj/G) < u_t, i.e. ceil(u_t*G/U) - 1.
+  __device__ int owner(int ph, int tl, int sl, int G) const {
+    const int L = len(ph), U = (ph == 0 ? T1 : T2) * L;
+    int h0, hl;
+    half_of(ph, sl, &h0, &hl);
+    const unsigned ut = (unsigned)(tl * L + min(sl + kTcChunk / 2, h0 + hl));
+    const int jj = (int)((ut * (unsigned)G + (unsigned)U - 1u) / (unsigned)U) - 1;
+    return min(max(jj, 0), G - 1);
+  }
   // 8-row groups of a tile holding real rows (16, or 8 for a last half tile)
   __device__ int groups(int tile) const {
     const int rows = tile < T1 ? F - 128 * (tile % ns1) : H - 128 * ((tile - T1) % nr2);
@@ -181,11 +211,10 @@ struct TcGeom {
   }
 };
 
-// Partial-sum slot `slot` (2*phase + first/last) of CTA `cta`.
+// Partial sums CTA `cta` publishes in phase `ph` (at most one tile per phase: the first of its range).
 template <int NT>
-__device__ __forceinline__ float* tc_partial(float* base, int part_floats, int cta, int slot) {
-  float* b = base + (size_t)cta * part_floats;
-  return slot < 2 ? b + slot * (2 * NT * 128) : b + 2 * (2 * NT * 128) + (slot - 2) * 128;
+__device__ __forceinline__ float* tc_partial(float* base, int part_floats, int cta, int ph) {
+  return base + (size_t)cta * part_floats + (ph == 0 ? 0 : 2 * NT * 128);
 }
 
 __device__ __forceinline__ bool tc_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag) {
@@ -576,30 +605,11 @@ __global__ void __launch_bounds__(kTcThreads, 1) moe_tc_kernel(const __grid_cons
       g.nb_f = a.nb_f;
       g.H = H;
       g.F = F;
-      auto bnd = [&](int ph, int jj) -> int {  // start of CTA jj's range in phase ph (tile-major blocks)
-        const int L = g.len(ph), Uph = (ph == 0 ? g.T1 : g.T2) * L;
-        if (jj <= 0) return 0;
-        if (jj >= G) return Uph;
-        const int u = (int)(((unsigned)Uph * (unsigned)jj) / (unsigned)G);  // Uph * G < 2^32 (host-checked)
-        const int i = (int)((unsigned)u / (unsigned)L);
-        return i * L + g.snap(ph, u - i * L);
-      };
-      // CTA owning the chunk that starts at tile-local block sl of tile tl: the last jj with
-      // bnd(jj) <= tl*L + sl.  snap(u) passes sl once u reaches sl + 7 (or the end of sl's half),
-      // so that jj is the last one with floor(Uph*jj/G) < u_t, i.e. ceil(u_t*G/Uph) - 1.
-      auto owner = [&](int ph, int tl, int sl) -> int {
-        const int L = g.len(ph), Uph = (ph == 0 ? g.T1 : g.T2) * L;
-        int h0, hl;
-        g.half_of(ph, sl, &h0, &hl);
-        const unsigned ut = (unsigned)(tl * L + min(sl + kTcChunk / 2, h0 + hl));
-        const int jj = (int)((ut * (unsigned)G + (unsigned)Uph - 1u) / (unsigned)Uph) - 1;
-        return min(max(jj, 0), G - 1);
-      };
       int n[2], lo[2], hi[2];
       for (int ph = 0; ph < 2; ++ph) {
         const int L = g.len(ph);
-        lo[ph] = bnd(ph, c);
-        hi[ph] = bnd(ph, c + 1);
+        lo[ph] = g.bnd(ph, c, G);
+        hi[ph] = g.bnd(ph, c + 1, G);
         n[ph] = hi[ph] > lo[ph] ? (hi[ph] - 1) / L - lo[ph] / L + 1 : 0;
       }
       const int ns = n[0] + n[1];
@@ -617,32 +627,8 @@ __global__ void __launch_bounds__(kTcThreads, 1) moe_tc_kernel(const __grid_cons
         sg.tile = ph == 0 ? tl : g.T1 + tl;
         sg.k0 = max(lo[ph], s0) - s0;
         sg.k1 = min(hi[ph], e0) - s0;
-        sg.my_slot = 2 * ph + (li == 0 ? 0 : 1);
         sg.grp = ph == 0 ? tl / g.ns1 : tl / g.nr2;       // slot (phase 1) or pair (phase 2)
         sg.sub = ph == 0 ? tl - sg.grp * g.ns1 : tl - sg.grp * g.nr2;  // 128-row block within it
-        // the CTAs sharing the tile, ascending: the owners of its chunks (chunks restart at each half).
-        // A sharer whose range starts inside the tile holds it as its first tile (slot 0), any other
-        // as its last (slot 1).
-        int nsp = 0, prev = -1;
-        for (int sl = 0; sl < L;) {
-          int h0, hl;
-          g.half_of(ph, sl, &h0, &hl);
-          const int cc = owner(ph, tl, sl);
-          if (cc != prev) {
-            if (nsp < kTcMaxSplit) {
-              sg.split_cta[nsp] = (short)cc;
-              sg.split_slot[nsp] = (char)(2 * ph + (bnd(ph, cc) >= s0 ? 0 : 1));
-            }
-            ++nsp;
-            prev = cc;
-          }
-          sl = min(sl + kTcChunk, h0 + hl);
-        }
-        sg.nsplit = nsp;
-        if (nsp > kTcMaxSplit) {
-          raise_device_error(NS_DEVERR_ROUTE);
-          S.abort_flag = 1;
-        }
       }
       if (lane == 0) {
         S.nseg = ns > kTcMaxSegs ? 0 : ns;
@@ -951,6 +937,55 @@ __global__ void __launch_bounds__(kTcThreads, 1) moe_tc_kernel(const __grid_cons
         const int el = S.slot_expert[S.pair_slot[qq / geo.nr2]] - p.expert_lo;
         if (r < H && p.down_b) bias0 = p.down_b[(int64_t)el * H + r];
       }
+      // ---- split tile, finishing side: find the other sharers and sum their partials (published at
+      // the start of their ranges) while this CTA's own MMAs for the tile are still running
+      const int L = geo.len(ph);
+      const bool split = !(sg.k0 == 0 && sg.k1 == L), finisher = sg.k0 == 0;
+      float pre[2 * NT];
+#pragma unroll
+      for (int v = 0; v < 2 * NT; ++v) pre[v] = 0.f;
+      if (split && finisher) {
+        if (q == 0) {
+          const int nq = geo.nchunks(ph), tl = ph == 0 ? i : i - geo.T1;
+          const int cc = lane < nq ? geo.owner(ph, tl, geo.chunk_start(ph, lane), G) : -1;
+          const int prev = __shfl_up_sync(0xffffffffu, cc, 1);
+          const bool nw = lane > 0 && lane < nq && cc != prev;  // owners ascend; chunk 0 is this CTA's
+          const unsigned m = __ballot_sync(0xffffffffu, nw);
+          if (nw) S.sh_cta[__popc(m & ((1u << lane) - 1u))] = (short)cc;
+          if (lane == 0) S.nsh = __popc(m);
+        }
+        named_sync(1, 128);
+        const int nsh = S.nsh;
+        if (et == 0) {  // each sharer adds 1 after publishing
+          const uint64_t t0 = globaltimer_ns();
+          while (ld_acquire_u32(a.cnt + i) < (unsigned)nsh) {
+            if (*abort_flag) break;
+            if (globaltimer_ns() - t0 > kWaitLimitNs) {
+              raise_device_error(NS_DEVERR_GRID_WAIT);
+              *abort_flag = 1;
+              break;
+            }
+            __nanosleep(32);
+          }
+        }
+        named_sync(1, 128);
+        const int nv0 = ph == 0 ? 2 * NT : 1;
+        for (int g0 = 0; g0 < nsh; g0 += 4) {  // four sharers' loads in flight, then summed in order
+          float pv[4][2 * NT];
+#pragma unroll
+          for (int g = 0; g < 4; ++g) {
+            const bool ok = g0 + g < nsh;
+            const float* pg = tc_partial<NT>(a.partial, a.part_floats, ok ? S.sh_cta[g0 + g] : c, ph);
+#pragma unroll
+            for (int v = 0; v < 2 * NT; ++v) pv[g][v] = ok && v < nv0 ? __ldcg(pg + v * 128 + mrow) : 0.f;
+          }
+#pragma unroll
+          for (int g = 0; g < 4; ++g)
+#pragma unroll
+            for (int v = 0; v < 2 * NT; ++v)
+              if (g0 + g < nsh) pre[v] += pv[g][v];
+        }
+      }
       if (!tc_wait(&full_d[db], (sgi >> 1) & 1, abort_flag)) break;
       tc_fence_after();
       // vals: phase 1 gate[t] at t, up[t] at NT + t; phase 2 the down row at 0
@@ -988,38 +1023,19 @@ __global__ void __launch_bounds__(kTcThreads, 1) moe_tc_kernel(const __grid_cons
       if (lane == 0) mbar_arrive(&empty_d[db]);
       const int nv = ph == 0 ? 2 * NT : 1;
 
-      // ---- split tile: publish this segment's partial; the last CTA to arrive finishes the tile
-      if (sg.nsplit > 1) {
-        float* part = tc_partial<NT>(a.partial, a.part_floats, c, sg.my_slot);
+      if (split && !finisher) {
+        // ---- split tile, publishing side: this CTA's partial sums, then one count on the tile
+        float* part = tc_partial<NT>(a.partial, a.part_floats, c, ph);
 #pragma unroll
         for (int v = 0; v < 2 * NT; ++v)
           if (v < nv) __stcg(part + v * 128 + mrow, vals[v]);
         named_sync(1, 128);
-        if (et == 0) {
-          const unsigned old = atom_add_acq_rel(a.cnt + i, 1u);
-          S.fin = old == (unsigned)(sg.nsplit - 1);
-        }
-        named_sync(1, 128);
-        if (!S.fin) continue;
-        // all partials loaded together (up to 4 segments at a time), then summed in segment order
+        if (et == 0) red_add_release(a.cnt + i, 1u);
+        continue;
+      }
+      if (split) {  // finishing side: own sum first, then the sharers' in CTA order
 #pragma unroll
-        for (int v = 0; v < 2 * NT; ++v) vals[v] = 0.f;
-        for (int g0 = 0; g0 < sg.nsplit; g0 += 4) {
-          float pv[4][2 * NT];
-#pragma unroll
-          for (int g = 0; g < 4; ++g) {
-            const bool ok = g0 + g < sg.nsplit;
-            const float* pg = ok ? tc_partial<NT>(a.partial, a.part_floats, sg.split_cta[g0 + g], sg.split_slot[g0 + g])
-                                 : nullptr;
-#pragma unroll
-            for (int v = 0; v < 2 * NT; ++v) pv[g][v] = ok && v < nv ? __ldcg(pg + v * 128 + mrow) : 0.f;
-          }
-#pragma unroll
-          for (int g = 0; g < 4; ++g)
-#pragma unroll
-            for (int v = 0; v < 2 * NT; ++v)
-              if (g0 + g < sg.nsplit) vals[v] += pv[g][v];
-        }
+        for (int v = 0; v < 2 * NT; ++v) vals[v] += pre[v];
       }
 
       if (ph == 0) {
@@ -1134,7 +1150,7 @@ static void moe_tc_plan(const ns_moe_layer_t* p, int grid, TcPlan* t) {
   const int pairs = p->T * p->k;
   const int nb_f = p->F / 32;
   t->grid = grid;
-  t->part_floats = (4 * p->T + 2) * 128;
+  t->part_floats = (2 * p->T + 1) * 128;
   t->img_bytes = (int)align_up((size_t)nb_f * 128 + (size_t)nb_f * 8, 256);
   t->max_tiles = pairs * ((p->F + 127) / 128) + pairs * ((p->H + 127) / 128);
   size_t off = kTcWsHeader;
