@@ -169,7 +169,13 @@ typedef struct ns_moe_layer {
 } ns_moe_layer_t;
 
 /* Workspace bytes a layer call needs (zeroed once with ns_moe_workspace_init;
- * one workspace serves any number of stream-ordered calls on one device). */
+ * one workspace serves any number of stream-ordered calls on one device).
+ * The tensor-core layer kernel is launched with programmatic dependent launch:
+ * it may read norm_w and router_w before the previous kernel on the stream has
+ * finished, if that kernel signals its dependents early (the layer kernel
+ * itself does so). Do not write a layer's weights in such a kernel; x, the
+ * workspace and everything else are read only after the previous kernel
+ * completes. */
 int ns_moe_workspace_bytes(const ns_moe_layer_t* p, size_t* bytes);
 int ns_moe_workspace_init(void* workspace, size_t bytes, ns_stream_t stream);
 int ns_moe_decode_layer(const ns_moe_layer_t* p, void* workspace, size_t workspace_bytes,

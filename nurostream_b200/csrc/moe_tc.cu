@@ -365,36 +365,44 @@ __global__ void __launch_bounds__(kTcThreads, 1) moe_tc_kernel(const __grid_cons
     prefetch_tmap(&a.tm_down16);
   }
   if (warp == kTcMmaWarp) tmem_alloc(&S.tmem_base, kTcTmemCols);
+
+  // ---- 1. x into shared memory, RMSNorm sum of squares, this CTA's router logit.  The layer's own
+  // constants (norm weight, this CTA's router row; one pass covers H <= 4096) are loaded before the
+  // wait on the previous kernel of the stream: under programmatic dependent launch that wait is
+  // where x and the workspace, which the previous layer wrote, become visible.
+  static_assert(128 * 32 <= 8 * kTcThreads, "H <= 4096 (moe_tc_eligible) must fit one pass");
+  float* h = reinterpret_cast<float*>(raw);  // T x H fp32, reused by the raw ring after the prologue
+  const bool own_expert = c < E;
+  float wv[8], rv[8];
+#pragma unroll
+  for (int u = 0; u < 8; ++u) {
+    const int i = tid + u * kTcThreads;
+    const bool ok = i < H;
+    wv[u] = ok && p.norm_w ? p.norm_w[i] : 1.0f;
+    rv[u] = ok && own_expert ? load_float(p.router_w, p.router_dtype, (int64_t)c * H + i) : 0.f;
+  }
+  griddep_wait();
   // counters of this launch (used only after the routing barrier)
   if (c == 0) {
     for (int i = tid; i < a.zero_tiles; i += kTcThreads) a.cnt[i] = 0u;
     for (int i = tid; i < kMaxPairs; i += kTcThreads) a.ready[i] = 0u;
     for (int i = tid; i < kTcMaxRowTiles; i += kTcThreads) a.cnt2[i] = 0u;
   }
-
-  // ---- 1. x into shared memory, RMSNorm sum of squares, this CTA's router logit
-  float* h = reinterpret_cast<float*>(raw);  // T x H fp32, reused by the raw ring after the prologue
-  const bool own_expert = c < E;
   for (int t = 0; t < T; ++t) {
     float ss = 0.f, dot = 0.f;
-    for (int i0 = tid; i0 < H; i0 += 8 * kTcThreads) {  // 8 loads in flight per thread, then the sums in order
-      float xv[8], wv[8], rv[8];
+    float xv[8];
 #pragma unroll
-      for (int u = 0; u < 8; ++u) {
-        const int i = i0 + u * kTcThreads;
-        const bool ok = i < H;
-        xv[u] = ok ? p.x[(int64_t)t * H + i] : 0.f;
-        wv[u] = ok && p.norm_w ? p.norm_w[i] : 1.0f;
-        rv[u] = ok && own_expert ? load_float(p.router_w, p.router_dtype, (int64_t)c * H + i) : 0.f;
-      }
+    for (int u = 0; u < 8; ++u) {  // 8 loads in flight per thread, then the sums in order
+      const int i = tid + u * kTcThreads;
+      xv[u] = i < H ? p.x[(int64_t)t * H + i] : 0.f;
+    }
 #pragma unroll
-      for (int u = 0; u < 8; ++u) {
-        const int i = i0 + u * kTcThreads;
-        if (i < H) {
-          h[t * H + i] = xv[u];
-          ss = fmaf(xv[u], xv[u], ss);
-          dot = fmaf(xv[u] * wv[u], rv[u], dot);
-        }
+    for (int u = 0; u < 8; ++u) {
+      const int i = tid + u * kTcThreads;
+      if (i < H) {
+        h[t * H + i] = xv[u];
+        ss = fmaf(xv[u], xv[u], ss);
+        dot = fmaf(xv[u] * wv[u], rv[u], dot);
       }
     }
     ss = warp_sum(ss);
@@ -417,16 +425,11 @@ __global__ void __launch_bounds__(kTcThreads, 1) moe_tc_kernel(const __grid_cons
   }
   __syncthreads();
   if (p.norm_w)
-    for (int i0 = tid; i0 < H; i0 += 8 * kTcThreads) {
-      float wv[8];
 #pragma unroll
-      for (int u = 0; u < 8; ++u) wv[u] = i0 + u * kTcThreads < H ? p.norm_w[i0 + u * kTcThreads] : 0.f;
-#pragma unroll
-      for (int u = 0; u < 8; ++u) {
-        const int i = i0 + u * kTcThreads;
-        if (i < H)
-          for (int t = 0; t < T; ++t) h[t * H + i] = __fmul_rn(__fmul_rn(h[t * H + i], S.rscale[t]), wv[u]);
-      }
+    for (int u = 0; u < 8; ++u) {
+      const int i = tid + u * kTcThreads;
+      if (i < H)
+        for (int t = 0; t < T; ++t) h[t * H + i] = __fmul_rn(__fmul_rn(h[t * H + i], S.rscale[t]), wv[u]);
     }
   __syncthreads();
   if (tid == 0) stamp(a.trace, kEvNorm);
@@ -473,6 +476,9 @@ __global__ void __launch_bounds__(kTcThreads, 1) moe_tc_kernel(const __grid_cons
       __nanosleep(32);
     }
     stamp(a.trace, kEvBarrier1);
+    // every CTA of this layer is past its reads of the previous layer's results: the next kernel in
+    // the stream may start its CTAs as SMs free up (they wait for this grid before reading x)
+    griddep_launch_dependents();
   }
   __syncthreads();
 
@@ -1228,6 +1234,8 @@ static int make_row_group_map(CUtensorMap* m, const uint8_t* base, int64_t rows,
   return NS_OK;
 }
 
+static bool g_tc_pdl = true;  // programmatic dependent launch accepted so far
+
 template <int NT>
 static int launch_moe_tc(const MoeTcArgs& a, int grid, size_t smem, cudaStream_t stream) {
   auto kern = moe_tc_kernel<NT>;
@@ -1240,12 +1248,24 @@ static int launch_moe_tc(const MoeTcArgs& a, int grid, size_t smem, cudaStream_t
   cfg.blockDim = dim3(kTcThreads);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
+  // Programmatic dependent launch: this grid's CTAs may start while the previous kernel of the
+  // stream finishes; the kernel waits for it (griddepcontrol.wait) before reading anything that
+  // kernel may have written other than the layer's weights.
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeCooperative;
   attr[0].val.cooperative = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  NS_CUDA_TRY(cudaLaunchKernelEx(&cfg, kern, a));
+  cfg.numAttrs = g_tc_pdl ? 2 : 1;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, kern, a);
+  if (e != cudaSuccess && g_tc_pdl) {  // runtime without programmatic launch for cooperative grids
+    (void)cudaGetLastError();
+    g_tc_pdl = false;
+    cfg.numAttrs = 1;
+    e = cudaLaunchKernelEx(&cfg, kern, a);
+  }
+  NS_CUDA_TRY(e);
   return NS_OK;
 }
 
