@@ -52,16 +52,24 @@ class MoeShape:
         return router + experts + biases + acts
 
 
+def expert_range(rank: int, world: int, n_expert: int) -> tuple[int, int]:
+    """Experts [lo, hi) that rank `rank` of `world` holds: an even, contiguous split by index.
+
+    Each rank's share is one row window of every stacked expert tensor.  Rank 0 also adds the
+    residual, so summing the ranks' layer outputs gives the full layer.
+    """
+    if n_expert % world:
+        raise ValueError(f"{n_expert} experts do not split evenly over {world} ranks")
+    return rank * n_expert // world, (rank + 1) * n_expert // world
+
+
 class MoeDecoder:
     def __init__(self, shape: MoeShape, device: torch.device | str = "cuda", rank: int = 0, world: int = 1,
                  group=None, use_graph: bool = True):
         self.shape = shape
         self.device = torch.device(device)
         self.rank, self.world, self.group = rank, world, group
-        E = shape.n_expert
-        if E % world:
-            raise ValueError(f"{E} experts do not split evenly over {world} ranks")
-        self.lo, self.hi = rank * E // world, (rank + 1) * E // world
+        self.lo, self.hi = expert_range(rank, world, shape.n_expert)
         self.layers = [self._make_layer(l) for l in range(shape.n_layer)]
         H = shape.hidden
         self.x = torch.zeros((1, H), device=self.device, dtype=torch.float32)
