@@ -193,7 +193,8 @@ int ns_moe_decode_layer(const ns_moe_layer_t* p, void* workspace, size_t workspa
  * Same computation and results as ns_moe_decode_layer; the scratch comes from
  * one fixed array of NS_MOE_STATIC_SCRATCH_BYTES linked into the library, one
  * per device.  A layer whose ns_moe_workspace_bytes exceeds that returns
- * NS_ERR_SIZE without launching (T=1, k=4, F=2880, 128 experts needs 47,616).
+ * NS_ERR_SIZE without launching (T=1, k=4, H=F=2880, 128 experts needs
+ * 349,696).
  * The first call on a device (that device current) resolves and clears the
  * array and synchronises the device: make it before any stream capture.
  * Calls that overlap on the GPU (unordered streams) race on the one array and
