@@ -6,6 +6,12 @@ One step = one decode token through 36 MoE layers (RMSNorm -> router top-4 of
 bytes per step (1.9 GB) are far larger than L2 (126 MB), so no flush is needed.
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+  python bench.py --workload gemv [--steps K] [--warmup W]
+
+``--workload gemv`` measures the dense dequant-GEMV sweep instead (batch 1,
+K = 4096, N in {4096, 11008, 14336}, MXFP4 / Q4_K / Q8_0): one JSON line per
+case, HBM GB/s against the measured copy peak, weight copies rotated so that
+every launch streams from HBM.
 
 N > 1 runs expert parallel under torchrun (experts split by index, one NCCL
 all-reduce per layer).  ``--impl reference`` times the reference's CPU path
@@ -305,6 +311,81 @@ def run_ours(args, rank, world, local_rank, group):
     return line
 
 
+def run_gemv_sweep(args):
+    """Dense dequant-GEMV at batch 1 (the reference's ``fused_gemv``, ``triton_kernels.py:199-228``).
+
+    Each case rotates over enough copies of the weight matrix (>= 512 MB) that no launch finds its
+    rows in the 126 MB L2; one step is one launch through ``ns_gemv``, timed with CUDA events on
+    the launching stream.  Algorithmic bytes: the rows, x (fp32) and y (fp32).
+    """
+    import torch
+
+    from nurostream_b200 import _lib, synth
+    from nurostream_b200.ggml import GGMLType, row_bytes
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    stream = torch.cuda.current_stream(dev)
+    peak, peak_kind = measured_peaks()
+    K = 4096
+    lines = []
+    for t in (GGMLType.MXFP4, GGMLType.Q4_K, GGMLType.Q8_0):
+        for N in (4096, 11008, 14336):
+            if args.gemv_case and args.gemv_case != f"{t.name}:{N}":
+                continue
+            rb = row_bytes(t, K)
+            mbytes = N * rb
+            copies = max(2, -(-(512 << 20) // mbytes))
+            w = torch.empty(copies * mbytes, dtype=torch.uint8, device=dev)
+            synth.fill_quant(w, t, 0, 900 + int(t), 0)
+            x = torch.empty((1, K), dtype=torch.float32, device=dev)
+            synth.fill_float(x.view(-1), 0, 901, 0)
+            y = torch.empty((1, N), dtype=torch.float32, device=dev)
+
+            def launch(i):
+                _lib.call("ns_gemv", w.data_ptr() + (i % copies) * mbytes, mbytes, int(t), N, K,
+                          x.data_ptr(), _lib.NS_F32, K, 1, y.data_ptr(), _lib.NS_F32, N,
+                          torch.cuda.current_stream(dev).cuda_stream)
+
+            # one graph of `copies` back-to-back launches (each on the next copy), replayed: the timing
+            # is the kernels', not the host's launch rate
+            for i in range(copies):
+                launch(i)
+            torch.cuda.synchronize()
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g):
+                for i in range(copies):
+                    launch(i)
+            reps = max(1, -(-args.steps // copies))
+            for _ in range(max(1, args.warmup // copies)):
+                g.replay()
+            torch.cuda.synchronize()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            for _ in range(reps):
+                g.replay()
+            e1.record(stream)
+            torch.cuda.synchronize()
+            n_launches = reps * copies
+            us = e0.elapsed_time(e1) * 1000.0 / n_launches
+            nbytes = mbytes + 4 * K + 4 * N
+            gbs = nbytes / (us * 1e-6) / 1e9
+            lines.append({
+                "metric": "dequant-GEMV HBM GB/s at batch 1", "value": round(gbs, 1), "unit": "GB/s",
+                "n_gpus": 1, "steps": n_launches, "warmup": args.warmup, "us_per_launch": round(us, 3),
+                "higher_is_better": True, "dtype": f"{t.name} weights, fp32 accumulate",
+                "data": "synthetic (seeded splitmix64 GGUF bytes generated in HBM)",
+                "config": {"workload": f"dense dequant-GEMV {t.name} N={N} K={K} T=1", "type": t.name, "N": N,
+                           "K": K, "l2": f"{copies} rotated weight copies ({copies * mbytes >> 20} MiB) per case"},
+                "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": peak, "unit": "GB/s",
+                             "frac": round(gbs / peak, 4), "peak_kind": peak_kind, "kernel": "gemv_kernel",
+                             "algorithmic_bytes_per_launch": nbytes},
+            })
+            del g, w
+            torch.cuda.empty_cache()
+    return lines
+
+
 def run_reference(args, rank, world):
     """The reference's own CPU implementation of the path (oracle port), host cores only.
 
@@ -356,6 +437,8 @@ def main():
     ap.add_argument("--ref-layers", type=int, default=2)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-graph", action="store_true")
+    ap.add_argument("--workload", choices=["decode", "gemv"], default="decode")
+    ap.add_argument("--gemv-case", default="", help="run one GEMV case only, e.g. MXFP4:14336")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
 
@@ -363,6 +446,10 @@ def main():
     rank = int(os.environ.get("RANK", "0"))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
     group = None
+    if args.workload == "gemv":
+        for line in run_gemv_sweep(args):
+            print(json.dumps(line), flush=True)
+        return
     if args.impl == "reference":
         line = run_reference(args, rank, world)
     else:

@@ -14,6 +14,7 @@ namespace ns {
 constexpr int kGemvThreads = 256;
 constexpr int kGemvStages = 3;
 constexpr int kSmemBudget = 220 * 1024;
+constexpr int kXG = 36;  // shared-memory floats per 32-element group of x
 
 struct GemvArgs {
   const uint8_t* w;
@@ -34,8 +35,9 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(GemvArgs a) {
   extern __shared__ __align__(128) uint8_t smem[];
   const int K = a.K, T = a.T;
   float* xs = reinterpret_cast<float*>(smem);
-  const int x_floats = ((T * K + 31) / 32) * 32;
-  uint8_t* stages = smem + x_floats * 4;
+  // x in fp32, each 32-element group padded to kXG floats (lane g reads group g: distinct banks)
+  const int xt = (K / 32) * kXG;  // floats per token
+  uint8_t* stages = smem + (size_t)T * xt * 4;
   uint64_t* bars = reinterpret_cast<uint64_t*>(stages + kGemvStages * a.stage_bytes);
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -67,7 +69,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(GemvArgs a) {
   // activations -> fp32 shared memory (overlaps with the first copies)
   for (int i = tid; i < T * K; i += kGemvThreads) {
     int t = i / K, k = i - t * K;
-    xs[i] = load_float(a.x, a.x_dtype, (int64_t)t * a.x_stride + k);
+    xs[t * xt + (k >> 5) * kXG + (k & 31)] = load_float(a.x, a.x_dtype, (int64_t)t * a.x_stride + k);
   }
   __syncthreads();
 
@@ -98,7 +100,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(GemvArgs a) {
         int tok[NT];
 #pragma unroll
         for (int t = 0; t < NT; ++t) tok[t] = t;
-        dot_rows<FMT, NT, R>(rows, nrows, ngroups, lane, xs, K, tok, T, acc);
+        dot_rows<FMT, NT, R, kXG>(rows, nrows, ngroups, lane, xs, xt, tok, T, acc);
 #pragma unroll
         for (int r = 0; r < R; ++r) {
 #pragma unroll
@@ -161,7 +163,7 @@ extern "C" int ns_gemv(const uint8_t* w, size_t w_bytes, int ggml_type, int n_ro
   int nsm = 0;
   int st = num_sms(&nsm);
   if (st) return st;
-  const size_t x_bytes = (size_t)((T * K + 31) / 32) * 32 * 4;
+  const size_t x_bytes = (size_t)T * (K / 32) * kXG * 4;
   if (x_bytes + kGemvStages * (rb + 64) + 64 > (size_t)kSmemBudget)
     return fail(NS_ERR_UNSUPPORTED, "ns_gemv: T*K=%d activations plus a %lld-byte row exceed shared memory",
                 T * K, (long long)rb);

@@ -64,13 +64,13 @@ struct QGroup<NS_GGML_MXFP4> {
     for (int i = 0; i < 4; ++i) q[i] = __funnelshift_r(w[i], w[i + 1], 8);
   }
   // sub-chunk s: payload bytes 4s..4s+3 -> elements {4s+i, 16+4s+i}
-  template <int NT>
+  template <int NT, int XG = 32>
   static __device__ __forceinline__ void load_x(const float* x, int64_t xs, const int (&tok)[NT], int nt, int g,
                                                 int s, float (&xv)[NT][8]) {
 #pragma unroll
     for (int t = 0; t < NT; ++t) {
       if (t < nt) {
-        const float* p = x + tok[t] * xs + 32 * g;
+        const float* p = x + tok[t] * xs + XG * g;
         float4 a = *reinterpret_cast<const float4*>(p + 4 * s);
         float4 b = *reinterpret_cast<const float4*>(p + 16 + 4 * s);
         xv[t][0] = a.x; xv[t][1] = b.x; xv[t][2] = a.y; xv[t][3] = b.y;
@@ -112,13 +112,13 @@ struct QGroup<NS_GGML_Q8_0> {
 #pragma unroll
     for (int i = 0; i < 8; ++i) q[i] = __funnelshift_r(w[i], w[i + 1], 16) ^ 0x80808080u;
   }
-  template <int NT>
+  template <int NT, int XG = 32>
   static __device__ __forceinline__ void load_x(const float* x, int64_t xs, const int (&tok)[NT], int nt, int g,
                                                 int s, float (&xv)[NT][8]) {
 #pragma unroll
     for (int t = 0; t < NT; ++t) {
       if (t < nt) {
-        const float* p = x + tok[t] * xs + 32 * g + 8 * s;
+        const float* p = x + tok[t] * xs + XG * g + 8 * s;
         float4 a = *reinterpret_cast<const float4*>(p);
         float4 b = *reinterpret_cast<const float4*>(p + 4);
         xv[t][0] = a.x; xv[t][1] = a.y; xv[t][2] = a.z; xv[t][3] = a.w;
@@ -176,10 +176,10 @@ struct QGroup<NS_GGML_Q4_K> {
 #pragma unroll
     for (int i = 0; i < 8; ++i) q[i] = (w[i] >> sh) & 0x0F0F0F0Fu;
   }
-  template <int NT>
+  template <int NT, int XG = 32>
   static __device__ __forceinline__ void load_x(const float* x, int64_t xs, const int (&tok)[NT], int nt, int g,
                                                 int s, float (&xv)[NT][8]) {
-    QGroup<NS_GGML_Q8_0>::load_x<NT>(x, xs, tok, nt, g, s, xv);
+    QGroup<NS_GGML_Q8_0>::load_x<NT, XG>(x, xs, tok, nt, g, s, xv);
   }
   template <int NT>
   __device__ __forceinline__ void fma(int s, const float (&xv)[NT][8], int nt, float (&part)[NT][kParts]) const {
@@ -225,10 +225,10 @@ struct QGroup<NS_GGML_Q6_K> {
     dsc0 = d * (float)(int8_t)(scw & 0xFFu);
     dsc1 = d * (float)(int8_t)((scw >> 8) & 0xFFu);
   }
-  template <int NT>
+  template <int NT, int XG = 32>
   static __device__ __forceinline__ void load_x(const float* x, int64_t xs, const int (&tok)[NT], int nt, int g,
                                                 int s, float (&xv)[NT][8]) {
-    QGroup<NS_GGML_Q8_0>::load_x<NT>(x, xs, tok, nt, g, s, xv);
+    QGroup<NS_GGML_Q8_0>::load_x<NT, XG>(x, xs, tok, nt, g, s, xv);
   }
   template <int NT>
   __device__ __forceinline__ void fma(int s, const float (&xv)[NT][8], int nt, float (&part)[NT][kParts]) const {
@@ -255,8 +255,9 @@ struct QGroup<NS_GGML_Q6_K> {
 // acc[r][t] += sum over this lane's groups of row r (smem) . x[t]
 // rows[r] may be nullptr (row absent) for r >= nrows; nrows is warp-uniform.
 // x: generic pointer; token t's activations are the row x + tok[t]*xs (floats,
-// 16-byte aligned rows), for t < nt <= NT.
-template <int FMT, int NT, int R>
+// 16-byte aligned rows), group g of it at + XG*g, for t < nt <= NT.  In shared
+// memory XG = 36 keeps the lanes (one group each) on distinct banks.
+template <int FMT, int NT, int R, int XG = 32>
 __device__ __forceinline__ void dot_rows(const uint8_t* const (&rows)[R], int nrows, int ngroups, int lane,
                                          const float* x, int64_t xs, const int (&tok)[NT], int nt,
                                          float (&acc)[R][NT]) {
@@ -279,7 +280,7 @@ __device__ __forceinline__ void dot_rows(const uint8_t* const (&rows)[R], int nr
 #pragma unroll
     for (int s = 0; s < 4; ++s) {
       float xv[NT][8];
-      G::template load_x<NT>(x, xs, tok, nt, g, s, xv);
+      G::template load_x<NT, XG>(x, xs, tok, nt, g, s, xv);
       if (FMT == NS_GGML_Q4_K) {
 #pragma unroll
         for (int t = 0; t < NT; ++t)
