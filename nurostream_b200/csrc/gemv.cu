@@ -1,18 +1,26 @@
 // ns_gemv: fused dequant-GEMV from GGUF bytes (batch 1..NS_MAX_TOKENS).
 //
-// Layout: each CTA owns a contiguous run of rows, walked in tiles of TR rows.
-// A tile's bytes are one contiguous range of the weight buffer; thread 0
-// streams tiles into a 3-stage shared-memory ring with 1-D bulk copies (the
-// TMA engine, completion on an mbarrier), so ~2 tiles are in flight while the
-// CTA decodes the third.  The activations are converted to fp32 once per CTA
-// and kept in shared memory.  8 warps split a tile's rows R at a time; the 32
-// lanes of a warp split each row's 32-element groups (qdot.cuh).
+// Layout: each CTA owns a contiguous run of rows, walked in tiles of TILE rows
+// (16, or 8 for wide rows and several tokens).  A tile's bytes are one
+// contiguous range of the weight buffer; thread 0 streams tiles into a ring of
+// shared-memory stages with 1-D bulk copies (the TMA engine, completion on an
+// mbarrier).  The activations are converted to fp32 once per CTA and kept in
+// shared memory, each 32-element group padded to kXG floats so that lanes
+// reading different groups hit different banks.
+//
+// Work split of a tile: the W warps take interleaved slices of K, and each
+// warp's lanes form RS row subsets of LG = 32/RS lanes: lane (s, j) takes
+// rows s, s + RS, .. of the tile and the groups w*LG + j, + W*LG, .. of K.  So
+// every lane runs TILE/RS independent row sums and loads each activation
+// group once for all of them.  Lane sums meet by shuffles within each subset,
+// then across the W warps in shared memory, in a fixed order.  One token:
+// 16 warps x 4 subsets (4 rows a lane); more tokens: 8 warps x 2 subsets.
 #include "qdot.cuh"
 
 namespace ns {
 
-constexpr int kGemvThreads = 256;
-constexpr int kGemvStages = 3;
+constexpr int kGemvMaxWarps = 16;
+constexpr int kGemvMaxStages = 6;
 constexpr int kSmemBudget = 220 * 1024;
 constexpr int kXG = 36;  // shared-memory floats per 32-element group of x
 
@@ -26,112 +34,123 @@ struct GemvArgs {
   void* y;
   int y_dtype;
   int64_t y_stride;
-  int tile_rows;
+  int stages;
   int stage_bytes;
 };
 
-template <int FMT, int NT, int R>
-__global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(GemvArgs a) {
+template <int FMT, int NT, int TILE, int W, int RS>
+__global__ void __launch_bounds__(W * 32, 1) gemv_kernel(GemvArgs a) {
+  constexpr int kThreads = W * 32, LG = 32 / RS, R = TILE / RS;  // lanes per row subset, rows per lane
   extern __shared__ __align__(128) uint8_t smem[];
-  const int K = a.K, T = a.T;
+  const int K = a.K, T = a.T, nst = a.stages;
   float* xs = reinterpret_cast<float*>(smem);
-  // x in fp32, each 32-element group padded to kXG floats (lane g reads group g: distinct banks)
   const int xt = (K / 32) * kXG;  // floats per token
-  uint8_t* stages = smem + (size_t)T * xt * 4;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(stages + kGemvStages * a.stage_bytes);
+  float* red = xs + NT * xt;      // 2 x [warp][row][token] partial sums
+  uint8_t* stages = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(red + 2 * W * TILE * NT) + 127) & ~uintptr_t(127));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(stages + nst * a.stage_bytes);
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
 
   // contiguous, balanced row range of this CTA
   const int r_begin = (int)((int64_t)a.n_rows * blockIdx.x / gridDim.x);
   const int r_end = (int)((int64_t)a.n_rows * (blockIdx.x + 1) / gridDim.x);
-  const int n_tiles = (r_end - r_begin + a.tile_rows - 1) / a.tile_rows;
+  const int n_tiles = (r_end - r_begin + TILE - 1) / TILE;
 
   auto tile_span = [&](int i) -> Span {
-    int r0 = r_begin + i * a.tile_rows;
-    int r1 = min(r0 + a.tile_rows, r_end);
+    int r0 = r_begin + i * TILE;
+    int r1 = min(r0 + TILE, r_end);
     return Span{a.w + (int64_t)r0 * a.rb, a.w + (int64_t)r1 * a.rb};
   };
   auto issue = [&](int i) {
-    uint64_t* bar = &bars[i % kGemvStages];
+    uint64_t* bar = &bars[i % nst];
     Span s = tile_span(i);
     uintptr_t lo, hi;
     bulk_window(s, a.w, a.w_end, &lo, &hi);
     mbar_arrive_expect_tx(bar, hi > lo ? (uint32_t)(hi - lo) : 0u);
-    issue_span(stages + (i % kGemvStages) * a.stage_bytes, s, a.w, a.w_end, bar);
+    issue_span(stages + (i % nst) * a.stage_bytes, s, a.w, a.w_end, bar);
   };
 
   if (tid == 0) {
-    for (int s = 0; s < kGemvStages; ++s) mbar_init(&bars[s], 1);
+    for (int s = 0; s < nst; ++s) mbar_init(&bars[s], 1);
     fence_mbar_init();
-    for (int i = 0; i < kGemvStages && i < n_tiles; ++i) issue(i);
+    for (int i = 0; i < nst && i < n_tiles; ++i) issue(i);
   }
-  // activations -> fp32 shared memory (overlaps with the first copies)
-  for (int i = tid; i < T * K; i += kGemvThreads) {
+  // activations -> padded fp32 shared memory (overlaps with the first copies); token slots T..NT-1
+  // hold zeros, so every lane computes all NT slots without tests
+  for (int i = tid; i < NT * K; i += kThreads) {
     int t = i / K, k = i - t * K;
-    xs[t * xt + (k >> 5) * kXG + (k & 31)] = load_float(a.x, a.x_dtype, (int64_t)t * a.x_stride + k);
+    xs[t * xt + (k >> 5) * kXG + (k & 31)] = t < T ? load_float(a.x, a.x_dtype, (int64_t)t * a.x_stride + k) : 0.f;
   }
   __syncthreads();
 
   const int ngroups = K / 32;
+  const int sub = lane / LG, lg = lane % LG;
+  int tok[NT];
+#pragma unroll
+  for (int t = 0; t < NT; ++t) tok[t] = t;
   for (int i = 0; i < n_tiles; ++i) {
-    const int st = i % kGemvStages;
+    const int st = i % nst;
     uint8_t* buf = stages + st * a.stage_bytes;
     const Span s = tile_span(i);
-    bool ok = mbar_wait_bounded(&bars[st], (uint32_t)((i / kGemvStages) & 1));
+    bool ok = mbar_wait_bounded(&bars[st], (uint32_t)((i / nst) & 1));
     if (span_has_ragged(s, a.w, a.w_end)) {
       if (warp == 0) copy_ragged(buf, s, a.w, a.w_end, lane);
       __syncthreads();
     }
+    const int r0 = r_begin + i * TILE;
+    const int nr = (int)((s.g1 - s.g0) / a.rb);
+    float* rd = red + (i & 1) * (W * TILE * NT);
     if (ok) {
-      const int r0 = r_begin + i * a.tile_rows;
-      const int nr = (int)((s.g1 - s.g0) / a.rb);
       const uint8_t* base = buf + (reinterpret_cast<uintptr_t>(s.g0) & 15);
-      for (int rr = warp * R; rr < nr; rr += (kGemvThreads / 32) * R) {
-        const uint8_t* rows[R];
-        const int nrows = min(R, nr - rr);
+      // this subset's rows sub, sub + RS, ..; those at or past nr repeat row nr - 1 and are dropped
+      const uint8_t* rows[R];
 #pragma unroll
-        for (int r = 0; r < R; ++r) rows[r] = base + (int64_t)(rr + min(r, nrows - 1)) * a.rb;
-        float acc[R][NT];
+      for (int r = 0; r < R; ++r) rows[r] = base + (int64_t)min(sub + RS * r, nr - 1) * a.rb;
+      float acc[R][NT];
 #pragma unroll
-        for (int r = 0; r < R; ++r)
+      for (int r = 0; r < R; ++r)
 #pragma unroll
-          for (int t = 0; t < NT; ++t) acc[r][t] = 0.f;
-        int tok[NT];
+        for (int t = 0; t < NT; ++t) acc[r][t] = 0.f;
+      dot_rows<FMT, NT, R, kXG, true>(rows, R, ngroups, warp * LG + lg, xs, xt, tok, NT, acc, W * LG);
 #pragma unroll
-        for (int t = 0; t < NT; ++t) tok[t] = t;
-        dot_rows<FMT, NT, R, kXG>(rows, nrows, ngroups, lane, xs, xt, tok, T, acc);
+      for (int r = 0; r < R; ++r)
 #pragma unroll
-        for (int r = 0; r < R; ++r) {
+        for (int t = 0; t < NT; ++t) {
+          float v = acc[r][t];
 #pragma unroll
-          for (int t = 0; t < NT; ++t) {
-            float v = warp_sum(acc[r][t]);
-            if (lane == 0 && r < nrows && t < T)
-              store_float(a.y, a.y_dtype, (int64_t)t * a.y_stride + r0 + rr + r, v);
-          }
+          for (int o = 1; o < LG; o <<= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+          if (lg == 0) rd[(warp * TILE + sub + RS * r) * NT + t] = v;
         }
-      }
     }
-    __syncthreads();  // stage st fully consumed
-    if (tid == 0 && i + kGemvStages < n_tiles) issue(i + kGemvStages);
+    __syncthreads();  // stage st consumed, this tile's partial sums in rd
+    if (ok && tid < nr * T) {
+      const int row = tid / T, t = tid - row * T;
+      float v = 0.f;
+#pragma unroll
+      for (int w = 0; w < W; ++w) v += rd[(w * TILE + row) * NT + t];
+      store_float(a.y, a.y_dtype, (int64_t)t * a.y_stride + r0 + row, v);
+    }
+    if (tid == 0 && i + nst < n_tiles) issue(i + nst);
   }
 }
 
-template <int FMT, int NT, int R>
+template <int FMT, int NT, int TILE, int W, int RS>
 static int launch_gemv(const GemvArgs& a, int grid, size_t smem, cudaStream_t stream) {
-  auto kern = gemv_kernel<FMT, NT, R>;
+  auto kern = gemv_kernel<FMT, NT, TILE, W, RS>;
   NS_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-  kern<<<grid, kGemvThreads, smem, stream>>>(a);
+  kern<<<grid, W * 32, smem, stream>>>(a);
   NS_CUDA_TRY(cudaGetLastError());
   return NS_OK;
 }
 
 template <int FMT>
-static int dispatch_gemv_t(const GemvArgs& a, int grid, size_t smem, cudaStream_t stream) {
-  if (a.T == 1) return launch_gemv<FMT, 1, 4>(a, grid, smem, stream);
-  if (a.T == 2) return launch_gemv<FMT, 2, 4>(a, grid, smem, stream);
-  if (a.T <= 4) return launch_gemv<FMT, 4, 2>(a, grid, smem, stream);
-  return launch_gemv<FMT, 8, 2>(a, grid, smem, stream);
+static int dispatch_gemv_t(const GemvArgs& a, int tile, int grid, size_t smem, cudaStream_t stream) {
+  if (a.T == 1)
+    return tile == 16 ? launch_gemv<FMT, 1, 16, 16, 4>(a, grid, smem, stream) : launch_gemv<FMT, 1, 8, 16, 4>(a, grid, smem, stream);
+  if (a.T == 2) return launch_gemv<FMT, 2, 8, 8, 2>(a, grid, smem, stream);
+  if (a.T <= 4) return launch_gemv<FMT, 4, 8, 8, 2>(a, grid, smem, stream);
+  return launch_gemv<FMT, 8, 8, 8, 2>(a, grid, smem, stream);
 }
 
 }  // namespace ns
@@ -163,24 +182,26 @@ extern "C" int ns_gemv(const uint8_t* w, size_t w_bytes, int ggml_type, int n_ro
   int nsm = 0;
   int st = num_sms(&nsm);
   if (st) return st;
-  const size_t x_bytes = (size_t)T * (K / 32) * kXG * 4;
-  if (x_bytes + kGemvStages * (rb + 64) + 64 > (size_t)kSmemBudget)
-    return fail(NS_ERR_UNSUPPORTED, "ns_gemv: T*K=%d activations plus a %lld-byte row exceed shared memory",
-                T * K, (long long)rb);
-  int stage_bytes = (int)std::min<size_t>(48 * 1024, ((kSmemBudget - x_bytes - 64) / kGemvStages) & ~size_t(15));
-  int tr_max = (int)((stage_bytes - 64) / rb);
-  int per_cta = (n_rows + nsm - 1) / nsm;
-  int tile_rows = std::max(1, std::min(tr_max, per_cta));
-  int grid = std::min(nsm, (n_rows + tile_rows - 1) / tile_rows);
-  size_t smem = x_bytes + (size_t)kGemvStages * stage_bytes + kGemvStages * 8;
+  // tiles of 16 rows for one token when they fit a stage of <= 48 KB, else 8
+  const int tile = (T == 1 && 16 * rb + 32 <= 48 * 1024) ? 16 : 8;
+  const int nt_slots = T == 1 ? 1 : T <= 2 ? 2 : T <= 4 ? 4 : 8;  // the kernel's NT
+  const size_t x_bytes = (size_t)nt_slots * (K / 32) * kXG * 4;
+  const size_t red_bytes = (size_t)2 * (T == 1 ? 16 : 8) * tile * nt_slots * 4;
+  const int stage_bytes = (int)((tile * rb + 32 + 15) & ~int64_t(15));
+  const size_t fixed = x_bytes + red_bytes + 128 + kGemvMaxStages * 8;
+  const int stages = (int)std::min<size_t>(kGemvMaxStages, fixed < (size_t)kSmemBudget ? (kSmemBudget - fixed) / stage_bytes : 0);
+  if (stages < 2)
+    return fail(NS_ERR_UNSUPPORTED, "ns_gemv: T*K=%d activations plus two %d-row tiles of %lld-byte rows exceed shared memory",
+                T * K, tile, (long long)rb);
+  const int grid = std::min(nsm, n_rows);
+  const size_t smem = fixed + (size_t)stages * stage_bytes;
 
-  GemvArgs a{w, w + w_bytes, n_rows, K, (int)rb, T, x, x_dtype, x_stride, y, y_dtype, y_stride, tile_rows,
-             stage_bytes};
+  GemvArgs a{w, w + w_bytes, n_rows, K, (int)rb, T, x, x_dtype, x_stride, y, y_dtype, y_stride, stages, stage_bytes};
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   switch (ggml_type) {
-    case NS_GGML_MXFP4: return dispatch_gemv_t<NS_GGML_MXFP4>(a, grid, smem, s);
-    case NS_GGML_Q8_0: return dispatch_gemv_t<NS_GGML_Q8_0>(a, grid, smem, s);
-    case NS_GGML_Q4_K: return dispatch_gemv_t<NS_GGML_Q4_K>(a, grid, smem, s);
-    default: return dispatch_gemv_t<NS_GGML_Q6_K>(a, grid, smem, s);
+    case NS_GGML_MXFP4: return dispatch_gemv_t<NS_GGML_MXFP4>(a, tile, grid, smem, s);
+    case NS_GGML_Q8_0: return dispatch_gemv_t<NS_GGML_Q8_0>(a, tile, grid, smem, s);
+    case NS_GGML_Q4_K: return dispatch_gemv_t<NS_GGML_Q4_K>(a, tile, grid, smem, s);
+    default: return dispatch_gemv_t<NS_GGML_Q6_K>(a, tile, grid, smem, s);
   }
 }

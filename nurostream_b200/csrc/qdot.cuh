@@ -257,12 +257,16 @@ struct QGroup<NS_GGML_Q6_K> {
 // x: generic pointer; token t's activations are the row x + tok[t]*xs (floats,
 // 16-byte aligned rows), group g of it at + XG*g, for t < nt <= NT.  In shared
 // memory XG = 36 keeps the lanes (one group each) on distinct banks.
-template <int FMT, int NT, int R, int XG = 32>
-__device__ __forceinline__ void dot_rows(const uint8_t* const (&rows)[R], int nrows, int ngroups, int lane,
-                                         const float* x, int64_t xs, const int (&tok)[NT], int nt,
-                                         float (&acc)[R][NT]) {
+// Groups g0, g0 + gstep, .. (gstep = 32: one lane per group of the row).  ALL: every one of the
+// R rows and NT tokens is valid (no per-element tests); otherwise rows >= nrows and tokens >= nt
+// are skipped.
+template <int FMT, int NT, int R, int XG = 32, bool ALL = false>
+__device__ __forceinline__ void dot_rows(const uint8_t* const (&rows)[R], int nrows_, int ngroups, int g0,
+                                         const float* x, int64_t xs, const int (&tok)[NT], int nt_,
+                                         float (&acc)[R][NT], int gstep = 32) {
   using G = QGroup<FMT>;
-  for (int g = lane; g < ngroups; g += 32) {
+  const int nrows = ALL ? R : nrows_, nt = ALL ? NT : nt_;
+  for (int g = g0; g < ngroups; g += gstep) {
     G q[R];
 #pragma unroll
     for (int r = 0; r < R; ++r)
