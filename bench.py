@@ -7,11 +7,14 @@ bytes per step (1.9 GB) are far larger than L2 (126 MB), so no flush is needed.
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
   python bench.py --workload gemv [--steps K] [--warmup W]
+  python bench.py --workload qwen3 [--layers L] [--steps K] [--warmup W]
 
 ``--workload gemv`` measures the dense dequant-GEMV sweep instead (batch 1,
 K = 4096, N in {4096, 11008, 14336}, MXFP4 / Q4_K / Q8_0): one JSON line per
 case, HBM GB/s against the measured copy peak, weight copies rotated so that
-every launch streams from HBM.
+every launch streams from HBM.  ``--workload qwen3`` runs the decode step on
+the Qwen3-235B-A22B shape instead (94 MoE layers, hidden 4096, 128 experts,
+top-8, expert ffn 1536, Q4_K experts; MoE layers only).
 
 N > 1 runs expert parallel under torchrun (experts split by index, one NCCL
 all-reduce per layer).  ``--impl reference`` times the reference's CPU path
@@ -42,6 +45,17 @@ KERNEL = "moe_tc_kernel"
 
 
 def workload_config(shape, world):
+    if shape.arch == "qwen3":
+        return {
+            "workload": (f"qwen3-235b-a22b-shape MoE decode path: {shape.n_layer} layers x (router softmax "
+                         f"top-{shape.top_k}/{shape.n_expert} renormalised + Q4_K gate/up/down "
+                         f"{shape.hidden}x{shape.expert_ffn} + silu*up + weighted combine + residual), batch 1"),
+            "layers": shape.n_layer, "experts": shape.n_expert, "top_k": shape.top_k, "hidden": shape.hidden,
+            "expert_ffn": shape.expert_ffn, "expert_format": "Q4_K (GGUF bytes, HBM-resident)",
+            "router": "bf16 weight, no bias", "global_batch": 1, "seq_len": 1,
+            "parallelism": f"ep{world}" if world > 1 else "single",
+            "l2": "inputs larger than L2 (expert bytes per step far above L2 126 MB)",
+        }
     return {
         "workload": (f"gpt-oss-120b-shape MoE decode path: {shape.n_layer} layers x (RMSNorm + router "
                      f"top-{shape.top_k}/{shape.n_expert} + MXFP4 gate/up/down {shape.hidden}x{shape.expert_ffn} "
@@ -198,16 +212,27 @@ def measured_peaks():
     return 6650.0, "fallback"
 
 
+def bench_shape(args):
+    from nurostream_b200.decoder import MoeShape
+    from nurostream_b200.ggml import GGMLType
+
+    if args.workload == "qwen3":
+        return MoeShape(n_layer=args.layers, hidden=4096, expert_ffn=1536, n_expert=128, top_k=8,
+                        ggml_type=int(GGMLType.Q4_K), arch="qwen3")
+    return MoeShape(n_layer=args.layers)
+
+
 def run_ours(args, rank, world, local_rank, group):
     import torch
     import torch.distributed as dist
 
     from nurostream_b200 import _lib, synth
     from nurostream_b200.decoder import MoeDecoder, MoeShape
+    from nurostream_b200.ggml import GGMLType
 
     dev = torch.device("cuda", local_rank)
     torch.cuda.set_device(dev)
-    shape = MoeShape(n_layer=args.layers)
+    shape = bench_shape(args)
     dec = MoeDecoder(shape, dev, rank, world, group, use_graph=not args.no_graph)
     H = shape.hidden
     npool = 64
@@ -273,9 +298,11 @@ def run_ours(args, rank, world, local_rank, group):
     per_launch_s = step_ms / 1000.0 / shape.n_layer
     achieved = bytes_layer / per_launch_s / 1e9 if world == 1 else bytes_layer / per_launch_s / 1e9
     line = {
-        "metric": METRIC, "value": round(tok_s, 2), "unit": UNIT, "n_gpus": world, "steps": args.steps,
+        "metric": METRIC if shape.arch == "gpt-oss" else "decode tok/s at batch 1 (Qwen3-235B-A22B shape, MoE layers)",
+        "value": round(tok_s, 2), "unit": UNIT, "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round(step_ms, 4), "higher_is_better": True,
-        "scaling": "strong", "vs_baseline": None, "dtype": "mxfp4 weights, fp32 accumulate",
+        "scaling": "strong", "vs_baseline": None,
+        "dtype": f"{GGMLType(shape.ggml_type).name.lower()} weights, fp32 accumulate",
         "data": "synthetic (seeded splitmix64 GGUF bytes generated in HBM)",
         "config": workload_config(shape, world),
         "e2e": {"value": round(1000.0 * args.steps / ms_e2e, 2), "unit": UNIT,
@@ -283,7 +310,8 @@ def run_ours(args, rank, world, local_rank, group):
         "gpu_launches": shape.n_layer * args.steps,
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                      "frac": round(achieved / (peak * (1 if world == 1 else world)), 4),
-                     "traffic": None, "peak_kind": peak_kind, "kernel": KERNEL,
+                     "traffic": None, "peak_kind": peak_kind,
+                     "kernel": KERNEL if shape.arch == "gpt-oss" else "moe_layer_kernel",
                      "algorithmic_bytes_per_launch": bytes_layer,
                      "launch_ms": round(per_launch_s * 1000, 5),
                      "launch_ms_from": "CUDA events over the timed region / layer launches in it (one kernel "
@@ -292,14 +320,14 @@ def run_ours(args, rank, world, local_rank, group):
         "routing_identical_on_all_ranks": ids_ok,
     }
     traffic = ROOT / "profiles" / "moe_tc_kernel_traffic.json"
-    if traffic.exists():
+    if traffic.exists() and shape.arch == "gpt-oss":
         try:
             line["roofline"]["traffic"] = json.loads(traffic.read_text()).get("dram_bytes_per_launch")
         except Exception:
             pass
     if clk:
         line["clocks"] = clk
-    if world == 1 and not args.no_cpu_baseline:
+    if world == 1 and not args.no_cpu_baseline and shape.arch == "gpt-oss":
         threads = cpu_cores()
         cpu_tok_s, per_layer, _ = cpu_layer_sample(shape, args.cpu_layers, threads)
         line["cpu_baseline"] = {
@@ -432,15 +460,17 @@ def main():
     ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--layers", type=int, default=36)
+    ap.add_argument("--layers", type=int, default=None, help="MoE layers (36 for decode, 94 for qwen3)")
     ap.add_argument("--cpu-layers", type=int, default=4)
     ap.add_argument("--ref-layers", type=int, default=2)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-graph", action="store_true")
-    ap.add_argument("--workload", choices=["decode", "gemv"], default="decode")
+    ap.add_argument("--workload", choices=["decode", "gemv", "qwen3"], default="decode")
     ap.add_argument("--gemv-case", default="", help="run one GEMV case only, e.g. MXFP4:14336")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
+    if args.layers is None:
+        args.layers = 94 if args.workload == "qwen3" else 36
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))

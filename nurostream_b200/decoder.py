@@ -35,6 +35,9 @@ class MoeShape:
     router_dtype: torch.dtype = torch.bfloat16
     seed: int = 0
     bias_sigma: float = 0.02
+    # "gpt-oss": RMSNorm, biased router, top-k then softmax, clamped SwiGLU, expert biases.
+    # "qwen3": no norm or biases, softmax then top-k renormalised, silu(gate) * up.
+    arch: str = "gpt-oss"
 
     @property
     def expert_bytes(self) -> int:
@@ -45,10 +48,11 @@ class MoeShape:
     def layer_bytes_per_token(self) -> int:
         """Algorithmic bytes one layer reads/writes for one token (the roofline numerator)."""
         H, F, E, k = self.hidden, self.expert_ffn, self.n_expert, self.top_k
-        router = E * H * (2 if self.router_dtype == torch.bfloat16 else 4) + 4 * E
+        gptoss = self.arch == "gpt-oss"
+        router = E * H * (2 if self.router_dtype == torch.bfloat16 else 4) + (4 * E if gptoss else 0)
         experts = k * self.expert_bytes
-        biases = k * 4 * (2 * F + H)
-        acts = 4 * H * 3        # x in, norm weight, out
+        biases = k * 4 * (2 * F + H) if gptoss else 0
+        acts = 4 * H * (3 if gptoss else 2)  # x in, norm weight (GPT-OSS), out
         return router + experts + biases + acts
 
 
@@ -96,6 +100,14 @@ class MoeDecoder:
             synth.fill_float(buf, sh.seed, stream, start, sigma)
             return buf
 
+        if sh.arch == "qwen3":
+            return MoeLayer(
+                H=H, F=F, n_expert=E, k=sh.top_k, ggml_type=t,
+                router_w=flt(E * H, s.router_w, 0.02, sh.router_dtype).reshape(E, H),
+                gate=quant(s.gate, F, H), up=quant(s.up, F, H), down=quant(s.down, H, F),
+                expert_lo=self.lo, expert_hi=self.hi, max_tokens=1,
+                route_mode=_lib.NS_ROUTE_SOFTMAX_TOPK_NORM, act_mode=_lib.NS_ACT_SILU_MUL,
+            )
         norm = flt(H, s.norm_w, 0.1) + 1.0
         return MoeLayer(
             H=H, F=F, n_expert=E, k=sh.top_k, ggml_type=t,
