@@ -212,6 +212,21 @@ __device__ __forceinline__ uint32_t issue_span(uint8_t* dst, Span s, const uint8
   return bytes;
 }
 
+// Same as issue_span, as bulk copies of at most `piece` bytes (a multiple of 16), all completing
+// on `bar`: several copies in flight instead of one long one.
+__device__ __forceinline__ uint32_t issue_span_pieces(uint8_t* dst, Span s, const uint8_t* buf0, const uint8_t* buf1,
+                                                      uint64_t* bar, uint32_t piece) {
+  uintptr_t lo, hi;
+  bulk_window(s, buf0, buf1, &lo, &hi);
+  if (hi <= lo) return 0;
+  uintptr_t base = floor16(reinterpret_cast<uintptr_t>(s.g0));
+  for (uintptr_t p = lo; p < hi; p += piece) {
+    const uint32_t n = (uint32_t)min((uintptr_t)piece, hi - p);
+    bulk_g2s(dst + (p - base), reinterpret_cast<const void*>(p), n, bar);
+  }
+  return (uint32_t)(hi - lo);
+}
+
 // Copy the bytes of span s that issue_span left out (at most 15 at each end),
 // with plain loads.  Called by a whole warp after the barrier completed.
 __device__ __forceinline__ void copy_ragged(uint8_t* dst, Span s, const uint8_t* buf0, const uint8_t* buf1,

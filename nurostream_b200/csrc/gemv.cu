@@ -8,6 +8,12 @@
 // shared memory, each 32-element group padded to kXG floats so that lanes
 // reading different groups hit different banks.
 //
+// Q8_0 and Q4_K take their weights as the int8 / 4-bit integers they are and
+// the activations as three int8 digit planes per 32-element group (an exact
+// 22-bit fixed point of the group, scale 2^(e-22) with max|x| < 2^e): the
+// group's dot product is three dp4a chains per weight word, combined in fp32
+// and scaled once.  MXFP4 and Q6_K decode to fp32 and use fp32 FMAs.
+//
 // Work split of a tile: the W warps take interleaved slices of K, and each
 // warp's lanes form RS row subsets of LG = 32/RS lanes: lane (s, j) takes
 // rows s, s + RS, .. of the tile and the groups w*LG + j, + W*LG, .. of K.  So
@@ -22,7 +28,74 @@ namespace ns {
 constexpr int kGemvMaxWarps = 16;
 constexpr int kGemvMaxStages = 6;
 constexpr int kSmemBudget = 220 * 1024;
-constexpr int kXG = 36;  // shared-memory floats per 32-element group of x
+constexpr int kXG = 36;     // shared-memory floats per 32-element group of x (fp32 path)
+constexpr int kXQG = 112;  // shared-memory bytes per 32-element group of x planes (integer path)
+
+template <int FMT>
+struct GemvInt8 {
+  static constexpr bool value = FMT == NS_GGML_Q8_0 || FMT == NS_GGML_Q4_K;
+};
+
+// Shared-memory bytes of the activations of NT token slots (K elements each).
+__host__ __device__ inline size_t gemv_x_bytes(bool int8, int nt, int K) {
+  const size_t ng = (size_t)K / 32;
+  return int8 ? (size_t)nt * ng * (kXQG + 8) : (size_t)nt * ng * kXG * 4;
+}
+
+// Integer-path dot products: rows[r] (shared memory) against token slots t of the activation
+// planes xq (plane p of group g at xq + t*xqs + g*kXQG + 32p), with per-group scales xsc and
+// sums xsum (at t*ng + g).
+template <int FMT, int NT, int R>
+__device__ __forceinline__ void dot_rows_i8(const uint8_t* const (&rows)[R], int ngroups, int g0, int gstep,
+                                            const uint8_t* xq, int xqs, const float* xsc, const float* xsum,
+                                            float (&acc)[R][NT]) {
+  for (int g = g0; g < ngroups; g += gstep) {
+    uint32_t q[R][8];
+    float da[R], db[R];  // Q8_0: d, 0; Q4_K: d*sc, dmin*mn
+#pragma unroll
+    for (int r = 0; r < R; ++r) {
+      if (FMT == NS_GGML_Q8_0) {
+        uint32_t w[9];
+        lds_words_unaligned<9>(rows[r] + 34 * g, w);
+        da[r] = f16_bits_to_float(w[0]);
+        db[r] = 0.f;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) q[r][i] = __funnelshift_r(w[i], w[i + 1], 16);  // signed int8 x 4
+      } else {
+        QGroup<NS_GGML_Q4_K> qg;
+        qg.load(rows[r], g);
+        da[r] = qg.dsc;
+        db[r] = qg.mmn;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) q[r][i] = qg.q[i];  // 0..15 x 4
+      }
+    }
+#pragma unroll
+    for (int t = 0; t < NT; ++t) {
+      const uint4* xp = reinterpret_cast<const uint4*>(xq + (size_t)t * xqs + (size_t)g * kXQG);
+      uint32_t xw[3][8];
+#pragma unroll
+      for (int p = 0; p < 3; ++p) {
+        const uint4 lo = xp[2 * p], hi = xp[2 * p + 1];
+        xw[p][0] = lo.x; xw[p][1] = lo.y; xw[p][2] = lo.z; xw[p][3] = lo.w;
+        xw[p][4] = hi.x; xw[p][5] = hi.y; xw[p][6] = hi.z; xw[p][7] = hi.w;
+      }
+      const float sc = xsc[t * ngroups + g], sm = xsum[t * ngroups + g];
+#pragma unroll
+      for (int r = 0; r < R; ++r) {
+        int s0 = 0, s1 = 0, s2 = 0;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          s0 = __dp4a((int)q[r][i], (int)xw[0][i], s0);
+          s1 = __dp4a((int)q[r][i], (int)xw[1][i], s1);
+          s2 = __dp4a((int)q[r][i], (int)xw[2][i], s2);
+        }
+        const float f = fmaf((float)s2, 65536.f, fmaf((float)s1, 256.f, (float)s0)) * sc;
+        acc[r][t] = fmaf(f, da[r], FMT == NS_GGML_Q4_K ? fmaf(-db[r], sm, acc[r][t]) : acc[r][t]);
+      }
+    }
+  }
+}
 
 struct GemvArgs {
   const uint8_t* w;
@@ -43,9 +116,15 @@ __global__ void __launch_bounds__(W * 32, 1) gemv_kernel(GemvArgs a) {
   constexpr int kThreads = W * 32, LG = 32 / RS, R = TILE / RS;  // lanes per row subset, rows per lane
   extern __shared__ __align__(128) uint8_t smem[];
   const int K = a.K, T = a.T, nst = a.stages;
-  float* xs = reinterpret_cast<float*>(smem);
-  const int xt = (K / 32) * kXG;  // floats per token
-  float* red = xs + NT * xt;      // 2 x [warp][row][token] partial sums
+  constexpr bool kInt = GemvInt8<FMT>::value;
+  const int ngroups = K / 32;
+  float* xs = reinterpret_cast<float*>(smem);               // fp32 path: padded groups
+  const int xt = ngroups * kXG;                             // floats per token
+  uint8_t* xq = smem;                                       // integer path: digit planes
+  const int xqs = ngroups * kXQG;                           // bytes per token
+  float* xsc = reinterpret_cast<float*>(smem + (size_t)NT * xqs);  // [token][group] scale 2^(e-22)
+  float* xsum = xsc + NT * ngroups;                         // [token][group] sum of x
+  float* red = reinterpret_cast<float*>(smem + gemv_x_bytes(kInt, NT, K));  // 2 x [warp][row][token]
   uint8_t* stages = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(red + 2 * W * TILE * NT) + 127) & ~uintptr_t(127));
   uint64_t* bars = reinterpret_cast<uint64_t*>(stages + nst * a.stage_bytes);
@@ -68,7 +147,7 @@ __global__ void __launch_bounds__(W * 32, 1) gemv_kernel(GemvArgs a) {
     uintptr_t lo, hi;
     bulk_window(s, a.w, a.w_end, &lo, &hi);
     mbar_arrive_expect_tx(bar, hi > lo ? (uint32_t)(hi - lo) : 0u);
-    issue_span(stages + (i % nst) * a.stage_bytes, s, a.w, a.w_end, bar);
+    issue_span_pieces(stages + (i % nst) * a.stage_bytes, s, a.w, a.w_end, bar, 4096u);
   };
 
   if (tid == 0) {
@@ -76,15 +155,44 @@ __global__ void __launch_bounds__(W * 32, 1) gemv_kernel(GemvArgs a) {
     fence_mbar_init();
     for (int i = 0; i < nst && i < n_tiles; ++i) issue(i);
   }
-  // activations -> padded fp32 shared memory (overlaps with the first copies); token slots T..NT-1
-  // hold zeros, so every lane computes all NT slots without tests
-  for (int i = tid; i < NT * K; i += kThreads) {
-    int t = i / K, k = i - t * K;
-    xs[t * xt + (k >> 5) * kXG + (k & 31)] = t < T ? load_float(a.x, a.x_dtype, (int64_t)t * a.x_stride + k) : 0.f;
+  // activations -> shared memory (overlaps with the first copies); token slots T..NT-1 hold zeros,
+  // so every lane computes all NT slots without tests
+  if (kInt) {
+    // one warp per (token, group): element j in lane j; balanced radix-256 digits of
+    // X = rint(x * 2^(22-e)), |X| <= 2^22, so every digit fits int8
+    for (int it = warp; it < NT * ngroups; it += W) {
+      const int t = it / ngroups, g = it - t * ngroups;
+      const float v = t < T ? load_float(a.x, a.x_dtype, (int64_t)t * a.x_stride + 32 * g + lane) : 0.f;
+      float m = fabsf(v);
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+      // max|x| < 2^e with e = be - 126; groups below 2^-104 (and non-finite ones) are taken as zeros
+      const int be = (int)((__float_as_uint(m) >> 23) & 255u);
+      const bool live = be >= 22 && be < 255;
+      int X = 0;
+      if (live) X = __float2int_rn(v * __uint_as_float((uint32_t)(275 - be) << 23));  // v * 2^(22-e)
+      const int d0 = ((X + 128) & 255) - 128;
+      const int X1 = (X - d0) >> 8;
+      const int d1 = ((X1 + 128) & 255) - 128;
+      const int d2 = (X1 - d1) >> 8;
+      uint8_t* dst = xq + (size_t)t * xqs + (size_t)g * kXQG + lane;
+      dst[0] = (uint8_t)d0;
+      dst[32] = (uint8_t)d1;
+      dst[64] = (uint8_t)d2;
+      const float sum = warp_sum(v);
+      if (lane == 0) {
+        xsc[t * ngroups + g] = live ? __uint_as_float((uint32_t)(be - 21) << 23) : 0.f;  // 2^(e-22)
+        xsum[t * ngroups + g] = sum;
+      }
+    }
+  } else {
+    for (int i = tid; i < NT * K; i += kThreads) {
+      int t = i / K, k = i - t * K;
+      xs[t * xt + (k >> 5) * kXG + (k & 31)] = t < T ? load_float(a.x, a.x_dtype, (int64_t)t * a.x_stride + k) : 0.f;
+    }
   }
   __syncthreads();
 
-  const int ngroups = K / 32;
   const int sub = lane / LG, lg = lane % LG;
   int tok[NT];
 #pragma unroll
@@ -112,7 +220,10 @@ __global__ void __launch_bounds__(W * 32, 1) gemv_kernel(GemvArgs a) {
       for (int r = 0; r < R; ++r)
 #pragma unroll
         for (int t = 0; t < NT; ++t) acc[r][t] = 0.f;
-      dot_rows<FMT, NT, R, kXG, true>(rows, R, ngroups, warp * LG + lg, xs, xt, tok, NT, acc, W * LG);
+      if constexpr (kInt)
+        dot_rows_i8<FMT, NT, R>(rows, ngroups, warp * LG + lg, W * LG, xq, xqs, xsc, xsum, acc);
+      else
+        dot_rows<FMT, NT, R, kXG, true>(rows, R, ngroups, warp * LG + lg, xs, xt, tok, NT, acc, W * LG);
 #pragma unroll
       for (int r = 0; r < R; ++r)
 #pragma unroll
@@ -185,7 +296,8 @@ extern "C" int ns_gemv(const uint8_t* w, size_t w_bytes, int ggml_type, int n_ro
   // tiles of 16 rows for one token when they fit a stage of <= 48 KB, else 8
   const int tile = (T == 1 && 16 * rb + 32 <= 48 * 1024) ? 16 : 8;
   const int nt_slots = T == 1 ? 1 : T <= 2 ? 2 : T <= 4 ? 4 : 8;  // the kernel's NT
-  const size_t x_bytes = (size_t)nt_slots * (K / 32) * kXG * 4;
+  const bool int8_path = ggml_type == NS_GGML_Q8_0 || ggml_type == NS_GGML_Q4_K;
+  const size_t x_bytes = gemv_x_bytes(int8_path, nt_slots, K);
   const size_t red_bytes = (size_t)2 * (T == 1 ? 16 : 8) * tile * nt_slots * 4;
   const int stage_bytes = (int)((tile * rb + 32 + 15) & ~int64_t(15));
   const size_t fixed = x_bytes + red_bytes + 128 + kGemvMaxStages * 8;
