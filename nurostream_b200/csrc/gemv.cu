@@ -109,6 +109,7 @@ struct GemvArgs {
   int64_t y_stride;
   int stages;
   int stage_bytes;
+  int pitch;  // shared-memory bytes per staged row: rb, or rb padded against bank conflicts (row copies)
 };
 
 template <int FMT, int NT, int TILE, int W, int RS>
@@ -141,13 +142,21 @@ __global__ void __launch_bounds__(W * 32, 1) gemv_kernel(GemvArgs a) {
     int r1 = min(r0 + TILE, r_end);
     return Span{a.w + (int64_t)r0 * a.rb, a.w + (int64_t)r1 * a.rb};
   };
+  const bool row_copies = a.pitch != a.rb;  // rows 16-byte aligned: one copy per row into padded slots
   auto issue = [&](int i) {
     uint64_t* bar = &bars[i % nst];
+    uint8_t* dst = stages + (i % nst) * a.stage_bytes;
     Span s = tile_span(i);
+    if (row_copies) {
+      const int nr = (int)((s.g1 - s.g0) / a.rb);
+      mbar_arrive_expect_tx(bar, (uint32_t)(nr * a.rb));
+      for (int r = 0; r < nr; ++r) bulk_g2s(dst + r * a.pitch, s.g0 + (int64_t)r * a.rb, (uint32_t)a.rb, bar);
+      return;
+    }
     uintptr_t lo, hi;
     bulk_window(s, a.w, a.w_end, &lo, &hi);
     mbar_arrive_expect_tx(bar, hi > lo ? (uint32_t)(hi - lo) : 0u);
-    issue_span_pieces(stages + (i % nst) * a.stage_bytes, s, a.w, a.w_end, bar, 4096u);
+    issue_span_pieces(dst, s, a.w, a.w_end, bar, 4096u);
   };
 
   if (tid == 0) {
@@ -160,35 +169,57 @@ __global__ void __launch_bounds__(W * 32, 1) gemv_kernel(GemvArgs a) {
   if (kInt) {
     // one warp per (token, group): element j in lane j; balanced radix-256 digits of
     // X = rint(x * 2^(22-e)), |X| <= 2^22, so every digit fits int8
-    for (int it = warp; it < NT * ngroups; it += W) {
-      const int t = it / ngroups, g = it - t * ngroups;
-      const float v = t < T ? load_float(a.x, a.x_dtype, (int64_t)t * a.x_stride + 32 * g + lane) : 0.f;
-      float m = fabsf(v);
+    constexpr int kB = 8;  // (token, group) items per warp whose loads are issued together
+    for (int it0 = warp; it0 < NT * ngroups; it0 += kB * W) {
+      float vb[kB];
 #pragma unroll
-      for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-      // max|x| < 2^e with e = be - 126; groups below 2^-104 (and non-finite ones) are taken as zeros
-      const int be = (int)((__float_as_uint(m) >> 23) & 255u);
-      const bool live = be >= 22 && be < 255;
-      int X = 0;
-      if (live) X = __float2int_rn(v * __uint_as_float((uint32_t)(275 - be) << 23));  // v * 2^(22-e)
-      const int d0 = ((X + 128) & 255) - 128;
-      const int X1 = (X - d0) >> 8;
-      const int d1 = ((X1 + 128) & 255) - 128;
-      const int d2 = (X1 - d1) >> 8;
-      uint8_t* dst = xq + (size_t)t * xqs + (size_t)g * kXQG + lane;
-      dst[0] = (uint8_t)d0;
-      dst[32] = (uint8_t)d1;
-      dst[64] = (uint8_t)d2;
-      const float sum = warp_sum(v);
-      if (lane == 0) {
-        xsc[t * ngroups + g] = live ? __uint_as_float((uint32_t)(be - 21) << 23) : 0.f;  // 2^(e-22)
-        xsum[t * ngroups + g] = sum;
+      for (int b = 0; b < kB; ++b) {
+        const int it = it0 + b * W, t = it / ngroups, g = it - t * ngroups;
+        vb[b] = it < NT * ngroups && t < T ? load_float(a.x, a.x_dtype, (int64_t)t * a.x_stride + 32 * g + lane) : 0.f;
+      }
+#pragma unroll
+      for (int b = 0; b < kB; ++b) {
+        const int it = it0 + b * W;
+        if (it >= NT * ngroups) break;
+        const int t = it / ngroups, g = it - t * ngroups;
+        const float v = vb[b];
+        float m = fabsf(v);
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+        // max|x| < 2^e with e = be - 126; groups below 2^-104 (and non-finite ones) are taken as zeros
+        const int be = (int)((__float_as_uint(m) >> 23) & 255u);
+        const bool live = be >= 22 && be < 255;
+        int X = 0;
+        if (live) X = __float2int_rn(v * __uint_as_float((uint32_t)(275 - be) << 23));  // v * 2^(22-e)
+        const int d0 = ((X + 128) & 255) - 128;
+        const int X1 = (X - d0) >> 8;
+        const int d1 = ((X1 + 128) & 255) - 128;
+        const int d2 = (X1 - d1) >> 8;
+        uint8_t* dst = xq + (size_t)t * xqs + (size_t)g * kXQG + lane;
+        dst[0] = (uint8_t)d0;
+        dst[32] = (uint8_t)d1;
+        dst[64] = (uint8_t)d2;
+        const float sum = warp_sum(v);
+        if (lane == 0) {
+          xsc[t * ngroups + g] = live ? __uint_as_float((uint32_t)(be - 21) << 23) : 0.f;  // 2^(e-22)
+          xsum[t * ngroups + g] = sum;
+        }
       }
     }
   } else {
-    for (int i = tid; i < NT * K; i += kThreads) {
-      int t = i / K, k = i - t * K;
-      xs[t * xt + (k >> 5) * kXG + (k & 31)] = t < T ? load_float(a.x, a.x_dtype, (int64_t)t * a.x_stride + k) : 0.f;
+    constexpr int kB = 8;  // elements per thread whose loads are issued together
+    for (int i0 = tid; i0 < NT * K; i0 += kB * kThreads) {
+      float vb[kB];
+#pragma unroll
+      for (int b = 0; b < kB; ++b) {
+        const int i = i0 + b * kThreads, t = i / K, k = i - t * K;
+        vb[b] = i < NT * K && t < T ? load_float(a.x, a.x_dtype, (int64_t)t * a.x_stride + k) : 0.f;
+      }
+#pragma unroll
+      for (int b = 0; b < kB; ++b) {
+        const int i = i0 + b * kThreads, t = i / K, k = i - t * K;
+        if (i < NT * K) xs[t * xt + (k >> 5) * kXG + (k & 31)] = vb[b];
+      }
     }
   }
   __syncthreads();
@@ -202,7 +233,7 @@ __global__ void __launch_bounds__(W * 32, 1) gemv_kernel(GemvArgs a) {
     uint8_t* buf = stages + st * a.stage_bytes;
     const Span s = tile_span(i);
     bool ok = mbar_wait_bounded(&bars[st], (uint32_t)((i / nst) & 1));
-    if (span_has_ragged(s, a.w, a.w_end)) {
+    if (!row_copies && span_has_ragged(s, a.w, a.w_end)) {
       if (warp == 0) copy_ragged(buf, s, a.w, a.w_end, lane);
       __syncthreads();
     }
@@ -210,11 +241,11 @@ __global__ void __launch_bounds__(W * 32, 1) gemv_kernel(GemvArgs a) {
     const int nr = (int)((s.g1 - s.g0) / a.rb);
     float* rd = red + (i & 1) * (W * TILE * NT);
     if (ok) {
-      const uint8_t* base = buf + (reinterpret_cast<uintptr_t>(s.g0) & 15);
+      const uint8_t* base = row_copies ? buf : buf + (reinterpret_cast<uintptr_t>(s.g0) & 15);
       // this subset's rows sub, sub + RS, ..; those at or past nr repeat row nr - 1 and are dropped
       const uint8_t* rows[R];
 #pragma unroll
-      for (int r = 0; r < R; ++r) rows[r] = base + (int64_t)min(sub + RS * r, nr - 1) * a.rb;
+      for (int r = 0; r < R; ++r) rows[r] = base + (int64_t)min(sub + RS * r, nr - 1) * a.pitch;
       float acc[R][NT];
 #pragma unroll
       for (int r = 0; r < R; ++r)
@@ -299,7 +330,15 @@ extern "C" int ns_gemv(const uint8_t* w, size_t w_bytes, int ggml_type, int n_ro
   const bool int8_path = ggml_type == NS_GGML_Q8_0 || ggml_type == NS_GGML_Q4_K;
   const size_t x_bytes = gemv_x_bytes(int8_path, nt_slots, K);
   const size_t red_bytes = (size_t)2 * (T == 1 ? 16 : 8) * tile * nt_slots * 4;
-  const int stage_bytes = (int)((tile * rb + 32 + 15) & ~int64_t(15));
+  // Rows that start on 16-byte boundaries are copied one by one into slots whose pitch is rb
+  // rounded up to a residue mod 128 B at which the lanes of a warp, reading blocks g.. of
+  // rows sub, sub + RS, .., spread over the 32 banks (at most 2-way conflicts, against 4-way
+  // when rb is a multiple of 128); other rows are copied as one span.
+  const int rs = T == 1 ? 4 : 2;
+  const int residue = rs == 2 ? 64 : ggml_type == NS_GGML_MXFP4 ? 32 : 48;
+  const bool rows_aligned = rb % 16 == 0 && reinterpret_cast<uintptr_t>(w) % 16 == 0;
+  const int pitch = rows_aligned ? (int)(rb + ((residue - rb % 128) + 128) % 128) : (int)rb;
+  const int stage_bytes = rows_aligned ? tile * pitch : (int)((tile * rb + 32 + 15) & ~int64_t(15));
   const size_t fixed = x_bytes + red_bytes + 128 + kGemvMaxStages * 8;
   const int stages = (int)std::min<size_t>(kGemvMaxStages, fixed < (size_t)kSmemBudget ? (kSmemBudget - fixed) / stage_bytes : 0);
   if (stages < 2)
@@ -308,7 +347,7 @@ extern "C" int ns_gemv(const uint8_t* w, size_t w_bytes, int ggml_type, int n_ro
   const int grid = std::min(nsm, n_rows);
   const size_t smem = fixed + (size_t)stages * stage_bytes;
 
-  GemvArgs a{w, w + w_bytes, n_rows, K, (int)rb, T, x, x_dtype, x_stride, y, y_dtype, y_stride, stages, stage_bytes};
+  GemvArgs a{w, w + w_bytes, n_rows, K, (int)rb, T, x, x_dtype, x_stride, y, y_dtype, y_stride, stages, stage_bytes, pitch};
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   switch (ggml_type) {
     case NS_GGML_MXFP4: return dispatch_gemv_t<NS_GGML_MXFP4>(a, tile, grid, smem, s);
