@@ -15,10 +15,12 @@
 // and scaled once.  MXFP4 and Q6_K decode to fp32 and use fp32 FMAs.
 //
 // Work split of a tile: the W warps take interleaved slices of K, and each
-// warp's lanes form RS row subsets of LG = 32/RS lanes: lane (s, j) takes
-// rows s, s + RS, .. of the tile and the groups w*LG + j, + W*LG, .. of K.  So
-// every lane runs TILE/RS independent row sums and loads each activation
-// group once for all of them.  Lane sums meet by shuffles within each subset,
+// warp's lanes form RS row subsets of LG = 32/RS lanes: lane (s, j) takes the
+// R = TILE/RS rows sR .. sR + R - 1 of the tile and the groups w*LG + j,
+// + W*LG, .. of K.  So every lane runs R independent row sums and loads each
+// activation group once for all of them.  The rows of a subset are one
+// "piece" of the stage: when rows start on 16-byte boundaries each piece is
+// one bulk copy into a slot whose pitch keeps the subsets on different banks.  Lane sums meet by shuffles within each subset,
 // then across the W warps in shared memory, in a fixed order.  One token:
 // 16 warps x 4 subsets (4 rows a lane); more tokens: 8 warps x 2 subsets.
 #include "qdot.cuh"
@@ -27,6 +29,7 @@ namespace ns {
 
 constexpr int kGemvMaxWarps = 16;
 constexpr int kGemvMaxStages = 6;
+constexpr int kGemvEarlyTiles = 1;  // tiles requested before the activations are staged
 constexpr int kSmemBudget = 220 * 1024;
 constexpr int kXG = 36;     // shared-memory floats per 32-element group of x (fp32 path)
 constexpr int kXQG = 112;  // shared-memory bytes per 32-element group of x planes (integer path)
@@ -109,12 +112,14 @@ struct GemvArgs {
   int64_t y_stride;
   int stages;
   int stage_bytes;
-  int pitch;  // shared-memory bytes per staged row: rb, or rb padded against bank conflicts (row copies)
+  int pitch;  // shared-memory bytes between pieces of R rows: R*rb, or more (padded piece copies)
 };
 
 template <int FMT, int NT, int TILE, int W, int RS>
-__global__ void __launch_bounds__(W * 32, 1) gemv_kernel(GemvArgs a) {
+__global__ void __launch_bounds__((W + 1) * 32, 1) gemv_kernel(GemvArgs a) {
+  // W compute warps (kThreads threads) and one producer warp, warp W
   constexpr int kThreads = W * 32, LG = 32 / RS, R = TILE / RS;  // lanes per row subset, rows per lane
+  static_assert(32 % W == 0 && (TILE * NT) % (32 / W) == 0, "final reduce: whole warps per pass");
   extern __shared__ __align__(128) uint8_t smem[];
   const int K = a.K, T = a.T, nst = a.stages;
   constexpr bool kInt = GemvInt8<FMT>::value;
@@ -128,7 +133,8 @@ __global__ void __launch_bounds__(W * 32, 1) gemv_kernel(GemvArgs a) {
   float* red = reinterpret_cast<float*>(smem + gemv_x_bytes(kInt, NT, K));  // 2 x [warp][row][token]
   uint8_t* stages = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(red + 2 * W * TILE * NT) + 127) & ~uintptr_t(127));
-  uint64_t* bars = reinterpret_cast<uint64_t*>(stages + nst * a.stage_bytes);
+  uint64_t* full = reinterpret_cast<uint64_t*>(stages + nst * a.stage_bytes);  // stage landed
+  uint64_t* empty = full + nst;                                                 // stage consumed
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
 
@@ -142,15 +148,16 @@ __global__ void __launch_bounds__(W * 32, 1) gemv_kernel(GemvArgs a) {
     int r1 = min(r0 + TILE, r_end);
     return Span{a.w + (int64_t)r0 * a.rb, a.w + (int64_t)r1 * a.rb};
   };
-  const bool row_copies = a.pitch != a.rb;  // rows 16-byte aligned: one copy per row into padded slots
+  const bool row_copies = a.pitch != R * a.rb;  // rows 16-byte aligned: one copy per piece, padded slots
   auto issue = [&](int i) {
-    uint64_t* bar = &bars[i % nst];
+    uint64_t* bar = &full[i % nst];
     uint8_t* dst = stages + (i % nst) * a.stage_bytes;
     Span s = tile_span(i);
     if (row_copies) {
       const int nr = (int)((s.g1 - s.g0) / a.rb);
       mbar_arrive_expect_tx(bar, (uint32_t)(nr * a.rb));
-      for (int r = 0; r < nr; ++r) bulk_g2s(dst + r * a.pitch, s.g0 + (int64_t)r * a.rb, (uint32_t)a.rb, bar);
+      for (int p = 0; p * R < nr; ++p)
+        bulk_g2s(dst + p * a.pitch, s.g0 + (int64_t)p * R * a.rb, (uint32_t)(min(R, nr - p * R) * a.rb), bar);
       return;
     }
     uintptr_t lo, hi;
@@ -159,10 +166,29 @@ __global__ void __launch_bounds__(W * 32, 1) gemv_kernel(GemvArgs a) {
     issue_span_pieces(dst, s, a.w, a.w_end, bar, 4096u);
   };
 
-  if (tid == 0) {
-    for (int s = 0; s < nst; ++s) mbar_init(&bars[s], 1);
-    fence_mbar_init();
-    for (int i = 0; i < nst && i < n_tiles; ++i) issue(i);
+
+  // The producer warp issues every copy: a bulk copy's issue blocks for a while once the SM's
+  // copy queue is busy, which would otherwise stall a compute warp.  The first stages go out
+  // before the activations are staged; the rest once x is in shared memory, since with every
+  // SM's whole ring in flight the activation loads queue behind the weight stream.
+  const int early = min(min(kGemvEarlyTiles, nst), n_tiles);
+  if (warp == W) {
+    if (lane == 0) {
+      for (int s = 0; s < nst; ++s) {
+        mbar_init(&full[s], 1);
+        mbar_init(&empty[s], 1);
+      }
+      fence_mbar_init();
+      for (int i = 0; i < early; ++i) issue(i);
+    }
+    __syncthreads();  // barriers initialised, x staged
+    if (lane == 0) {
+      for (int i = early; i < n_tiles; ++i) {
+        if (i >= nst && !mbar_wait_bounded(&empty[i % nst], (uint32_t)((i / nst - 1) & 1))) break;
+        issue(i);
+      }
+    }
+    return;
   }
   // activations -> shared memory (overlaps with the first copies); token slots T..NT-1 hold zeros,
   // so every lane computes all NT slots without tests
@@ -232,10 +258,10 @@ __global__ void __launch_bounds__(W * 32, 1) gemv_kernel(GemvArgs a) {
     const int st = i % nst;
     uint8_t* buf = stages + st * a.stage_bytes;
     const Span s = tile_span(i);
-    bool ok = mbar_wait_bounded(&bars[st], (uint32_t)((i / nst) & 1));
+    const bool ok = mbar_wait_bounded(&full[st], (uint32_t)((i / nst) & 1));
     if (!row_copies && span_has_ragged(s, a.w, a.w_end)) {
       if (warp == 0) copy_ragged(buf, s, a.w, a.w_end, lane);
-      __syncthreads();
+      named_sync(1, kThreads);
     }
     const int r0 = r_begin + i * TILE;
     const int nr = (int)((s.g1 - s.g0) / a.rb);
@@ -245,7 +271,10 @@ __global__ void __launch_bounds__(W * 32, 1) gemv_kernel(GemvArgs a) {
       // this subset's rows sub, sub + RS, ..; those at or past nr repeat row nr - 1 and are dropped
       const uint8_t* rows[R];
 #pragma unroll
-      for (int r = 0; r < R; ++r) rows[r] = base + (int64_t)min(sub + RS * r, nr - 1) * a.pitch;
+      for (int r = 0; r < R; ++r) {
+        const int q = min(sub * R + r, nr - 1);
+        rows[r] = base + (q / R) * a.pitch + (q % R) * a.rb;
+      }
       float acc[R][NT];
 #pragma unroll
       for (int r = 0; r < R; ++r)
@@ -262,18 +291,23 @@ __global__ void __launch_bounds__(W * 32, 1) gemv_kernel(GemvArgs a) {
           float v = acc[r][t];
 #pragma unroll
           for (int o = 1; o < LG; o <<= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-          if (lg == 0) rd[(warp * TILE + sub + RS * r) * NT + t] = v;
+          if (lg == 0) rd[(warp * TILE + sub * R + r) * NT + t] = v;
         }
     }
-    __syncthreads();  // stage st consumed, this tile's partial sums in rd
-    if (ok && tid < nr * T) {
-      const int row = tid / T, t = tid - row * T;
-      float v = 0.f;
+    named_sync(1, kThreads);  // stage st consumed, this tile's partial sums in rd
+    if (tid == 0) mbar_arrive(&empty[st]);
+    // the W warps' partials of each (row, token) meet in W consecutive lanes by shuffles, so no
+    // thread runs a long serial sum that would hold up the next tile
+    if (ok) {
+      const int w = tid % W;
+      for (int q = tid / W; q < TILE * NT; q += kThreads / W) {
+        const int row = q / NT, t = q - row * NT;
+        float v = rd[(w * TILE + row) * NT + t];
 #pragma unroll
-      for (int w = 0; w < W; ++w) v += rd[(w * TILE + row) * NT + t];
-      store_float(a.y, a.y_dtype, (int64_t)t * a.y_stride + r0 + row, v);
+        for (int o = 1; o < W; o <<= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+        if (w == 0 && row < nr && t < T) store_float(a.y, a.y_dtype, (int64_t)t * a.y_stride + r0 + row, v);
+      }
     }
-    if (tid == 0 && i + nst < n_tiles) issue(i + nst);
   }
 }
 
@@ -281,7 +315,7 @@ template <int FMT, int NT, int TILE, int W, int RS>
 static int launch_gemv(const GemvArgs& a, int grid, size_t smem, cudaStream_t stream) {
   auto kern = gemv_kernel<FMT, NT, TILE, W, RS>;
   NS_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-  kern<<<grid, W * 32, smem, stream>>>(a);
+  kern<<<grid, (W + 1) * 32, smem, stream>>>(a);
   NS_CUDA_TRY(cudaGetLastError());
   return NS_OK;
 }
@@ -330,16 +364,17 @@ extern "C" int ns_gemv(const uint8_t* w, size_t w_bytes, int ggml_type, int n_ro
   const bool int8_path = ggml_type == NS_GGML_Q8_0 || ggml_type == NS_GGML_Q4_K;
   const size_t x_bytes = gemv_x_bytes(int8_path, nt_slots, K);
   const size_t red_bytes = (size_t)2 * (T == 1 ? 16 : 8) * tile * nt_slots * 4;
-  // Rows that start on 16-byte boundaries are copied one by one into slots whose pitch is rb
-  // rounded up to a residue mod 128 B at which the lanes of a warp, reading blocks g.. of
-  // rows sub, sub + RS, .., spread over the 32 banks (at most 2-way conflicts, against 4-way
-  // when rb is a multiple of 128); other rows are copied as one span.
-  const int rs = T == 1 ? 4 : 2;
+  // When rows start on 16-byte boundaries, each piece of R rows is one bulk copy into a slot
+  // whose pitch is R*rb rounded up to a residue mod 128 B at which the lanes of a warp (subset
+  // s reading row sR + r, blocks g..) spread over the 32 banks: at most 2-way conflicts,
+  // against 4-way when rb is a multiple of 128.  Other rows are copied as one span.
+  const int rs = T == 1 ? 4 : 2, rpp = tile / rs;
   const int residue = rs == 2 ? 64 : ggml_type == NS_GGML_MXFP4 ? 32 : 48;
   const bool rows_aligned = rb % 16 == 0 && reinterpret_cast<uintptr_t>(w) % 16 == 0;
-  const int pitch = rows_aligned ? (int)(rb + ((residue - rb % 128) + 128) % 128) : (int)rb;
-  const int stage_bytes = rows_aligned ? tile * pitch : (int)((tile * rb + 32 + 15) & ~int64_t(15));
-  const size_t fixed = x_bytes + red_bytes + 128 + kGemvMaxStages * 8;
+  const int64_t pb = rpp * rb;
+  const int pitch = (int)(rows_aligned ? pb + ((residue - pb % 128) + 128) % 128 : pb);
+  const int stage_bytes = rows_aligned ? rs * pitch : (int)((tile * rb + 32 + 15) & ~int64_t(15));
+  const size_t fixed = x_bytes + red_bytes + 128 + 2 * kGemvMaxStages * 8;
   const int stages = (int)std::min<size_t>(kGemvMaxStages, fixed < (size_t)kSmemBudget ? (kSmemBudget - fixed) / stage_bytes : 0);
   if (stages < 2)
     return fail(NS_ERR_UNSUPPORTED, "ns_gemv: T*K=%d activations plus two %d-row tiles of %lld-byte rows exceed shared memory",

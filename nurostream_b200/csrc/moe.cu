@@ -229,14 +229,6 @@ __device__ __forceinline__ unsigned long long ld_acquire_u64(const unsigned long
   return v;
 }
 
-__device__ __forceinline__ void named_sync(int id, int nthreads) {
-  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
-}
-
-__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
-  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_addr(bar)) : "memory");
-}
-
 // Grid-wide barrier on a monotonically increasing 64-bit counter: barrier
 // instance n completes when the counter reaches (n+1)*G.  Bounded wait.
 // Called by thread 0 only; the caller synchronises its CTA around it.
