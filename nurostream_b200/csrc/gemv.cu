@@ -12,7 +12,9 @@
 // the activations as three int8 digit planes per 32-element group (an exact
 // 22-bit fixed point of the group, scale 2^(e-22) with max|x| < 2^e): the
 // group's dot product is three dp4a chains per weight word, combined in fp32
-// and scaled once.  MXFP4 and Q6_K decode to fp32 and use fp32 FMAs.
+// and scaled once.  MXFP4 and Q6_K decode to fp32 and use fp32 FMAs (an
+// MXFP4 variant on dp4a, with the e2m1 nibbles mapped to int8 by prmt table
+// lookups, measured slower: the decode costs as much as the conversions).
 //
 // Work split of a tile: the W warps take interleaved slices of K, and each
 // warp's lanes form RS row subsets of LG = 32/RS lanes: lane (s, j) takes the
@@ -193,43 +195,73 @@ __global__ void __launch_bounds__((W + 1) * 32, 1) gemv_kernel(GemvArgs a) {
   // activations -> shared memory (overlaps with the first copies); token slots T..NT-1 hold zeros,
   // so every lane computes all NT slots without tests
   if (kInt) {
-    // one warp per (token, group): element j in lane j; balanced radix-256 digits of
-    // X = rint(x * 2^(22-e)), |X| <= 2^22, so every digit fits int8
-    constexpr int kB = 8;  // (token, group) items per warp whose loads are issued together
-    for (int it0 = warp; it0 < NT * ngroups; it0 += kB * W) {
-      float vb[kB];
+    // one thread per (token, group): balanced radix-256 digits of X = rint(x * 2^(22-e)),
+    // |X| <= 2^22 with max|x| < 2^e, so every digit fits int8
+    const bool x_vec = a.x_dtype == NS_F32 && (reinterpret_cast<uintptr_t>(a.x) & 15) == 0 && (a.x_stride & 3) == 0;
+    for (int it = tid; it < NT * ngroups; it += kThreads) {
+      const int t = it / ngroups, g = it - t * ngroups;
+      float v[32];
+      if (t >= T) {
 #pragma unroll
-      for (int b = 0; b < kB; ++b) {
-        const int it = it0 + b * W, t = it / ngroups, g = it - t * ngroups;
-        vb[b] = it < NT * ngroups && t < T ? load_float(a.x, a.x_dtype, (int64_t)t * a.x_stride + 32 * g + lane) : 0.f;
+        for (int j = 0; j < 32; ++j) v[j] = 0.f;
+      } else if (x_vec) {
+        const float4* src = reinterpret_cast<const float4*>(static_cast<const float*>(a.x) + (int64_t)t * a.x_stride + 32 * g);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const float4 f = src[j];
+          v[4 * j] = f.x; v[4 * j + 1] = f.y; v[4 * j + 2] = f.z; v[4 * j + 3] = f.w;
+        }
+      } else {
+#pragma unroll
+        for (int j = 0; j < 32; ++j) v[j] = load_float(a.x, a.x_dtype, (int64_t)t * a.x_stride + 32 * g + j);
       }
+      float m = 0.f, sum = 0.f;
 #pragma unroll
-      for (int b = 0; b < kB; ++b) {
-        const int it = it0 + b * W;
-        if (it >= NT * ngroups) break;
-        const int t = it / ngroups, g = it - t * ngroups;
-        const float v = vb[b];
-        float m = fabsf(v);
+      for (int j = 0; j < 32; ++j) {
+        m = fmaxf(m, fabsf(v[j]));
+        sum += v[j];
+      }
+      // max|x| < 2^e with e = be - 126; groups below 2^-104 (and non-finite ones) are taken as zeros
+      const int be = (int)((__float_as_uint(m) >> 23) & 255u);
+      const bool live = be >= 22 && be < 255;
+      const float to_fixed = __uint_as_float((uint32_t)(275 - be) << 23);  // 2^(22-e)
+      uint32_t pl[3][8] = {};
 #pragma unroll
-        for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-        // max|x| < 2^e with e = be - 126; groups below 2^-104 (and non-finite ones) are taken as zeros
-        const int be = (int)((__float_as_uint(m) >> 23) & 255u);
-        const bool live = be >= 22 && be < 255;
-        int X = 0;
-        if (live) X = __float2int_rn(v * __uint_as_float((uint32_t)(275 - be) << 23));  // v * 2^(22-e)
+      for (int j = 0; j < 32; ++j) {
+        const int X = live ? __float2int_rn(v[j] * to_fixed) : 0;
         const int d0 = ((X + 128) & 255) - 128;
         const int X1 = (X - d0) >> 8;
         const int d1 = ((X1 + 128) & 255) - 128;
         const int d2 = (X1 - d1) >> 8;
-        uint8_t* dst = xq + (size_t)t * xqs + (size_t)g * kXQG + lane;
-        dst[0] = (uint8_t)d0;
-        dst[32] = (uint8_t)d1;
-        dst[64] = (uint8_t)d2;
-        const float sum = warp_sum(v);
-        if (lane == 0) {
-          xsc[t * ngroups + g] = live ? __uint_as_float((uint32_t)(be - 21) << 23) : 0.f;  // 2^(e-22)
-          xsum[t * ngroups + g] = sum;
-        }
+        pl[0][j >> 2] |= (uint32_t)(d0 & 255) << (8 * (j & 3));
+        pl[1][j >> 2] |= (uint32_t)(d1 & 255) << (8 * (j & 3));
+        pl[2][j >> 2] |= (uint32_t)(d2 & 255) << (8 * (j & 3));
+      }
+      uint4* grp = reinterpret_cast<uint4*>(xq + (size_t)t * xqs + (size_t)g * kXQG);
+#pragma unroll
+      for (int p = 0; p < 3; ++p) {
+        grp[2 * p] = make_uint4(pl[p][0], pl[p][1], pl[p][2], pl[p][3]);
+        grp[2 * p + 1] = make_uint4(pl[p][4], pl[p][5], pl[p][6], pl[p][7]);
+      }
+      xsc[t * ngroups + g] = live ? __uint_as_float((uint32_t)(be - 21) << 23) : 0.f;  // 2^(e-22)
+      xsum[t * ngroups + g] = sum;
+    }
+  } else if (a.x_dtype == NS_F32 && (reinterpret_cast<uintptr_t>(a.x) & 15) == 0 && (a.x_stride & 3) == 0) {
+    // fp32 x: 4 elements a load (a group's padded row is 144 B, so float4 stores stay aligned)
+    constexpr int kB = 4;
+    const int n4 = NT * K / 4;
+    for (int i0 = tid; i0 < n4; i0 += kB * kThreads) {
+      float4 vb[kB];
+#pragma unroll
+      for (int b = 0; b < kB; ++b) {
+        const int i = i0 + b * kThreads, t = 4 * i / K, k = 4 * i - t * K;
+        vb[b] = i < n4 && t < T ? *reinterpret_cast<const float4*>(static_cast<const float*>(a.x) + (int64_t)t * a.x_stride + k)
+                                : make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+#pragma unroll
+      for (int b = 0; b < kB; ++b) {
+        const int i = i0 + b * kThreads, t = 4 * i / K, k = 4 * i - t * K;
+        if (i < n4) *reinterpret_cast<float4*>(xs + t * xt + (k >> 5) * kXG + (k & 31)) = vb[b];
       }
     }
   } else {
