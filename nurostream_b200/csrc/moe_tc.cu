@@ -279,40 +279,21 @@ __device__ __forceinline__ void halfwarp_block_planes(float v0, float v1, uint8_
     for (int p = 0; p < 8; ++p) sdst[p * sstride] = (uint8_t)plane_scale(p, be);
 }
 
-// Phase-1 B operand: the digit planes of h = (x * r) * norm_w, built from L2 by 16 warps (32
-// half-warps, index hw) while the first weight chunks are in flight.  Token t's planes are rows
-// 8t..8t+7: core matrix (t, block b) at b1 + t*nb_h*128 + b*128; scale atom b/4 at
-// sfb1 + (b/4)*sfb1_atom, byte 16*(8t+p) + b%4.
-__device__ __forceinline__ void tc_build_b1(const ns_moe_layer_t& p, int T, int nb_h, const float* rscale, uint8_t* b1,
-                                            uint8_t* sfb1, int sfb1_atom, int hw, int lane) {
+// Phase-1 B operand: the digit planes of h = (x * r) * norm_w, built by 16 warps (32 half-warps,
+// index hw) from the copy of h the prologue left in shared memory, while the first weight chunks
+// are in flight.  (Reading x again from L2 here queued behind the weight stream for ~4 us.)
+// Token t's planes are rows 8t..8t+7: core matrix (t, block b) at b1 + t*nb_h*128 + b*128; scale
+// atom b/4 at sfb1 + (b/4)*sfb1_atom, byte 16*(8t+p) + b%4.
+__device__ __forceinline__ void tc_build_b1(const float* h, int H, int T, int nb_h, uint8_t* b1, uint8_t* sfb1,
+                                            int sfb1_atom, int hw, int lane) {
   const int hl = lane & 15;
   const unsigned mask = 0xFFFFu << (lane & 16);
   const int nit = T * nb_h;
-  for (int it0 = hw; it0 < nit; it0 += 4 * 32) {  // up to 4 blocks per half-warp: all loads first
-    float v[4][2], w[4][2];
-#pragma unroll
-    for (int u = 0; u < 4; ++u) {
-      const int it = it0 + 32 * u;
-      const int t = it < nit ? it / nb_h : 0, b = it < nit ? it - t * nb_h : 0;
-      const int64_t i0 = (int64_t)t * p.H + 32 * b + hl;
-      v[u][0] = it < nit ? p.x[i0] : 0.f;
-      v[u][1] = it < nit ? p.x[i0 + 16] : 0.f;
-      w[u][0] = it < nit && p.norm_w ? p.norm_w[32 * b + hl] : 1.f;
-      w[u][1] = it < nit && p.norm_w ? p.norm_w[32 * b + hl + 16] : 1.f;
-    }
-#pragma unroll
-    for (int u = 0; u < 4; ++u) {
-      const int it = it0 + 32 * u;
-      if (it >= nit) break;
-      const int t = it / nb_h, b = it - t * nb_h;
-      float v0 = v[u][0], v1 = v[u][1];
-      if (p.norm_w) {
-        v0 = __fmul_rn(__fmul_rn(v0, rscale[t]), w[u][0]);
-        v1 = __fmul_rn(__fmul_rn(v1, rscale[t]), w[u][1]);
-      }
-      halfwarp_block_planes(v0, v1, b1 + (size_t)t * nb_h * 128 + b * 128,
-                            sfb1 + (b >> 2) * sfb1_atom + 16 * (8 * t) + (b & 3), 16, hl, mask);
-    }
+  for (int it = hw; it < nit; it += 32) {
+    const int t = it / nb_h, b = it - t * nb_h;
+    const float* hb = h + (int64_t)t * H + 32 * b + hl;
+    halfwarp_block_planes(hb[0], hb[16], b1 + (size_t)t * nb_h * 128 + b * 128,
+                          sfb1 + (b >> 2) * sfb1_atom + 16 * (8 * t) + (b & 3), 16, hl, mask);
   }
 }
 
@@ -371,7 +352,10 @@ __global__ void __launch_bounds__(kTcThreads, 1) moe_tc_kernel(const __grid_cons
   // wait on the previous kernel of the stream: under programmatic dependent launch that wait is
   // where x and the workspace, which the previous layer wrote, become visible.
   static_assert(128 * 32 <= 8 * kTcThreads, "H <= 4096 (moe_tc_eligible) must fit one pass");
-  float* h = reinterpret_cast<float*>(raw);  // T x H fp32, reused by the raw ring after the prologue
+  static_assert(2 * 4096 * 4 <= kTcRawBytes, "T x H fp32 (T <= 2, H <= 4096) must fit one raw stage");
+  // T x H fp32 in the last raw stage: read by the prologue and the phase-1 plane builders; the
+  // producer overwrites it only after b1_ready
+  float* h = reinterpret_cast<float*>(raw + (TcRaw<NT>::kStages - 1) * kTcRawBytes);
   const bool own_expert = c < E;
   float wv[8], rv[8];
 #pragma unroll
@@ -695,6 +679,8 @@ __global__ void __launch_bounds__(kTcThreads, 1) moe_tc_kernel(const __grid_cons
                                           : up ? (gv == 16 ? &a.tm_up16 : &a.tm_up8)
                                                : (gv == 16 ? &a.tm_gate16 : &a.tm_gate8);
           const int st = n % TcRaw<NT>::kStages;
+          // the last stage holds h until the phase-1 planes are built
+          if (n == TcRaw<NT>::kStages - 1 && !tc_wait(b1_ready, 0, abort_flag)) break;
           if (!tc_wait(&empty_raw[st], ((n / TcRaw<NT>::kStages) & 1) ^ 1, abort_flag)) break;
           mbar_arrive_expect_tx(&full_raw[st], (uint32_t)(8 * gv * kTcBoxW));
           uint8_t* dst = raw + st * kTcRawBytes;
@@ -791,7 +777,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) moe_tc_kernel(const __grid_cons
     // block: 5 word loads of the staged row, the 16 payload bytes to 4 TMEM columns of row m; the
     // E8M0 bytes of a 4-block atom form one TMEM word of row m (lane m, column 4*atom + m/32).
     const int rw = tc_repack_index(warp);  // 0..11
-    tc_build_b1(p, T, a.nb_h, S.rscale, b1, sfb1, a.sfb1_atom, 2 * rw + (lane >> 4), lane);
+    tc_build_b1(h, H, T, a.nb_h, b1, sfb1, a.sfb1_atom, 2 * rw + (lane >> 4), lane);
     fence_proxy_async_smem();
     __syncwarp();
     if (lane == 0) mbar_arrive(b1_ready);
@@ -922,7 +908,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) moe_tc_kernel(const __grid_cons
     const int row = tc_row_of(mrow);      // the tile row it holds
     const int et = mrow;                  // 0..127
     float* xchg = reinterpret_cast<float*>(smem + a.off_xchg);
-    tc_build_b1(p, T, a.nb_h, S.rscale, b1, sfb1, a.sfb1_atom, 2 * (kTcRepackWarps + q) + (lane >> 4), lane);
+    tc_build_b1(h, H, T, a.nb_h, b1, sfb1, a.sfb1_atom, 2 * (kTcRepackWarps + q) + (lane >> 4), lane);
     fence_proxy_async_smem();
     __syncwarp();
     if (lane == 0) mbar_arrive(b1_ready);
