@@ -8,13 +8,16 @@ bytes per step (1.9 GB) are far larger than L2 (126 MB), so no flush is needed.
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
   python bench.py --workload gemv [--steps K] [--warmup W]
   python bench.py --workload qwen3 [--layers L] [--steps K] [--warmup W]
+  python bench.py --workload prefill [--layers L] [--steps K] [--warmup W]
 
 ``--workload gemv`` measures the dense dequant-GEMV sweep instead (batch 1,
 K = 4096, N in {4096, 11008, 14336}, MXFP4 / Q4_K / Q8_0): one JSON line per
 case, HBM GB/s against the measured copy peak, weight copies rotated so that
 every launch streams from HBM.  ``--workload qwen3`` runs the decode step on
 the Qwen3-235B-A22B shape instead (94 MoE layers, hidden 4096, 128 experts,
-top-8, expert ffn 1536, Q4_K experts; MoE layers only).
+top-8, expert ffn 1536, Q4_K experts; MoE layers only).  ``--workload prefill``
+runs 512 prompt tokens through the GPT-OSS-shaped MoE layers (config 5), each
+layer as slices of a few tokens through the fused layer kernel.
 
 N > 1 runs expert parallel under torchrun (experts split by index, one NCCL
 all-reduce per layer).  ``--impl reference`` times the reference's CPU path
@@ -414,6 +417,91 @@ def run_gemv_sweep(args):
     return lines
 
 
+def run_prefill(args):
+    """Prefill of ``--prefill-tokens`` prompt tokens through the GPT-OSS-shaped MoE layers (config 5).
+
+    Each layer runs as slices of 2 tokens through the tensor-core layer kernel (``MoeLayer.prefill``), all
+    launches of a step captured in one CUDA graph.  Algorithmic bytes per layer: every expert that the
+    step's tokens route to, read once (at T = 512 that is all 128), plus the router and activations.
+    """
+    import torch
+
+    from nurostream_b200 import synth
+    from nurostream_b200.decoder import MoeDecoder
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    shape = bench_shape(args)
+    T, H = args.prefill_tokens, shape.hidden
+    dec = MoeDecoder(shape, dev, 0, 1, None, use_graph=False, max_tokens=8)
+    x = torch.empty((T, H), device=dev, dtype=torch.float32)
+    synth.fill_float(x.view(-1), 778, 1)
+    x_host = x.cpu().pin_memory()
+    out_host = torch.empty((T, H), dtype=torch.float32, pin_memory=True)
+    bufs = [torch.empty_like(x) for _ in range(2)]
+    dec.prefill(x, bufs)                         # warm-up outside capture (settles the slice size)
+    torch.cuda.synchronize()
+    sl = dec.layers[0]._slice
+    n_launch = -(-T // sl)
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        y = dec.prefill(x, bufs)
+    for _ in range(args.warmup):
+        g.replay()
+    torch.cuda.synchronize()
+    dec.check_device_errors()
+    clocks = ClockSampler(0)
+    clocks.start()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        g.replay()
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / args.steps
+    # end to end: prompt in from pinned host memory, hidden states back, every step
+    f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    f0.record()
+    for _ in range(args.steps):
+        x.copy_(x_host, non_blocking=True)
+        g.replay()
+        out_host.copy_(y, non_blocking=True)
+    f1.record()
+    torch.cuda.synchronize()
+    ms_e2e = f0.elapsed_time(f1) / args.steps
+    clk = clocks.stop()
+    dec.check_device_errors()
+    peak, peak_kind = measured_peaks()
+    E = shape.n_expert
+    expert_bytes = shape.expert_bytes                      # one expert's gate + up + down rows
+    layer_bytes = E * expert_bytes + E * H * 2 + 2 * T * H * 4   # all experts (T = 512 touches all 128)
+    per_layer_s = ms / 1000.0 / shape.n_layer
+    achieved = layer_bytes / per_layer_s / 1e9
+    line = {
+        "metric": "prefill tok/s (GPT-OSS-120B shape, 512-token prompt, MoE layers)", "value": round(T * 1000.0 / ms, 1),
+        "unit": "tok/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 3),
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+        "dtype": "mxfp4 weights, fp32 accumulate", "data": "synthetic (seeded splitmix64 GGUF bytes generated in HBM)",
+        "config": {"workload": f"gpt-oss-120b-shape MoE prefill: {T} tokens x {shape.n_layer} layers, each layer as "
+                               f"{n_launch} fused launches of {sl} tokens", "tokens": T, "layers": shape.n_layer,
+                   "experts": E, "top_k": shape.top_k, "parallelism": "single",
+                   "l2": "inputs larger than L2 (every layer streams its experts from HBM)"},
+        "e2e": {"value": round(T * 1000.0 / ms_e2e, 1), "unit": "tok/s", "h2d_bytes_per_step": T * H * 4,
+                "d2h_bytes_per_step": T * H * 4},
+        "gpu_launches": shape.n_layer * n_launch * args.steps,
+        "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                     "frac": round(achieved / peak, 4), "traffic": None, "peak_kind": peak_kind,
+                     "kernel": "moe_tc_kernel" if sl <= 2 else "moe_layer_kernel",
+                     "algorithmic_bytes_per_layer": layer_bytes,
+                     "note": "each slice streams the experts its tokens route to, so an expert is read once per "
+                             "slice that uses it: HBM traffic is many times the algorithmic bytes"},
+    }
+    if clk:
+        line["clocks"] = clk
+    g = None
+    return line
+
+
 def run_reference(args, rank, world):
     """The reference's own CPU implementation of the path (oracle port), host cores only.
 
@@ -465,7 +553,8 @@ def main():
     ap.add_argument("--ref-layers", type=int, default=2)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-graph", action="store_true")
-    ap.add_argument("--workload", choices=["decode", "gemv", "qwen3"], default="decode")
+    ap.add_argument("--workload", choices=["decode", "gemv", "qwen3", "prefill"], default="decode")
+    ap.add_argument("--prefill-tokens", type=int, default=512)
     ap.add_argument("--gemv-case", default="", help="run one GEMV case only, e.g. MXFP4:14336")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
@@ -479,6 +568,9 @@ def main():
     if args.workload == "gemv":
         for line in run_gemv_sweep(args):
             print(json.dumps(line), flush=True)
+        return
+    if args.workload == "prefill" and args.impl == "ours" and world == 1:
+        print(json.dumps(run_prefill(args)), flush=True)
         return
     if args.impl == "reference":
         line = run_reference(args, rank, world)

@@ -168,8 +168,9 @@ typedef struct ns_moe_layer {
   float* weights;         /* T x k fp32 routing weights, or NULL */
 } ns_moe_layer_t;
 
-/* Workspace bytes a layer call needs (zeroed once with ns_moe_workspace_init;
- * one workspace serves any number of stream-ordered calls on one device).
+/* Workspace bytes a layer call with 1..p->T tokens needs (zeroed once with
+ * ns_moe_workspace_init; one workspace serves any number of stream-ordered
+ * calls on one device).
  * The tensor-core layer kernel is launched with programmatic dependent launch:
  * it may read norm_w and router_w before the previous kernel on the stream has
  * finished, if that kernel signals its dependents early (the layer kernel

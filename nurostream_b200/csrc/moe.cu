@@ -1130,7 +1130,16 @@ extern "C" int ns_moe_workspace_bytes(const ns_moe_layer_t* p, size_t* bytes) {
   MoePlan plan;
   int st = moe_validate(p, &plan);
   if (st) return st;
-  *bytes = plan.ws_total;
+  size_t need = plan.ws_total;
+  // a layer sized for T tokens serves calls with fewer; those may take the tensor-core kernel,
+  // whose scratch differs from the CUDA-core kernel's
+  for (int t = 1; t < p->T; ++t) {
+    ns_moe_layer_t q = *p;
+    q.T = t;
+    MoePlan pt;
+    if (moe_validate(&q, &pt) == NS_OK) need = std::max(need, pt.ws_total);
+  }
+  *bytes = need;
   return NS_OK;
 }
 

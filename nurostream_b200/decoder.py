@@ -69,8 +69,9 @@ def expert_range(rank: int, world: int, n_expert: int) -> tuple[int, int]:
 
 class MoeDecoder:
     def __init__(self, shape: MoeShape, device: torch.device | str = "cuda", rank: int = 0, world: int = 1,
-                 group=None, use_graph: bool = True):
+                 group=None, use_graph: bool = True, max_tokens: int = 1):
         self.shape = shape
+        self.max_tokens = max_tokens  # rows per fused launch (prefill runs slices of this many)
         self.device = torch.device(device)
         self.rank, self.world, self.group = rank, world, group
         self.lo, self.hi = expert_range(rank, world, shape.n_expert)
@@ -105,7 +106,7 @@ class MoeDecoder:
                 H=H, F=F, n_expert=E, k=sh.top_k, ggml_type=t,
                 router_w=flt(E * H, s.router_w, 0.02, sh.router_dtype).reshape(E, H),
                 gate=quant(s.gate, F, H), up=quant(s.up, F, H), down=quant(s.down, H, F),
-                expert_lo=self.lo, expert_hi=self.hi, max_tokens=1,
+                expert_lo=self.lo, expert_hi=self.hi, max_tokens=self.max_tokens,
                 route_mode=_lib.NS_ROUTE_SOFTMAX_TOPK_NORM, act_mode=_lib.NS_ACT_SILU_MUL,
             )
         norm = flt(H, s.norm_w, 0.1) + 1.0
@@ -118,7 +119,7 @@ class MoeDecoder:
             gate_b=flt(n_local * F, s.gate_b, sh.bias_sigma, start=self.lo * F).reshape(n_local, F),
             up_b=flt(n_local * F, s.up_b, sh.bias_sigma, start=self.lo * F).reshape(n_local, F),
             down_b=flt(n_local * H, s.down_b, sh.bias_sigma, start=self.lo * H).reshape(n_local, H),
-            expert_lo=self.lo, expert_hi=self.hi, rms_eps=1e-5, max_tokens=1,
+            expert_lo=self.lo, expert_hi=self.hi, rms_eps=1e-5, max_tokens=self.max_tokens,
         )
 
     # ------------------------------------------------------------------ one token
@@ -169,6 +170,22 @@ class MoeDecoder:
         out_host.copy_(y, non_blocking=True)
         torch.cuda.current_stream(self.device).synchronize()
         return out_host
+
+    # ------------------------------------------------------------------ many tokens
+
+    def prefill(self, x: torch.Tensor, bufs: list[torch.Tensor] | None = None) -> torch.Tensor:
+        """T tokens (T, H) fp32 on device through every layer, each layer as slices of max_tokens
+        rows (``MoeLayer.prefill``); bufs: two (T, H) fp32 ping-pong buffers (allocated if None)."""
+        if bufs is None:
+            bufs = [torch.empty_like(x) for _ in range(2)]
+        cur = x
+        for l, layer in enumerate(self.layers):
+            nxt = bufs[l % 2]
+            layer.prefill(cur, out=nxt, add_residual=(self.rank == 0))
+            if self.world > 1:
+                torch.distributed.all_reduce(nxt, group=self.group)
+            cur = nxt
+        return cur
 
     def release(self) -> None:
         """Drop the graph (it may hold NCCL work) before the process group goes away."""

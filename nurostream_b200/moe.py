@@ -96,6 +96,7 @@ class MoeLayer:
         self.route_mode, self.act_mode = route_mode, act_mode
         self.alpha, self.limit, self.rms_eps = alpha, limit, rms_eps
         self.max_tokens = max_tokens
+        self._slice = 0  # rows per launch that prefill settled on
         self.device = dev
         p = self._params(max_tokens, None, None, True, None, None)
         n = C.c_size_t(0)
@@ -132,6 +133,40 @@ class MoeLayer:
             out = torch.empty_like(x)
         p = self._params(T, x, out, add_residual, ids, weights)
         _lib.call("ns_moe_decode_layer", C.byref(p), self._ws_ptr, self._ws_bytes, stream_of(x))
+        return out
+
+    def prefill(self, x: torch.Tensor, out: torch.Tensor | None = None, add_residual: bool = True,
+                ids: torch.Tensor | None = None, weights: torch.Tensor | None = None) -> torch.Tensor:
+        """Any number of token rows (prefill, T > max_tokens): the fused layer on successive slices
+        of ``max_tokens`` rows, stream-ordered, no host synchronisation.
+
+        Tokens are independent through RMSNorm, routing, the experts and the combine, so the slices
+        give exactly the rows of one T-row call.  Each slice streams the experts its tokens route
+        to, so an expert shared by several slices is read once per slice: the prefill of
+        ``blockffn.py:171-176`` / ``router.py:158-166`` without a grouped GEMM.
+        """
+        if x.dtype != torch.float32 or not x.is_contiguous() or x.dim() != 2:
+            raise TypeError("x must be a contiguous (T, H) float32 tensor")
+        T = x.shape[0]
+        if out is None:
+            out = torch.empty_like(x)
+        # MXFP4 slices of 2 rows run on the tensor-core layer kernel, which streams faster per token
+        # than the wider CUDA-core slices; a slice the library refuses (activations beyond shared
+        # memory) is halved once and for all
+        size = self._slice or (min(2, self.max_tokens) if self.t == GGMLType.MXFP4 else self.max_tokens)
+        t0 = 0
+        while t0 < T:
+            t1 = min(T, t0 + size)
+            try:
+                self(x[t0:t1], out=out[t0:t1], add_residual=add_residual,
+                     ids=None if ids is None else ids[t0:t1], weights=None if weights is None else weights[t0:t1])
+            except _lib.NsError as e:
+                if e.status != -2 or t0 > 0 or size == 1:
+                    raise
+                size //= 2
+                continue
+            self._slice = size
+            t0 = t1
         return out
 
 
@@ -205,7 +240,7 @@ def _run_fused(model, layer_obj: MoeLayer, x: torch.Tensor, layer: int, add_resi
     ids = torch.empty((T, layer_obj.k), device=x.device, dtype=torch.int32)
     weights = torch.empty((T, layer_obj.k), device=x.device, dtype=torch.float32)
     try:
-        out = layer_obj(xf, add_residual=add_residual, ids=ids, weights=weights)
+        out = layer_obj.prefill(xf, add_residual=add_residual, ids=ids, weights=weights)
     except _lib.NsError as e:
         if e.status == -2:  # shape outside the fused kernel: use the streaming path
             return None
@@ -231,7 +266,7 @@ def gptoss_route(model, h: torch.Tensor, layer: int):
 
 def gptoss_ffn_block(model, x: torch.Tensor, layer: int):
     """Drop-in for ``GptOssModel._ffn_block``: ``x + MoE(rms_norm(x))``."""
-    if x.is_cuda and x.shape[0] <= _lib.NS_MAX_TOKENS:
+    if x.is_cuda and x.shape[0] >= 1:
         lay = _layer_for(model, layer, gptoss=True)
         if lay is not None:
             out = _run_fused(model, lay, x, layer, add_residual=True)
@@ -242,7 +277,7 @@ def gptoss_ffn_block(model, x: torch.Tensor, layer: int):
 
 def moe_ffn(model, h: torch.Tensor, layer: int) -> torch.Tensor:
     """Drop-in for ``neurostream.moe.router.moe_ffn`` (Qwen3-MoE; returns the MoE output only)."""
-    if h.is_cuda and h.shape[0] <= _lib.NS_MAX_TOKENS:
+    if h.is_cuda and h.shape[0] >= 1:
         lay = _layer_for(model, layer, gptoss=False)
         if lay is not None:
             out = _run_fused(model, lay, h, layer, add_residual=False)

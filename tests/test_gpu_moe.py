@@ -128,3 +128,24 @@ def test_too_many_activation_rows_is_reported_not_run():
     with pytest.raises(_lib.NsError) as e:
         layer(torch.from_numpy(L.x).cuda())
     assert e.value.status == -2
+
+
+@pytest.mark.parametrize("kw", [
+    dict(T=20),                                                                       # GPT-OSS, 8 + 8 + 4
+    dict(arch="qwen3moe", type=12, E=32, k=8, H=1024, F=512, T=11, bias=False, norm=None),
+])
+def test_prefill_slices_match_oracle(kw):
+    """T > max_tokens runs as slices of max_tokens rows; rows equal the oracle's T-row layer."""
+    c = _cfg(E=32, H=1024, F=1024, seed=31)
+    c.update(kw)
+    L = goldens.SynthLayer(c)
+    layer = layer_from_synth(L, max_tokens=8)
+    xt = torch.from_numpy(np.ascontiguousarray(L.x, dtype=np.float32)).cuda()
+    ids = torch.empty((L.T, L.k), dtype=torch.int32, device="cuda")
+    w = torch.empty((L.T, L.k), dtype=torch.float32, device="cuda")
+    out = layer.prefill(xt, add_residual=L.gptoss, ids=ids, weights=w)
+    torch.cuda.synchronize()
+    assert _lib.device_error() == 0
+    o_out, o_ids, _ = _oracle_layer(L)
+    np.testing.assert_array_equal(ids.cpu().numpy().astype(np.int64), o_ids)
+    assert_rel_close(out.cpu().numpy(), o_out, 2e-5, f"prefill {kw}")

@@ -83,6 +83,10 @@ def test_moe_workspace_bytes_and_validation(lib):
     assert n.value == max(v2, tc)
     assert lib.ns_moe_workspace_bytes(C.byref(_params(ggml_type=int(GGMLType.Q8_0))), C.byref(n)) == 0
     assert n.value == v2
+    # sized for up to 8 tokens: also covers the tensor-core kernel's scratch of the 1- and 2-token calls
+    n8 = C.c_size_t(0)
+    assert lib.ns_moe_workspace_bytes(C.byref(_params(T=8)), C.byref(n8)) == 0
+    assert n8.value >= max(v2, tc)
     bad = [dict(T=0), dict(T=9), dict(k=0), dict(k=33), dict(n_expert=600), dict(expert_lo=4, expert_hi=4),
            dict(H=100), dict(route_mode=7), dict(act_mode=3), dict(ggml_type=int(GGMLType.Q5_K)),
            dict(router_dtype=9)]
