@@ -103,3 +103,37 @@ def test_install_patches_and_restores_reference(monkeypatch):
         assert not tk.can_fuse(GGMLType.MXFP4, torch.zeros(1, 32))
     assert (tk.can_fuse, tk.fused_gemv, q.dequantize, cache_mod.dequantize, go.GptOssModel._route,
             go.GptOssModel._ffn_block, rt.moe_ffn) == originals
+
+
+def test_prefill_slices_cover_every_row_and_halve_on_refusal():
+    """MoeLayer.prefill: slices of the launch size in order, halved once when the library refuses
+    a slice (status -2) before anything ran; the settled size is kept for later calls."""
+    from nurostream_b200 import _lib
+    from nurostream_b200.moe import MoeLayer
+
+    calls = []
+
+    class Fake(MoeLayer):
+        def __init__(self, t, max_tokens, limit):
+            self.t, self.max_tokens, self._slice, self.limit = t, max_tokens, 0, limit
+
+        def __call__(self, x, out=None, add_residual=True, ids=None, weights=None):
+            if x.shape[0] > self.limit:
+                raise _lib.NsError(-2, "does not fit")
+            calls.append((x.shape[0], int(x[0, 0]), ids.shape[0] if ids is not None else None))
+            out.copy_(x + 1.0)
+            return out
+
+    x = torch.arange(20, dtype=torch.float32).reshape(20, 1).contiguous()
+    ids = torch.zeros((20, 4), dtype=torch.int32)
+    lay = Fake(GGMLType.Q4_K, 8, 4)
+    out = lay.prefill(x, ids=ids)
+    assert [c[0] for c in calls] == [4, 4, 4, 4, 4] and [c[1] for c in calls] == [0, 4, 8, 12, 16]
+    assert all(c[2] == c[0] for c in calls)
+    assert torch.equal(out, x + 1.0) and lay._slice == 4
+    calls.clear()
+    lay = Fake(GGMLType.MXFP4, 8, 8)          # MXFP4 takes 2-row slices (tensor-core layer kernel)
+    lay.prefill(x[:5].contiguous())
+    assert [c[0] for c in calls] == [2, 2, 1]
+    with pytest.raises(_lib.NsError):         # a refusal at one row is an error, not a loop
+        Fake(GGMLType.Q8_0, 8, 0).prefill(x)
