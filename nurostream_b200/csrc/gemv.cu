@@ -53,7 +53,7 @@ __host__ __device__ inline size_t gemv_x_bytes(bool int8, int nt, int K) {
 template <int FMT, int NT, int R>
 __device__ __forceinline__ void dot_rows_i8(const uint8_t* const (&rows)[R], int ngroups, int g0, int gstep,
                                             const uint8_t* xq, int xqs, const float* xsc, const float* xsum,
-                                            float (&acc)[R][NT]) {
+                                            float (&acc)[R][NT], bool rows16) {
   for (int g = g0; g < ngroups; g += gstep) {
     uint32_t q[R][8];
     float da[R], db[R];  // Q8_0: d, 0; Q4_K: d*sc, dmin*mn
@@ -68,7 +68,10 @@ __device__ __forceinline__ void dot_rows_i8(const uint8_t* const (&rows)[R], int
         for (int i = 0; i < 8; ++i) q[r][i] = __funnelshift_r(w[i], w[i + 1], 16);  // signed int8 x 4
       } else {
         QGroup<NS_GGML_Q4_K> qg;
-        qg.load(rows[r], g);
+        if (rows16)  // rows start on 16-byte boundaries
+          qg.load_aligned(rows[r], g);
+        else
+          qg.load(rows[r], g);
         da[r] = qg.dsc;
         db[r] = qg.mmn;
 #pragma unroll
@@ -313,7 +316,8 @@ __global__ void __launch_bounds__((W + 1) * 32, 1) gemv_kernel(GemvArgs a) {
 #pragma unroll
         for (int t = 0; t < NT; ++t) acc[r][t] = 0.f;
       if constexpr (kInt)
-        dot_rows_i8<FMT, NT, R>(rows, ngroups, warp * LG + lg, W * LG, xq, xqs, xsc, xsum, acc);
+        dot_rows_i8<FMT, NT, R>(rows, ngroups, warp * LG + lg, W * LG, xq, xqs, xsc, xsum, acc,
+                                row_copies || ((reinterpret_cast<uintptr_t>(base) & 15) == 0 && a.rb % 16 == 0));
       else
         dot_rows<FMT, NT, R, kXG, true>(rows, R, ngroups, warp * LG + lg, xs, xt, tok, NT, acc, W * LG);
 #pragma unroll

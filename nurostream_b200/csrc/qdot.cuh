@@ -151,28 +151,39 @@ struct QGroup<NS_GGML_Q4_K> {
   uint32_t q[8];
   float dsc, mmn;  // d*sc and dmin*mn of this sub-block (both exact in fp32)
 
+  // sub-block s's 6-bit scale and min from the 12 scale bytes (words h1, h2, h3 = bytes 0-3, 4-7,
+  // 8-11): s < 4 reads bytes s and s + 4; s >= 4 combines byte s + 4 with the top bits of bytes
+  // s - 4 and s.  Byte (s & 3) of each word, so no indexing by s.
+  __device__ __forceinline__ void scales(uint32_t hdw, uint32_t h1, uint32_t h2, uint32_t h3, int s) {
+    const unsigned sh = 8u * (unsigned)(s & 3);
+    const uint32_t b1 = (h1 >> sh) & 0xFFu, b2 = (h2 >> sh) & 0xFFu, b3 = (h3 >> sh) & 0xFFu;
+    const uint32_t sc = s < 4 ? (b1 & 63u) : ((b3 & 0x0Fu) | ((b1 >> 6) << 4));
+    const uint32_t mn = s < 4 ? (b2 & 63u) : ((b3 >> 4) | ((b2 >> 6) << 4));
+    dsc = f16_bits_to_float(hdw) * (float)sc;
+    mmn = f16_bits_to_float(hdw >> 16) * (float)mn;
+  }
+
   __device__ __forceinline__ void load(const uint8_t* row, int g) {
     const uint8_t* p = row + 144 * (g >> 3);
     const int s = g & 7;
     uint32_t hd[4];
     lds_words_unaligned<4>(p, hd);  // d | dmin | scales[0..11]
-    const float d = f16_bits_to_float(hd[0]);
-    const float dmin = f16_bits_to_float(hd[0] >> 16);
-    // scale byte j is byte (j % 4) of hd[1 + j / 4]
-    auto sb = [&](int j) -> uint32_t { return (hd[1 + (j >> 2)] >> (8 * (j & 3))) & 0xFFu; };
-    uint32_t sc, mn;
-    if (s < 4) {
-      sc = sb(s) & 63u;
-      mn = sb(s + 4) & 63u;
-    } else {
-      sc = (sb(s + 4) & 0x0Fu) | ((sb(s - 4) >> 6) << 4);
-      mn = (sb(s + 4) >> 4) | ((sb(s) >> 6) << 4);
-    }
-    dsc = d * (float)sc;
-    mmn = dmin * (float)mn;
+    scales(hd[0], hd[1], hd[2], hd[3], s);
     uint32_t w[8];
     lds_words_unaligned<8>(p + 16 + 32 * (s >> 1), w);
     const unsigned sh = (s & 1) ? 4u : 0u;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) q[i] = (w[i] >> sh) & 0x0F0F0F0Fu;
+  }
+  // the same from a 16-byte aligned row (superblocks are 144 = 9 x 16 bytes): three vector loads
+  __device__ __forceinline__ void load_aligned(const uint8_t* row, int g) {
+    const uint4* p = reinterpret_cast<const uint4*>(row + 144 * (g >> 3));
+    const int s = g & 7;
+    const uint4 hd = p[0];
+    scales(hd.x, hd.y, hd.z, hd.w, s);
+    const uint4 a = p[1 + 2 * (s >> 1)], b = p[2 + 2 * (s >> 1)];
+    const unsigned sh = (s & 1) ? 4u : 0u;
+    const uint32_t w[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
 #pragma unroll
     for (int i = 0; i < 8; ++i) q[i] = (w[i] >> sh) & 0x0F0F0F0Fu;
   }
