@@ -1,28 +1,27 @@
-"""Benchmark: batch-1 decode through the GPT-OSS-120B-shaped MoE hot path.
+"""Benchmark: batch-1 decode of a GPT-OSS-120B-shaped model on one B200 (or expert-parallel on N).
 
-One step = one decode token through 36 MoE layers (RMSNorm -> router top-4 of
-128 -> MXFP4 gate/up (2880x2880) -> clamped SwiGLU -> down -> weighted combine
--> residual), one fused launch per layer, captured in a CUDA graph.  Expert
-bytes per step (1.9 GB) are far larger than L2 (126 MB), so no flush is needed.
+One step = one decode token through the whole model (config 3): embedding, 36 x (RMSNorm + bf16
+q/k/v + YaRN RoPE + sink attention over a 2048-position KV cache, sliding window 128 on even
+layers, + bf16 output projection + the MoE block: RMSNorm, router top-4 of 128, MXFP4 gate/up
+2880x2880, clamped SwiGLU, down, weighted combine) and the LM head over a 201,088-token
+vocabulary: 146 kernel launches captured in one CUDA graph.  About 5 GB of weights are read per
+step against 126 MB of L2, so no flush is needed between steps.
 
-  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-  python bench.py --workload gemv [--steps K] [--warmup W]
-  python bench.py --workload qwen3 [--layers L] [--steps K] [--warmup W]
-  python bench.py --workload prefill [--layers L] [--steps K] [--warmup W]
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--ctx C]
+  python bench.py --workload moe     [--layers L]   # the 36 MoE blocks only
+  python bench.py --workload gemv                    # config 2: dense dequant-GEMV sweep
+  python bench.py --workload qwen3   [--layers L]   # config 4 MoE blocks (Q4_K, top-8)
+  python bench.py --workload prefill [--layers L]   # config 5: 512-token prefill of the MoE blocks
 
-``--workload gemv`` measures the dense dequant-GEMV sweep instead (batch 1,
-K = 4096, N in {4096, 11008, 14336}, MXFP4 / Q4_K / Q8_0): one JSON line per
-case, HBM GB/s against the measured copy peak, weight copies rotated so that
-every launch streams from HBM.  ``--workload qwen3`` runs the decode step on
-the Qwen3-235B-A22B shape instead (94 MoE layers, hidden 4096, 128 experts,
-top-8, expert ffn 1536, Q4_K experts; MoE layers only).  ``--workload prefill``
-runs 512 prompt tokens through the GPT-OSS-shaped MoE layers (config 5), each
-layer as slices of a few tokens through the fused layer kernel.
+``--workload gemv`` prints one JSON line per case (batch 1, K = 4096, N in {4096, 11008, 14336},
+MXFP4 / Q4_K / Q8_0), HBM GB/s against the measured copy peak, weight copies rotated so that every
+launch streams from HBM.
 
-N > 1 runs expert parallel under torchrun (experts split by index, one NCCL
-all-reduce per layer).  ``--impl reference`` times the reference's CPU path
-(the oracle port of it; the reference is Python and is not shipped to the GPU
-box) on the host cores.  Prints ONE JSON line on rank 0.
+N > 1 runs expert parallel under torchrun (experts split by index, one NCCL all-reduce per layer,
+everything else replicated).  ``--impl reference`` times the reference's own CPU implementation
+(``GptOssModel.forward`` of the installed reference package, all layers every step) on the host
+cores; when the package is not installed it times the numpy oracle port instead.  Prints ONE JSON
+line on rank 0.
 """
 from __future__ import annotations
 
@@ -170,9 +169,22 @@ class ClockSampler:
             self.f = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
             self.proc = subprocess.Popen(
                 ["nvidia-smi", "-i", str(self.idx), f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                 "-lms", "100"], stdout=self.f, stderr=subprocess.DEVNULL)
+                 "-lms", "50"], stdout=self.f, stderr=subprocess.DEVNULL)
         except Exception:
             self.proc = None
+
+    def wait_first(self, timeout: float = 5.0) -> None:
+        """Block until the sampler has written its first row (so that short timed regions are covered)."""
+        if self.proc is None:
+            return
+        t0 = time.time()
+        while time.time() - t0 < timeout:
+            try:
+                if os.path.getsize(self.f.name) > 0:
+                    return
+            except OSError:
+                return
+            time.sleep(0.05)
 
     def stop(self):
         if self.proc is None:
@@ -342,6 +354,154 @@ def run_ours(args, rank, world, local_rank, group):
     return line
 
 
+def full_decode_config(shape, world, ctx):
+    return {
+        "workload": (f"gpt-oss-120b-shape full decode: embedding + {shape.n_layer} x (RMSNorm + bf16 q/k/v + YaRN RoPE "
+                     f"+ sink attention over {ctx} cached positions (sliding window {shape.sliding_window} on even "
+                     f"layers) + bf16 o-proj + MoE: RMSNorm + router top-{shape.n_expert_used}/{shape.n_expert} + "
+                     f"MXFP4 gate/up/down {shape.n_embd}x{shape.n_ffn_expert} + clamped SwiGLU + combine) + RMSNorm "
+                     f"+ LM head {shape.vocab_size}x{shape.n_embd}, batch 1"),
+        "model": "gpt-oss-120b shape (synthetic weights)", "layers": shape.n_layer, "hidden": shape.n_embd,
+        "heads": f"{shape.n_head}q/{shape.n_head_kv}kv x {shape.head_dim}", "experts": shape.n_expert,
+        "top_k": shape.n_expert_used, "vocab": shape.vocab_size, "context": ctx, "global_batch": 1, "seq_len": 1,
+        "expert_format": "MXFP4 (GGUF bytes, HBM-resident)", "dense_format": "bf16", "kv_cache": "fp32",
+        "parallelism": f"ep{world}" if world > 1 else "single",
+        "l2": "inputs larger than L2 (about 5 GB of weights per step, L2 126 MB)",
+    }
+
+
+def run_full_decode(args, rank, world, local_rank, group):
+    """Config 3: one whole GPT-OSS-120B-shaped decode token per step (``GptOssDecoder``, one CUDA graph).
+
+    ``value``: K graph replays back to back, CUDA events on the launching stream, token and position
+    already in HBM (the same token at position ``ctx`` every step, so every step is the same work).
+    ``e2e``: ``GptOssDecoder.decode`` per step -- token id and position copied in from pinned host
+    memory, the logits copied back out.  Roofline: the step's algorithmic bytes (every weight byte
+    the token needs once, KV history read, activations) over the step time.
+    """
+    import torch
+    import torch.distributed as dist
+
+    from nurostream_b200.gptoss import GptOssDecoder
+    from nurostream_b200.shapes import GptOssShape
+
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    shape = GptOssShape(n_layer=args.layers)
+    clocks = ClockSampler(local_rank)
+    dec = GptOssDecoder(shape, dev, seed=0, ctx=args.ctx, max_ctx=args.ctx + 64, rank=rank, world=world,
+                        group=group, use_graph=not args.no_graph)
+    token = 1234
+    dec.set_token(token, args.ctx)
+    graphed = dec.capture()
+    tok_host = torch.tensor([token], dtype=torch.int32).pin_memory()
+    pos_host = torch.tensor([args.ctx], dtype=torch.int32).pin_memory()
+    logits_host = torch.empty(shape.vocab_size, dtype=torch.float32).pin_memory()
+
+    def barrier():
+        if world > 1:
+            dist.barrier(group=group)
+
+    clocks.start()
+    clocks.wait_first()
+    for _ in range(args.warmup):
+        dec.step()
+    torch.cuda.synchronize()
+    dec.check_device_errors()
+    stream = torch.cuda.current_stream(dev)
+    barrier()
+    torch.cuda.synchronize()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ev0.record(stream)
+    for _ in range(args.steps):
+        dec.step()
+    ev1.record(stream)
+    torch.cuda.synchronize()
+    barrier()
+    ms = ev0.elapsed_time(ev1)
+    # end to end through the public API: token and position in from host memory, logits out, every step
+    barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        dec.decode(tok_host, logits_host, pos_host)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    barrier()
+    ms_e2e = e0.elapsed_time(e1)
+    clk = clocks.stop()
+    dec.check_device_errors()
+    ids_ok = True
+    if world > 1:
+        t = torch.tensor([ms, ms_e2e], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX, group=group)
+        ms, ms_e2e = float(t[0]), float(t[1])
+        gathered = [torch.empty_like(dec.ids) for _ in range(world)]
+        dist.all_gather(gathered, dec.ids, group=group)
+        ids_ok = all(torch.equal(g_, gathered[0]) for g_ in gathered)
+    parts = dec.bytes_per_token()
+    dec.release()
+    if rank != 0:
+        return None
+    step_ms = ms / args.steps
+    peak, peak_kind = measured_peaks()
+    achieved = parts["total"] / (step_ms / 1000.0) / 1e9
+    line = {
+        "metric": METRIC, "value": round(1000.0 / step_ms, 2), "unit": UNIT, "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(step_ms, 4), "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None,
+        "dtype": "bf16 dense + mxfp4 expert weights, fp32 activations and accumulation",
+        "data": "synthetic (seeded splitmix64 weights and KV history generated in HBM)",
+        "config": full_decode_config(shape, world, args.ctx),
+        "e2e": {"value": round(1000.0 * args.steps / ms_e2e, 2), "unit": UNIT, "h2d_bytes_per_step": 8,
+                "d2h_bytes_per_step": 4 * shape.vocab_size},
+        "gpu_launches": dec.launches_per_step * args.steps,
+        "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                     "frac": round(achieved / peak, 4), "traffic": None, "peak_kind": peak_kind,
+                     "kernel": "decode step: ns_embed + 36 x (dense_gemv_kernel q/k/v, attn_decode_kernel, "
+                               "dense_gemv_kernel o-proj, moe_tc_kernel) + dense_gemv_kernel LM head, one CUDA graph",
+                     "algorithmic_bytes_per_step": parts["total"],
+                     "bytes_by_part": {k: v for k, v in parts.items() if k != "total"},
+                     "launch_ms": round(step_ms, 5),
+                     "launch_ms_from": "CUDA events around the K graph replays of the timed region / K"},
+        "cuda_graph": graphed,
+        "routing_identical_on_all_ranks": ids_ok,
+    }
+    traffic = ROOT / "profiles" / "decode_step_traffic.json"
+    if traffic.exists():
+        try:
+            line["roofline"]["traffic"] = json.loads(traffic.read_text()).get("dram_bytes_per_step")
+        except Exception:
+            pass
+    if clk:
+        line["clocks"] = clk
+    if world == 1 and not args.no_cpu_baseline:
+        line["cpu_baseline"] = cpu_baseline_full(shape, args.ctx)
+    return line
+
+
+def cpu_baseline_full(shape, ctx):
+    """A bounded sample of the reference's own CPU decode: set-up, one warm-up token, two timed tokens."""
+    threads = cpu_cores()
+    if import_reference() is None:
+        mshape = shape.moe_shape()
+        tok_s, per_layer, _ = cpu_layer_sample(mshape, 2, threads)
+        return {"value": round(tok_s, 5), "unit": UNIT, "cores": threads, "kind": "port",
+                "sample": ("reference package not installed on this box: numpy oracle port of the MoE layers only, "
+                           f"2 layers x 3 reps (median layer {per_layer * 1000:.1f} ms) scaled to {mshape.n_layer}")}
+    t0 = time.perf_counter()
+    ref = ReferenceDecode(shape, ctx=ctx, dense=True, threads=threads)
+    ref.step()
+    setup = time.perf_counter() - t0
+    times = [ref.step() for _ in range(2)]
+    v = 1.0 / statistics.mean(times)
+    return {"value": round(v, 5), "unit": UNIT, "cores": threads, "kind": "reference",
+            "sample": (f"2 whole tokens (mean {statistics.mean(times):.2f} s) through the reference's own "
+                       f"GptOssModel.forward at {ctx} context on device='cpu', fp32, block_rows=512, "
+                       f"torch.set_num_threads({threads}); set-up + 1 warm-up token {setup:.0f} s untimed")}
+
+
 def run_gemv_sweep(args):
     """Dense dequant-GEMV at batch 1 (the reference's ``fused_gemv``, ``triton_kernels.py:199-228``).
 
@@ -502,42 +662,249 @@ def run_prefill(args):
     return line
 
 
-def run_reference(args, rank, world):
-    """The reference's own CPU implementation of the path (oracle port), host cores only.
+# ----------------------------------------------------------------------------- reference arm
 
-    Each step is a bounded sample: one token through one MoE layer (cycling
-    over `--ref-layers` prepared layers), scaled to the full layer count.  The
-    number of timed steps is capped so the run ends within a few minutes.
+def import_reference():
+    """Put the reference package on sys.path (NS_REFERENCE_PATH, else the copy installed in
+    baseline/_ref); returns its path, or None when it is not installed on this machine."""
+    for p in (os.environ.get("NS_REFERENCE_PATH"), str(ROOT / "baseline" / "_ref")):
+        if p and (Path(p) / "neurostream").is_dir():
+            sys.dont_write_bytecode = True
+            if p not in sys.path:
+                sys.path.insert(0, p)
+            import neurostream  # noqa: F401
+            return p
+    return None
+
+
+class SynthGGUF:
+    """A GGUF-shaped synthetic weight source for the reference's own CPU path.
+
+    It presents ``MmapSource``'s surface (``neurostream/io/source.py:65-133``): ``raw_bytes``,
+    ``fetch``, ``raw_rows`` and ``fetch_rows`` hand out a fresh copy of the tensor's bytes and decode
+    them with the reference's own ``dequantize``, as ``MmapSource`` does over a page-cached file.
+    The bytes are generated on first touch and kept (they stand for the model file's pages in the
+    host page cache): dense tensors whole, stacked expert tensors one expert window at a time.
+    Values follow the configuration's distributions -- bf16 N(0, 0.02) dense weights, fp32
+    N(0, 0.02) biases and sinks, unit norm weights, MXFP4 codes uniform with E8M0 exponents uniform
+    in [118, 124] -- drawn with seeded torch/numpy generators: the reference's time does not depend on
+    the values, so they need not equal the GPU arm's bit for bit.
+    """
+
+    def __init__(self, shape, dense: bool = True, n_layer: int | None = None):
+        import torch
+        from neurostream.format.gguf import GGMLType as T, TensorInfo, nbytes_for
+
+        c = shape
+        L = c.n_layer if n_layer is None else n_layer
+        H, q, kv, E, F, V = c.n_embd, c.q_dim, c.kv_dim, c.n_expert, c.n_ffn_expert, c.vocab_size
+        spec = {}
+        if dense:
+            spec["token_embd.weight"] = ((V, H), T.BF16, 0.02)
+            spec["output_norm.weight"] = ((H,), T.F32, None)
+            spec["output.weight"] = ((V, H), T.BF16, 0.02)
+        for l in range(L):
+            p = f"blk.{l}."
+            if dense:
+                spec[p + "attn_norm.weight"] = ((H,), T.F32, None)
+                for nm, rows, cols in (("attn_q", q, H), ("attn_k", kv, H), ("attn_v", kv, H), ("attn_output", H, q)):
+                    spec[p + nm + ".weight"] = ((rows, cols), T.BF16, 0.02)
+                    spec[p + nm + ".bias"] = ((rows,), T.F32, 0.02)
+                spec[p + "attn_sinks.weight"] = ((c.n_head,), T.F32, 1.0)
+            spec[p + "post_attention_norm.weight"] = ((H,), T.F32, None)
+            spec[p + "ffn_gate_inp.weight"] = ((E, H), T.BF16, 0.02)
+            spec[p + "ffn_gate_inp.bias"] = ((E,), T.F32, 0.02)
+            for kind, rows, cols in (("gate", F, H), ("up", F, H), ("down", H, F)):
+                spec[p + f"ffn_{kind}_exps.weight"] = ((E, rows, cols), T.MXFP4, "expert")
+                spec[p + f"ffn_{kind}_exps.bias"] = ((E, rows), T.F32, 0.02)
+        self._spec = spec
+        infos = {}
+        for name, (shp, dt, _) in spec.items():
+            n = int(np.prod(shp))
+            infos[name] = TensorInfo(name, tuple(reversed(shp)), dt, 0, nbytes_for(dt, n))
+        from types import SimpleNamespace
+        self.gguf = SimpleNamespace(tensors=infos)
+        self._mem: dict = {}
+        self._torch = torch
+        self._seed = {name: i + 1 for i, name in enumerate(spec)}
+
+    # bytes -------------------------------------------------------------------
+    def _dense(self, name) -> np.ndarray:
+        got = self._mem.get(name)
+        if got is None:
+            torch = self._torch
+            shp, dt, sigma = self._spec[name]
+            n = int(np.prod(shp))
+            if sigma is None:
+                v = torch.ones(n, dtype=torch.float32)
+            else:
+                g = torch.Generator().manual_seed(self._seed[name])
+                v = torch.randn(n, generator=g) * sigma
+            v = v.to(torch.bfloat16) if dt.name == "BF16" else v
+            got = self._mem[name] = v.view(torch.uint8).numpy()
+        return got
+
+    def _expert(self, name, e) -> np.ndarray:
+        key = (name, e)
+        got = self._mem.get(key)
+        if got is None:
+            info = self.gguf.tensors[name]
+            nbytes = info.nbytes // info.torch_shape[0]
+            rng = np.random.default_rng((self._seed[name] << 16) + e)
+            got = rng.integers(0, 256, nbytes, dtype=np.uint8)
+            got[0::17] = 118 + got[0::17] % 7                  # E8M0 scale byte of each 17-byte block
+            self._mem[key] = got
+        return got
+
+    def _raw(self, name, start, nbytes):
+        info = self.gguf.tensors[name]
+        if self._spec[name][2] == "expert":
+            per = info.nbytes // info.torch_shape[0]
+            e = start // per
+            if start + nbytes > (e + 1) * per:
+                raise ValueError("a read spans two experts")
+            arr = self._expert(name, e)[start - e * per: start - e * per + nbytes]
+        else:
+            arr = self._dense(name)[start:start + nbytes]
+        return self._torch.from_numpy(arr.copy())
+
+    # MmapSource surface --------------------------------------------------------
+    def raw_bytes(self, name):
+        return self._raw(name, 0, self.gguf.tensors[name].nbytes)
+
+    def fetch(self, name, device="cpu", dtype=None):
+        from neurostream.compute.quant import dequantize
+        info = self.gguf.tensors[name]
+        raw = self.raw_bytes(name).to(device)
+        flat = dequantize(raw, info.dtype, info.n_elements, out_dtype=dtype or self._torch.float32)
+        return flat.reshape(info.torch_shape)
+
+    def raw_rows(self, name, start, end):
+        from neurostream.io.source import row_geometry
+        n_rows, _, rb = row_geometry(self.gguf.tensors[name])
+        start, end = max(0, start), min(n_rows, end)
+        return self._raw(name, start * rb, (end - start) * rb)
+
+    def fetch_rows(self, name, start, end, device="cpu", dtype=None):
+        from neurostream.compute.quant import dequantize
+        from neurostream.io.source import row_geometry
+        torch = self._torch
+        dtype = dtype or torch.float32
+        info = self.gguf.tensors[name]
+        n_rows, elems, rb = row_geometry(info)
+        start, end = max(0, start), min(n_rows, end)
+        if start >= end:
+            return torch.empty((0, elems), dtype=dtype, device=device)
+        raw = self.raw_rows(name, start, end).to(device)
+        return dequantize(raw, info.dtype, (end - start) * elems, out_dtype=dtype).reshape(end - start, elems)
+
+
+class ReferenceDecode:
+    """The reference's own GPT-OSS decode on the host cores, ready to time one token at a time.
+
+    ``GptOssModel`` (``neurostream/model/gpt_oss.py``) over a ``TieredCache`` on ``device='cpu'``,
+    fp32, ``block_rows=512``: float tensors (embedding, attention, router, norms, biases, LM head)
+    admitted to the cache's resident float tier once, expert tensors served by the source one
+    neuron block at a time (``stream_expert_ffn``), exactly the reference's stock neuron-block
+    path.  The KV cache holds ``ctx`` synthetic positions per layer; each step decodes one token at
+    position ``ctx`` from that same cache (the appended position is dropped after the step), so
+    every step is the same work: one token at ``ctx`` context.
+    With ``dense=False`` a step is instead one token through the MoE blocks only
+    (``GptOssModel._ffn_block`` per layer), the workload of ``--workload moe``.
+    """
+
+    def __init__(self, shape, ctx: int = 2048, dense: bool = True, threads: int | None = None):
+        import torch
+        from neurostream.model.gpt_oss import GptOssConfig, GptOssModel
+        from neurostream.model.qwen3 import KVCache
+        from neurostream.residency.cache import TieredCache
+
+        if threads:
+            torch.set_num_threads(threads)
+        self.shape, self.ctx, self.dense = shape, ctx, dense
+        self.src = SynthGGUF(shape, dense=dense)
+        self.cache = TieredCache(self.src, device="cpu", compute_dtype=torch.float32, vram_budget=1 << 44)
+        for name, info in self.src.gguf.tensors.items():
+            if info.dtype.name in ("F32", "F16", "BF16"):
+                assert self.cache.admit_vram(name), name
+        cfg = GptOssConfig(**shape.reference_config())
+        self.model = GptOssModel(self.cache, cfg, device="cpu", dtype=torch.float32, block_rows=512)
+        g = torch.Generator().manual_seed(5)
+        self.k0 = [torch.randn(shape.n_head_kv, ctx, shape.head_dim, generator=g) for _ in range(shape.n_layer)]
+        self.v0 = [torch.randn(shape.n_head_kv, ctx, shape.head_dim, generator=g) for _ in range(shape.n_layer)]
+        self.kv = KVCache(shape.n_layer)
+        self.x = torch.randn(1, shape.n_embd, generator=g)
+        self.token = 1234
+        self._torch = torch
+
+    def step(self) -> float:
+        """Seconds for one token (the reset of the KV cache to ``ctx`` positions is not timed)."""
+        torch = self._torch
+        self.kv.k, self.kv.v = list(self.k0), list(self.v0)
+        self.kv.length = self.ctx
+        with torch.no_grad():
+            t0 = time.perf_counter()
+            if self.dense:
+                logits = self.model.forward(tokens=[self.token], kv=self.kv, start_pos=self.ctx)
+                _ = float(logits[0, 0])
+            else:
+                x = self.x
+                for l in range(self.shape.n_layer):
+                    x = self.model._ffn_block(x, l)
+                _ = float(x[0, 0])
+            return time.perf_counter() - t0
+
+
+def run_reference(args, rank, world):
+    """``--impl reference``: the reference's own CPU implementation of the workload on the host cores.
+
+    Every step is one whole token through the same model as the GPU arm (all layers, timed in
+    full).  Rank 0 alone runs it; other ranks exit without work.  When the reference package is
+    not installed on the box, the numpy oracle port of its MoE path is timed instead
+    (``kind: port``).
     """
     if rank != 0:
         return None
-    from nurostream_b200.decoder import MoeShape
+    from nurostream_b200.shapes import GptOssShape
 
-    shape = MoeShape(n_layer=args.layers)
+    shape = GptOssShape(n_layer=args.layers)
     threads = cpu_cores()
-    layers = [CpuLayer(shape, l) for l in range(args.ref_layers)]
-    times = []
-    budget_s, t_start = 150.0, time.perf_counter()
-    with ThreadPoolExecutor(max_workers=threads) as pool:
-        for i in range(args.warmup):
-            layers[i % len(layers)].run(pool)
-        for i in range(args.steps):
-            times.append(layers[i % len(layers)].run(pool))
-            if time.perf_counter() - t_start > budget_s:
-                break
-    s_per_tok = statistics.median(times) * shape.n_layer
-    v = 1.0 / s_per_tok
+    dense = args.workload != "moe"
+    cfg = full_decode_config(shape, world, args.ctx) if dense else workload_config(shape.moe_shape(), world)
+    metric = METRIC
+    if import_reference() is not None:
+        t_setup = time.perf_counter()
+        ref = ReferenceDecode(shape, ctx=args.ctx, dense=dense, threads=threads)
+        for _ in range(args.warmup):
+            ref.step()
+        setup_s = time.perf_counter() - t_setup
+        times = [ref.step() for _ in range(args.steps)]
+        kind = "reference"
+        sample = (f"every step one whole token through the reference's own GptOssModel "
+                  f"({'forward: embedding, ' + str(shape.n_layer) + ' x (attention at ' + str(args.ctx) + ' context + MoE), LM head' if dense else str(shape.n_layer) + ' x _ffn_block'}) "
+                  f"on device='cpu', fp32, block_rows=512, torch.set_num_threads({threads}); "
+                  f"set-up and {args.warmup} warm-up tokens {setup_s:.0f} s untimed")
+    else:
+        mshape = shape.moe_shape()
+        layers = [CpuLayer(mshape, l) for l in range(mshape.n_layer)]
+        times = []
+        with ThreadPoolExecutor(max_workers=threads) as pool:
+            for i in range(args.warmup):
+                layers[i % len(layers)].run(pool)
+            for _ in range(args.steps):
+                times.append(sum(L.run(pool) for L in layers))
+        kind = "port"
+        sample = ("reference package not installed on this box: every step one token through the numpy "
+                  f"oracle port of the reference's {mshape.n_layer} MoE layers (attention and LM head not "
+                  f"included), expert matrices on a {threads}-thread pool")
+    step_s = statistics.mean(times)
+    v = 1.0 / step_s
     return {
-        "metric": METRIC, "impl": "reference", "value": round(v, 5), "unit": UNIT, "n_gpus": world,
-        "steps": args.steps, "steps_timed": len(times), "warmup": args.warmup,
-        "ms_per_step": round(s_per_tok * 1000, 2), "higher_is_better": True, "scaling": "strong",
-        "vs_baseline": None, "dtype": "fp32", "data": "synthetic (seeded splitmix64 GGUF bytes)",
-        "config": workload_config(shape, world),
-        "cpu_baseline": {"value": round(v, 5), "unit": UNIT, "cores": threads, "kind": "port",
-                         "sample": (f"each step: one token through one of {len(layers)} prepared MoE layers "
-                                    f"(median over {len(times)} steps), scaled to {shape.n_layer} layers; "
-                                    "numpy oracle of the reference CPU path, expert matrices on a "
-                                    f"{threads}-thread pool")},
+        "metric": metric, "impl": "reference", "value": round(v, 5), "unit": UNIT, "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(step_s * 1000, 2),
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "fp32",
+        "data": "synthetic", "config": cfg,
+        "cpu_baseline": {"value": round(v, 5), "unit": UNIT, "cores": threads, "kind": kind, "sample": sample},
         "e2e": {"value": round(v, 5), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
 
@@ -553,7 +920,8 @@ def main():
     ap.add_argument("--ref-layers", type=int, default=2)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-graph", action="store_true")
-    ap.add_argument("--workload", choices=["decode", "gemv", "qwen3", "prefill"], default="decode")
+    ap.add_argument("--workload", choices=["decode", "moe", "gemv", "qwen3", "prefill"], default="decode")
+    ap.add_argument("--ctx", type=int, default=2048, help="KV-cache positions before the decoded token")
     ap.add_argument("--prefill-tokens", type=int, default=512)
     ap.add_argument("--gemv-case", default="", help="run one GEMV case only, e.g. MXFP4:14336")
     args = ap.parse_args()
@@ -584,7 +952,10 @@ def main():
             dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                     device_id=torch.device("cuda", local_rank))
             group = dist.group.WORLD
-        line = run_ours(args, rank, world, local_rank, group)
+        if args.workload == "decode":
+            line = run_full_decode(args, rank, world, local_rank, group)
+        else:
+            line = run_ours(args, rank, world, local_rank, group)
         if world > 1:
             import torch.distributed as dist
             dist.destroy_process_group()

@@ -77,7 +77,7 @@ enum ns_act_mode {
 /* Bits of the per-device error word. */
 #define NS_DEVERR_GRID_WAIT 1u  /* grid-wide barrier ran out */
 #define NS_DEVERR_COPY_WAIT 2u  /* bulk-copy completion wait ran out */
-#define NS_DEVERR_ROUTE 4u      /* routing produced an invalid expert id */
+#define NS_DEVERR_ROUTE 4u      /* an invalid expert id, token id or position */
 
 const char* ns_last_error(void);
 int ns_abi_version(void);
@@ -193,16 +193,97 @@ int ns_moe_decode_layer(const ns_moe_layer_t* p, void* workspace, size_t workspa
  *
  * Same computation and results as ns_moe_decode_layer; the scratch comes from
  * one fixed array of NS_MOE_STATIC_SCRATCH_BYTES linked into the library, one
- * per device.  A layer whose ns_moe_workspace_bytes exceeds that returns
- * NS_ERR_SIZE without launching (T=1, k=4, H=F=2880, 128 experts needs
- * 349,696).
- * The first call on a device (that device current) resolves and clears the
- * array and synchronises the device: make it before any stream capture.
+ * per device.  A call whose own scratch -- what the kernel chosen for this
+ * call's T needs, which can be less than ns_moe_workspace_bytes reports for a
+ * layer sized for up to T tokens -- exceeds that returns NS_ERR_SIZE without
+ * launching (T=1, k=4, H=F=2880, 128 experts needs 349,696).
+ * The first call on a device (that device current) resolves the array's
+ * address and clears its first 1 KiB (the grid-barrier word) with a
+ * synchronous memset: make it before any stream capture.  Every launch clears
+ * its own counters, so nothing else needs to start at zero.  The address is
+ * cached per device ordinal: cudaDeviceReset after the first call is not
+ * supported.
  * Calls that overlap on the GPU (unordered streams) race on the one array and
  * give wrong results; calls ordered on one stream are safe.
  */
 #define NS_MOE_STATIC_SCRATCH_BYTES (1024 * 1024)
 int ns_moe_decode_layer_static(const ns_moe_layer_t* p, ns_stream_t stream);
+
+/*
+ * Dense projection with bf16 weights, fp32 activations and fp32 accumulation
+ * (batch 1): for each segment s, y_s = residual_s + (W_s @ x' + bias_s), where
+ * x' = rms_norm(x, norm_w) (x * rsqrt(mean(x^2) + eps) * norm_w) when norm_w is
+ * given, else x.  Up to NS_DENSE_MAX_SEG matrices with the same K run as one
+ * launch over their concatenated rows (q, k and v of an attention block).
+ * Replaces neurostream/model/qwen3.py:169-194 `Qwen3Model._linear` on float
+ * weights (`x @ W.T`) and neurostream/model/gpt_oss.py:97-99 `_biased_linear`,
+ * with neurostream/compute/ops.py:14-20 `rms_norm` before it and the residual
+ * add of gpt_oss.py:101-114 after it.
+ * K a multiple of 8 up to 8192; w, x, norm_w 16-byte aligned.
+ */
+#define NS_DENSE_MAX_SEG 4
+typedef struct ns_dense_seg {
+  const void* w;          /* rows x K weights (w_dtype), row-major */
+  int rows;
+  const float* bias;      /* rows fp32, or NULL */
+  const float* residual;  /* rows fp32, or NULL */
+  float* y;               /* rows fp32 */
+} ns_dense_seg_t;
+
+typedef struct ns_dense_gemv {
+  int K;
+  int w_dtype;            /* NS_BF16 */
+  int n_seg;              /* 1..NS_DENSE_MAX_SEG */
+  ns_dense_seg_t seg[NS_DENSE_MAX_SEG];
+  const float* x;         /* K fp32 */
+  const float* norm_w;    /* K fp32 RMSNorm weight, or NULL */
+  float rms_eps;
+} ns_dense_gemv_t;
+
+int ns_dense_gemv(const ns_dense_gemv_t* p, ns_stream_t stream);
+
+/*
+ * One decode token of attention with sinks over an fp32 KV cache.
+ * Replaces the core of neurostream/model/gpt_oss.py:101-114
+ * `GptOssModel._attention_block`: apply_rope on q and the new key
+ * (neurostream/compute/ops.py:136-151), KVCache.append
+ * (neurostream/model/qwen3.py:74-85), repeat_kv (ops.py:154-159) and
+ * sink_attention (gpt_oss.py:73-87), with its sliding window.
+ * qkv: the un-rotated projection output, q (n_head*head_dim) then k then v
+ * (n_head_kv*head_dim each).  The token's position is read from device memory
+ * (*pos), so one captured graph serves every position; its key and value are
+ * written to cache slot *pos.  Keys kp with (window ? pos - window < kp : 0 <= kp)
+ * and kp <= pos are visible.  head_dim 64; at most 8 query heads per kv head.
+ */
+typedef struct ns_attn_decode {
+  int n_head;
+  int n_head_kv;
+  int head_dim;
+  int max_ctx;              /* positions each cache holds */
+  int window;               /* 0: full causal attention; > 0: sliding window */
+  float scale;              /* 1 / sqrt(head_dim) */
+  const int32_t* pos;       /* device int32: position of the token */
+  const float* qkv;         /* fp32 projection output (see above) */
+  const float* rope_cos;    /* max_ctx x head_dim fp32 (the model's RoPE / YaRN tables) */
+  const float* rope_sin;
+  const float* sinks;       /* n_head fp32 sink logits, or NULL */
+  float* k_cache;           /* n_head_kv x max_ctx x head_dim fp32 */
+  float* v_cache;
+  float* out;               /* n_head*head_dim fp32 */
+} ns_attn_decode_t;
+
+/* Workspace of ns_attn_decode: zeroed once (ns_moe_workspace_init clears any
+ * buffer); calls ordered on one stream may share one. */
+int ns_attn_workspace_bytes(const ns_attn_decode_t* p, size_t* bytes);
+int ns_attn_decode(const ns_attn_decode_t* p, void* workspace, size_t workspace_bytes, ns_stream_t stream);
+
+/*
+ * The embedding row of the token *token (device int32) widened to fp32:
+ * neurostream/model/qwen3.py:266-275 `Qwen3Model.embed` (`W[tokens]`).
+ * table: rows x H of dtype (NS_F32 / NS_F16 / NS_BF16).
+ */
+int ns_embed(const void* table, int dtype, int64_t rows, int H, const int32_t* token, float* out,
+             ns_stream_t stream);
 
 /*
  * Kernel choice of ns_moe_decode_layer (diagnostic and benchmarking aid; no

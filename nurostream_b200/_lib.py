@@ -50,6 +50,32 @@ class MoeLayerParams(C.Structure):
     ]
 
 
+NS_DENSE_MAX_SEG = 4
+
+
+class DenseSeg(C.Structure):
+    """Mirror of ns_dense_seg_t."""
+
+    _fields_ = [("w", C.c_void_p), ("rows", C.c_int), ("bias", C.c_void_p), ("residual", C.c_void_p),
+                ("y", C.c_void_p)]
+
+
+class DenseGemvParams(C.Structure):
+    """Mirror of ns_dense_gemv_t."""
+
+    _fields_ = [("K", C.c_int), ("w_dtype", C.c_int), ("n_seg", C.c_int), ("seg", DenseSeg * NS_DENSE_MAX_SEG),
+                ("x", C.c_void_p), ("norm_w", C.c_void_p), ("rms_eps", C.c_float)]
+
+
+class AttnDecodeParams(C.Structure):
+    """Mirror of ns_attn_decode_t."""
+
+    _fields_ = [("n_head", C.c_int), ("n_head_kv", C.c_int), ("head_dim", C.c_int), ("max_ctx", C.c_int),
+                ("window", C.c_int), ("scale", C.c_float), ("pos", C.c_void_p), ("qkv", C.c_void_p),
+                ("rope_cos", C.c_void_p), ("rope_sin", C.c_void_p), ("sinks", C.c_void_p),
+                ("k_cache", C.c_void_p), ("v_cache", C.c_void_p), ("out", C.c_void_p)]
+
+
 _P, _I, _I64, _U64, _SZ, _F = C.c_void_p, C.c_int, C.c_int64, C.c_uint64, C.c_size_t, C.c_float
 
 SIGNATURES = {
@@ -67,6 +93,10 @@ SIGNATURES = {
     "ns_synth_fill": (_I, [_P, _U64, _I, _U64, _U64, _U64, _F, _I, _I, _F, _P]),
     "ns_moe_set_trace": (_I, [_P, _SZ]),
     "ns_moe_select_kernel": (_I, [_I]),
+    "ns_dense_gemv": (_I, [C.POINTER(DenseGemvParams), _P]),
+    "ns_attn_workspace_bytes": (_I, [C.POINTER(AttnDecodeParams), C.POINTER(_SZ)]),
+    "ns_attn_decode": (_I, [C.POINTER(AttnDecodeParams), _P, _SZ, _P]),
+    "ns_embed": (_I, [_P, _I, _I64, _I, _P, _P, _P]),
 }
 
 _lib = None

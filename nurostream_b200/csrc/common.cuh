@@ -269,6 +269,14 @@ __device__ __host__ __forceinline__ uint32_t span_smem_bytes(uint64_t nbytes) {
   return (uint32_t)(((nbytes + 15 + 15) / 16) * 16);
 }
 
+// Programmatic dependent launch: wait until the previous grid of the stream has completed and its
+// memory is visible (a no-op when this grid was launched without the attribute); let the next grid's
+// CTAs be scheduled once every CTA of this grid has signalled or exited.
+__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void griddep_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+inline size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
+
 // ----------------------------------------------------------------------------- warp utilities
 
 __device__ __forceinline__ float warp_sum(float v) {

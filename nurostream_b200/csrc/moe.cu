@@ -962,7 +962,6 @@ static int dispatch_moe_t(const MoeArgs& a, int grid, size_t smem, cudaStream_t 
   return launch_moe<FMT, 8>(a, grid, smem, s);
 }
 
-static size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 
 // Trace buffer per device (host-side table, set by ns_moe_set_trace).
 static unsigned long long* g_trace_buf[64] = {nullptr};

@@ -3,6 +3,8 @@
 // relocatable device code.
 #include "abi.cu"
 #include "dequant.cu"
+#include "dense.cu"
+#include "attn.cu"
 #include "gemv.cu"
 #include "moe.cu"
 #include "synth.cu"

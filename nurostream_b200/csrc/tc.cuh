@@ -180,11 +180,6 @@ __device__ __forceinline__ void prefetch_tmap(const CUtensorMap* tmap) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(tmap)) : "memory");
 }
 
-// Programmatic dependent launch: wait until the previous grid of the stream has completed and its
-// memory is visible (a no-op when this grid was launched without the attribute); let the next grid's
-// CTAs be scheduled once every CTA of this grid has signalled or exited.
-__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
-__device__ __forceinline__ void griddep_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 
 __device__ __forceinline__ uint32_t ld_acquire_u32(const unsigned* p) {
   uint32_t v;

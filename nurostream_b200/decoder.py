@@ -15,61 +15,61 @@ adds the residual), and one all-reduce(sum) per layer over NCCL combines them.
 """
 from __future__ import annotations
 
-from dataclasses import dataclass
-
 import torch
 
 from . import _lib, synth
 from .ggml import GGMLType, row_bytes
 from .moe import MoeLayer
+from .shapes import MoeShape, expert_range  # noqa: F401  (re-exported)
 
 
-@dataclass
-class MoeShape:
-    n_layer: int = 36
-    hidden: int = 2880
-    expert_ffn: int = 2880
-    n_expert: int = 128
-    top_k: int = 4
-    ggml_type: int = int(GGMLType.MXFP4)
-    router_dtype: torch.dtype = torch.bfloat16
-    seed: int = 0
-    bias_sigma: float = 0.02
-    # "gpt-oss": RMSNorm, biased router, top-k then softmax, clamped SwiGLU, expert biases.
-    # "qwen3": no norm or biases, softmax then top-k renormalised, silu(gate) * up.
-    arch: str = "gpt-oss"
+def synth_moe_layer(sh: MoeShape, l: int, dev, lo: int, hi: int, max_tokens: int = 1) -> MoeLayer:
+    """MoE layer ``l`` of the synthetic model ``sh``, generated in HBM, holding experts [lo, hi).
 
-    @property
-    def expert_bytes(self) -> int:
-        """Bytes of one expert's gate + up + down matrices."""
-        t = GGMLType(self.ggml_type)
-        return 2 * self.expert_ffn * row_bytes(t, self.hidden) + self.hidden * row_bytes(t, self.expert_ffn)
-
-    def layer_bytes_per_token(self) -> int:
-        """Algorithmic bytes one layer reads/writes for one token (the roofline numerator)."""
-        H, F, E, k = self.hidden, self.expert_ffn, self.n_expert, self.top_k
-        gptoss = self.arch == "gpt-oss"
-        router = E * H * (2 if self.router_dtype == torch.bfloat16 else 4) + (4 * E if gptoss else 0)
-        experts = k * self.expert_bytes
-        biases = k * 4 * (2 * F + H) if gptoss else 0
-        acts = 4 * H * (3 if gptoss else 2)  # x in, norm weight (GPT-OSS), out
-        return router + experts + biases + acts
-
-
-def expert_range(rank: int, world: int, n_expert: int) -> tuple[int, int]:
-    """Experts [lo, hi) that rank `rank` of `world` holds: an even, contiguous split by index.
-
-    Each rank's share is one row window of every stacked expert tensor.  Rank 0 also adds the
-    residual, so summing the ranks' layer outputs gives the full layer.
+    GPT-OSS: norm weight 1 + 0.1 N(0,1), router (``sh.router_dtype``) N(0, 0.02) with an fp32 bias,
+    fp32 expert biases N(0, ``sh.bias_sigma``); Qwen3: router only.  The host twin of every tensor is
+    ``nurostream_b200.synth`` with the same (seed, stream, offset).
     """
-    if n_expert % world:
-        raise ValueError(f"{n_expert} experts do not split evenly over {world} ranks")
-    return rank * n_expert // world, (rank + 1) * n_expert // world
+    s = synth.LayerStreams(l)
+    H, F, E, t = sh.hidden, sh.expert_ffn, sh.n_expert, GGMLType(sh.ggml_type)
+    n_local = hi - lo
+
+    def quant(stream, rows, K):
+        rb = row_bytes(t, K)
+        buf = torch.empty(n_local * rows * rb, dtype=torch.uint8, device=dev)
+        synth.fill_quant(buf, t, sh.seed, stream, start=lo * rows * rb)
+        return buf
+
+    def flt(n, stream, sigma, dtype=torch.float32, start=0):
+        buf = torch.empty(n, dtype=dtype, device=dev)
+        synth.fill_float(buf, sh.seed, stream, start, sigma)
+        return buf
+
+    if sh.arch == "qwen3":
+        return MoeLayer(
+            H=H, F=F, n_expert=E, k=sh.top_k, ggml_type=t,
+            router_w=flt(E * H, s.router_w, 0.02, sh.router_dtype).reshape(E, H),
+            gate=quant(s.gate, F, H), up=quant(s.up, F, H), down=quant(s.down, H, F),
+            expert_lo=lo, expert_hi=hi, max_tokens=max_tokens,
+            route_mode=_lib.NS_ROUTE_SOFTMAX_TOPK_NORM, act_mode=_lib.NS_ACT_SILU_MUL,
+        )
+    norm = flt(H, s.norm_w, 0.1) + 1.0
+    return MoeLayer(
+        H=H, F=F, n_expert=E, k=sh.top_k, ggml_type=t,
+        router_w=flt(E * H, s.router_w, 0.02, sh.router_dtype).reshape(E, H),
+        router_b=flt(E, s.router_b, 0.02),
+        norm_w=norm,
+        gate=quant(s.gate, F, H), up=quant(s.up, F, H), down=quant(s.down, H, F),
+        gate_b=flt(n_local * F, s.gate_b, sh.bias_sigma, start=lo * F).reshape(n_local, F),
+        up_b=flt(n_local * F, s.up_b, sh.bias_sigma, start=lo * F).reshape(n_local, F),
+        down_b=flt(n_local * H, s.down_b, sh.bias_sigma, start=lo * H).reshape(n_local, H),
+        expert_lo=lo, expert_hi=hi, rms_eps=1e-5, max_tokens=max_tokens,
+    )
 
 
 class MoeDecoder:
     def __init__(self, shape: MoeShape, device: torch.device | str = "cuda", rank: int = 0, world: int = 1,
-                 group=None, use_graph: bool = True, max_tokens: int = 1):
+                 group=None, use_graph: bool = True, max_tokens: int = 1, keep_layer_outputs: bool = False):
         self.shape = shape
         self.max_tokens = max_tokens  # rows per fused launch (prefill runs slices of this many)
         self.device = torch.device(device)
@@ -78,7 +78,9 @@ class MoeDecoder:
         self.layers = [self._make_layer(l) for l in range(shape.n_layer)]
         H = shape.hidden
         self.x = torch.zeros((1, H), device=self.device, dtype=torch.float32)
-        self.bufs = [torch.empty((1, H), device=self.device, dtype=torch.float32) for _ in range(2)]
+        # two ping-pong output buffers, or one per layer when every layer's output is kept (tests)
+        nbuf = shape.n_layer if keep_layer_outputs else 2
+        self.bufs = [torch.empty((1, H), device=self.device, dtype=torch.float32) for _ in range(nbuf)]
         self.ids = torch.zeros((shape.n_layer, shape.top_k), device=self.device, dtype=torch.int32)
         self.out = None
         self.graph = None
@@ -86,48 +88,14 @@ class MoeDecoder:
         self.launches_per_step = shape.n_layer
 
     def _make_layer(self, l: int) -> MoeLayer:
-        s, sh, dev = synth.LayerStreams(l), self.shape, self.device
-        H, F, E, t = sh.hidden, sh.expert_ffn, sh.n_expert, GGMLType(sh.ggml_type)
-        n_local = self.hi - self.lo
-
-        def quant(stream, rows, K):
-            rb = row_bytes(t, K)
-            buf = torch.empty(n_local * rows * rb, dtype=torch.uint8, device=dev)
-            synth.fill_quant(buf, t, sh.seed, stream, start=self.lo * rows * rb)
-            return buf
-
-        def flt(n, stream, sigma, dtype=torch.float32, start=0):
-            buf = torch.empty(n, dtype=dtype, device=dev)
-            synth.fill_float(buf, sh.seed, stream, start, sigma)
-            return buf
-
-        if sh.arch == "qwen3":
-            return MoeLayer(
-                H=H, F=F, n_expert=E, k=sh.top_k, ggml_type=t,
-                router_w=flt(E * H, s.router_w, 0.02, sh.router_dtype).reshape(E, H),
-                gate=quant(s.gate, F, H), up=quant(s.up, F, H), down=quant(s.down, H, F),
-                expert_lo=self.lo, expert_hi=self.hi, max_tokens=self.max_tokens,
-                route_mode=_lib.NS_ROUTE_SOFTMAX_TOPK_NORM, act_mode=_lib.NS_ACT_SILU_MUL,
-            )
-        norm = flt(H, s.norm_w, 0.1) + 1.0
-        return MoeLayer(
-            H=H, F=F, n_expert=E, k=sh.top_k, ggml_type=t,
-            router_w=flt(E * H, s.router_w, 0.02, sh.router_dtype).reshape(E, H),
-            router_b=flt(E, s.router_b, 0.02),
-            norm_w=norm,
-            gate=quant(s.gate, F, H), up=quant(s.up, F, H), down=quant(s.down, H, F),
-            gate_b=flt(n_local * F, s.gate_b, sh.bias_sigma, start=self.lo * F).reshape(n_local, F),
-            up_b=flt(n_local * F, s.up_b, sh.bias_sigma, start=self.lo * F).reshape(n_local, F),
-            down_b=flt(n_local * H, s.down_b, sh.bias_sigma, start=self.lo * H).reshape(n_local, H),
-            expert_lo=self.lo, expert_hi=self.hi, rms_eps=1e-5, max_tokens=self.max_tokens,
-        )
+        return synth_moe_layer(self.shape, l, self.device, self.lo, self.hi, self.max_tokens)
 
     # ------------------------------------------------------------------ one token
 
     def _run_layers(self) -> torch.Tensor:
         cur = self.x
         for l, layer in enumerate(self.layers):
-            nxt = self.bufs[l % 2]
+            nxt = self.bufs[l % len(self.bufs)]
             layer(cur, out=nxt, add_residual=(self.rank == 0), ids=self.ids[l])
             if self.world > 1:
                 torch.distributed.all_reduce(nxt, group=self.group)

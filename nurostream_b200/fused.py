@@ -35,15 +35,21 @@ def stream_of(t: torch.Tensor) -> int:
     return torch.cuda.current_stream(t.device).cuda_stream
 
 
-def _kernels_available() -> bool:
-    try:
-        _lib.load()
-        return True
-    except Exception:
-        return False
+_HAVE: bool | None = None
 
 
-HAVE_KERNELS = _kernels_available()
+def kernels_available() -> bool:
+    """True once libns_b200.so loads; the first call loads it (not at import time)."""
+    global _HAVE
+    if _HAVE is None:
+        try:
+            _lib.load()
+            _HAVE = True
+        except Exception:
+            _HAVE = False
+    return _HAVE
+
+
 MAX_TOKENS = _lib.NS_MAX_TOKENS
 
 
@@ -54,12 +60,12 @@ def can_fuse(dtype, x: torch.Tensor) -> bool:
     except ValueError:
         return False
     return (
-        HAVE_KERNELS
-        and x.is_cuda
+        x.is_cuda
         and x.dim() >= 1
         and 1 <= (x.shape[0] if x.dim() > 1 else 1) <= MAX_TOKENS
         and t in FUSED_TYPES
         and x.dtype in _TORCH_TO_NS
+        and kernels_available()
     )
 
 

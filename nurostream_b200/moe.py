@@ -83,21 +83,16 @@ class MoeLayer:
         self.hi = n_expert if expert_hi is None else expert_hi
         n_local = self.hi - self.lo
         dev = router_w.device
-        f32 = lambda v: None if v is None else v.to(device=dev, dtype=torch.float32).contiguous()
-        self.router_w = router_w.contiguous()
-        self.router_b = f32(router_b)
-        self.norm_w = f32(norm_w)
-        self.gate_b, self.up_b, self.down_b = f32(gate_b), f32(up_b), f32(down_b)
-        for name, t, rows, K in (("gate", gate, F, H), ("up", up, F, H), ("down", down, H, F)):
-            need = n_local * rows * row_bytes(self.t, K)
-            if t.dtype != torch.uint8 or not t.is_cuda or t.numel() < need:
-                raise ValueError(f"{name}: expected >= {need} uint8 CUDA bytes, got {t.numel()} {t.dtype} {t.device}")
-        self.gate, self.up, self.down = gate.contiguous(), up.contiguous(), down.contiguous()
+        self.device = dev
+        self._src = {}
+        self.bind_small(router_w=router_w, router_b=router_b, norm_w=norm_w, gate_b=gate_b, up_b=up_b,
+                        down_b=down_b)
+        self.n_local = n_local
+        self.bind(gate, up, down)
         self.route_mode, self.act_mode = route_mode, act_mode
         self.alpha, self.limit, self.rms_eps = alpha, limit, rms_eps
         self.max_tokens = max_tokens
         self._slice = 0  # rows per launch that prefill settled on
-        self.device = dev
         p = self._params(max_tokens, None, None, True, None, None)
         n = C.c_size_t(0)
         _lib.call("ns_moe_workspace_bytes", C.byref(p), C.byref(n))
@@ -106,6 +101,36 @@ class MoeLayer:
         self._ws_ptr = self.workspace.data_ptr() + off
         self._ws_bytes = n.value
         _lib.call("ns_moe_workspace_init", self._ws_ptr, self._ws_bytes, stream_of(self.workspace))
+
+    def bind(self, gate: torch.Tensor, up: torch.Tensor, down: torch.Tensor) -> None:
+        """Point the layer at (new) stacked expert byte tensors; sizes are checked."""
+        H, F, n_local = self.H, self.F, self.n_local
+        for name, t, rows, K in (("gate", gate, F, H), ("up", up, F, H), ("down", down, H, F)):
+            need = n_local * rows * row_bytes(self.t, K)
+            if t.dtype != torch.uint8 or not t.is_cuda or t.numel() < need:
+                raise ValueError(f"{name}: expected >= {need} uint8 CUDA bytes, got {t.numel()} {t.dtype} {t.device}")
+        self.gate, self.up, self.down = gate.contiguous(), up.contiguous(), down.contiguous()
+
+    def bind_small(self, **tensors) -> None:
+        """(Re)bind router / norm / bias tensors; a tensor is converted (fp32, contiguous) only when
+        the caller hands a different tensor than last time."""
+        for name, v in tensors.items():
+            key = None if v is None else (v.data_ptr(), v.dtype, tuple(v.shape))
+            if name in self._src and self._src[name] == key:
+                continue
+            if v is None:
+                conv = None
+            elif name == "router_w":
+                conv = v.contiguous()
+            else:
+                conv = v.to(device=self.device, dtype=torch.float32).contiguous()
+            setattr(self, name, conv)
+            self._src[name] = key
+
+    def release_weights(self) -> None:
+        """Drop the references to the expert bytes (stream-ordered use already enqueued stays valid:
+        the caching allocator reuses freed blocks in stream order)."""
+        self.gate = self.up = self.down = None
 
     def _params(self, T, x, out, add_residual, ids, weights) -> _lib.MoeLayerParams:
         p = _lib.MoeLayerParams()
@@ -176,7 +201,13 @@ _ORIGINALS: dict = {}   # filled by nurostream_b200.install
 
 
 def _vram_payload(cache, name):
-    """Device bytes of a VRAM-Q resident tensor, or None (no host->device upload)."""
+    """(device bytes, type) of a VRAM-Q resident tensor, else None (never uploads host bytes).
+
+    Called on every layer call, like the reference's own ``_linear`` calls ``raw_quantized`` per
+    projection (``neurostream/model/qwen3.py:176-180``): the lookup refreshes the tensor's LRU position
+    and counts a VRAM hit (``neurostream/residency/cache.py:411-420``), so eviction sees hot expert
+    slabs as hot, and an evicted tensor is simply no longer found.
+    """
     vram = getattr(cache, "_vram", None)
     if vram is None or name not in vram:
         return None
@@ -186,76 +217,180 @@ def _vram_payload(cache, name):
     return hit
 
 
-def _stats(model):
+class DeferredRouterStats:
+    """``router_stats`` whose expert counts arrive from the device without stalling the host.
+
+    The reference's ``RouterStats`` (``neurostream/moe/router.py:27-56``) is updated inside every MoE
+    call with host-side ids, which costs one device->host synchronisation per layer.  Here each fused
+    layer call queues a non-blocking copy of its (T, k) ids into pinned host memory behind an event;
+    finished copies are folded into the counters at the next call (``event.query()``, no wait), and
+    every read of ``hits`` / ``tokens_routed`` / ``expert_reads`` (``pin_hot_experts``,
+    ``speculative_prefetch``, ``summary``) first folds everything still pending, waiting only for
+    copies not yet done.  The counts are the reference's: per layer call ``tokens_routed += T``, and
+    per distinct expert e ``hits[(layer, e)] += rows routed to e`` and ``expert_reads += 1``.
+    """
+
+    MAX_PENDING = 4096
+
+    def __init__(self, base=None):
+        if base is None:
+            try:
+                from neurostream.moe.router import RouterStats as RefStats  # the reference's own class
+                base = RefStats()
+            except Exception:
+                base = RouterStats()
+        object.__setattr__(self, "_base", base)
+        object.__setattr__(self, "_pending", [])
+
+    # -- queueing (fused path)
+    def defer(self, layer: int, ids: torch.Tensor) -> None:
+        host = torch.empty(ids.shape, dtype=ids.dtype, pin_memory=True)
+        host.copy_(ids, non_blocking=True)
+        ev = torch.cuda.Event()
+        ev.record(torch.cuda.current_stream(ids.device))
+        self._pending.append((layer, host, ev))
+        self.poll()
+
+    def poll(self, wait: bool = False) -> None:
+        pend = self._pending
+        n = 0
+        while n < len(pend):
+            layer, host, ev = pend[n]
+            if not (wait or len(pend) - n > self.MAX_PENDING or ev.query()):
+                break
+            ev.synchronize()
+            self._fold(layer, host.numpy())
+            n += 1
+        del pend[:n]
+
+    def _fold(self, layer, ids) -> None:
+        b = self._base
+        b.tokens_routed += int(ids.shape[0])
+        for e in sorted(set(ids.reshape(-1).tolist())):
+            b.hits[(layer, int(e))] += int((ids == e).any(axis=-1).sum())
+            b.expert_reads += 1
+
+    # -- the RouterStats surface
+    def __getattr__(self, name):
+        if name in ("hits", "tokens_routed", "expert_reads"):
+            self.poll(wait=True)
+        return getattr(self._base, name)
+
+    def __setattr__(self, name, value):
+        if name in ("hits", "tokens_routed", "expert_reads"):
+            self.poll(wait=True)
+        setattr(self._base, name, value)
+
+    def top_experts(self, layer: int, k: int = 8):
+        self.poll(wait=True)
+        return self._base.top_experts(layer, k)
+
+    def skew(self) -> float:
+        self.poll(wait=True)
+        return self._base.skew()
+
+    def summary(self) -> str:
+        self.poll(wait=True)
+        return self._base.summary()
+
+
+def _stats(model) -> DeferredRouterStats:
     stats = getattr(model, "router_stats", None)
-    if stats is None:
-        try:
-            from neurostream.moe.router import RouterStats as RefStats  # the reference's own class
-            stats = RefStats()
-        except Exception:
-            stats = RouterStats()
+    if not isinstance(stats, DeferredRouterStats):
+        stats = DeferredRouterStats(stats)
         model.router_stats = stats
     return stats
 
 
-def _layer_for(model, layer: int, gptoss: bool) -> MoeLayer | None:
-    cache = getattr(model, "_ns_layers", None)
-    if cache is None:
-        cache = model._ns_layers = {}
-    if layer in cache:
-        return cache[layer]
-    c = model.cfg
+def _lookup(model, layer: int, gptoss: bool):
+    """This call's tensors of ``layer`` from the cache, in the order the reference touches them.
+
+    The reference's neuron-block ``_ffn_block`` reads, per call: the norm weight, the router weight
+    and bias, then per routed expert gate rows, gate bias, up rows, up bias, down rows, down bias
+    (``neurostream/model/gpt_oss.py:123-170``, ``neurostream/compute/blockffn.py:434-449``).  Each
+    lookup refreshes that tensor's LRU position in the cache, so the fused path leaves the cache's
+    eviction order as the reference leaves it.  Returns (expert hits or None, small tensors).
+    """
     p = f"blk.{layer}."
-    hits = [_vram_payload(model.cache, p + f"ffn_{kind}_exps.weight") for kind in ("gate", "up", "down")]
-    if any(h is None for h in hits) or len({h[1] for h in hits}) != 1:
-        cache[layer] = None
+    small = {}
+    if gptoss:
+        small["norm_w"] = model.w(p + "post_attention_norm.weight")
+    small["router_w"] = model.w(p + "ffn_gate_inp.weight")
+    if gptoss:
+        small["router_b"] = model.w(p + "ffn_gate_inp.bias")
+    hits = []
+    for kind in ("gate", "up", "down"):
+        hits.append(_vram_payload(model.cache, p + f"ffn_{kind}_exps.weight"))
+        if gptoss:
+            small[f"{kind}_b"] = model.w(p + f"ffn_{kind}_exps.bias")
+    if any(h is None for h in hits) or len({int(h[1]) for h in hits}) != 1:
+        return None, small
+    return hits, small
+
+
+def _layer_for(model, layer: int, gptoss: bool) -> MoeLayer | None:
+    """The fused layer of ``layer``, bound to this call's VRAM-Q expert bytes, or None.
+
+    The tensors are looked up in the cache on every call (``_lookup``) and the MoeLayer is rebound
+    to them: between calls it keeps only converted copies of the small tensors and its workspace,
+    never the expert bytes, so an eviction frees them and the next call falls back to the
+    reference's streaming path.  Nothing is cached for a layer that is not resident.
+    """
+    c = model.cfg
+    hits, small = _lookup(model, layer, gptoss)
+    if hits is None:
         return None
     t = GGMLType(int(hits[0][1]))
     if t not in FUSED_TYPES:
-        cache[layer] = None
         return None
-    kw = {}
+    cache = getattr(model, "_ns_layers", None)
+    if cache is None:
+        cache = model._ns_layers = {}
+    lay = cache.get(layer)
+    if lay is not None and lay.t == t:
+        try:
+            lay.bind(hits[0][0], hits[1][0], hits[2][0])
+            lay.bind_small(**small)
+            return lay
+        except ValueError:
+            cache.pop(layer, None)
+    kw = dict(small)
     if gptoss:
-        kw.update(router_b=model.w(p + "ffn_gate_inp.bias"),
-                  norm_w=model.w(p + "post_attention_norm.weight"),
-                  gate_b=model.w(p + "ffn_gate_exps.bias"), up_b=model.w(p + "ffn_up_exps.bias"),
-                  down_b=model.w(p + "ffn_down_exps.bias"), rms_eps=c.rms_eps,
-                  route_mode=_lib.NS_ROUTE_TOPK_SOFTMAX, act_mode=_lib.NS_ACT_CLAMPED_SWIGLU)
+        kw.update(rms_eps=c.rms_eps, route_mode=_lib.NS_ROUTE_TOPK_SOFTMAX, act_mode=_lib.NS_ACT_CLAMPED_SWIGLU)
     else:
         kw.update(route_mode=_lib.NS_ROUTE_SOFTMAX_TOPK_NORM, act_mode=_lib.NS_ACT_SILU_MUL)
-    rw = model.w(p + "ffn_gate_inp.weight")
     try:
-        layer_obj = MoeLayer(H=c.n_embd, F=c.n_ffn_expert, n_expert=c.n_expert, k=c.n_expert_used,
-                             ggml_type=t, router_w=rw, gate=hits[0][0], up=hits[1][0], down=hits[2][0],
-                             max_tokens=_lib.NS_MAX_TOKENS, **kw)
-    except _lib.NsError:
-        layer_obj = None
-    cache[layer] = layer_obj
-    return layer_obj
+        lay = MoeLayer(H=c.n_embd, F=c.n_ffn_expert, n_expert=c.n_expert, k=c.n_expert_used,
+                       ggml_type=t, gate=hits[0][0], up=hits[1][0], down=hits[2][0],
+                       max_tokens=_lib.NS_MAX_TOKENS, **kw)
+    except (_lib.NsError, ValueError):
+        return None
+    cache[layer] = lay
+    return lay
 
 
 def _run_fused(model, layer_obj: MoeLayer, x: torch.Tensor, layer: int, add_residual: bool):
     T = x.shape[0]
     xf = x.to(torch.float32).contiguous()
     ids = torch.empty((T, layer_obj.k), device=x.device, dtype=torch.int32)
-    weights = torch.empty((T, layer_obj.k), device=x.device, dtype=torch.float32)
     try:
-        out = layer_obj.prefill(xf, add_residual=add_residual, ids=ids, weights=weights)
+        out = layer_obj.prefill(xf, add_residual=add_residual, ids=ids)
     except _lib.NsError as e:
         if e.status == -2:  # shape outside the fused kernel: use the streaming path
             return None
         raise
-    stats = _stats(model)
-    stats.tokens_routed += T
-    for e in sorted(set(ids.view(-1).tolist())):      # one device->host copy per layer
-        rows = int((ids == e).any(-1).sum())
-        stats.hits[(layer, e)] += rows
-        stats.expert_reads += 1
+    finally:
+        layer_obj.release_weights()
+    _stats(model).defer(layer, ids)
     return out.to(x.dtype)
 
 
 def gptoss_route(model, h: torch.Tensor, layer: int):
-    """Drop-in for ``GptOssModel._route``: (chosen list, ids (T,k), weights (T,k))."""
+    """Drop-in for ``GptOssModel._route``: (chosen list, ids (T,k), weights (T,k)).
+
+    The reference's contract returns the chosen experts as a Python list, which needs the ids on the
+    host; the fused ``_ffn_block`` does not call this.
+    """
     p = f"blk.{layer}."
     if not h.is_cuda:
         return _ORIGINALS["gptoss_route"](model, h, layer)

@@ -58,10 +58,18 @@ def stream_key(seed: int, stream: int) -> int:
 
 
 def words(key: int, start: int, count: int) -> np.ndarray:
-    """Words ``start .. start+count-1`` of the stream with this key."""
-    i = np.arange(start, start + count, dtype=np.uint64)
+    """Words ``start .. start+count-1`` of the stream with this key (in-place uint64 passes)."""
+    z = np.arange(start + 1, start + count + 1, dtype=np.uint64)
+    t = np.empty_like(z)
     with np.errstate(over="ignore"):
-        return _mix64(_U64(key) + (i + _U64(1)) * _U64(GAMMA))
+        np.multiply(z, _U64(GAMMA), out=z)
+        np.add(z, _U64(key), out=z)
+        for shift, mult in ((30, _M1), (27, _M2), (31, None)):
+            np.right_shift(z, _U64(shift), out=t)
+            np.bitwise_xor(z, t, out=z)
+            if mult is not None:
+                np.multiply(z, _U64(mult), out=z)
+    return z
 
 
 def _scale_fp16(key: int, idx: np.ndarray, scale_mult: float) -> np.ndarray:
@@ -116,9 +124,14 @@ def float_values(seed: int, stream: int, start: int, count: int, sigma: float = 
                  dtype=np.float32) -> np.ndarray:
     """Values ``[start, start+count)`` of a synthetic near-normal float tensor."""
     key = stream_key(seed, stream)
-    w = words(key, 12 * start, 12 * count).reshape(count, 12)
-    s = (w >> _U64(40)).astype(np.int64).sum(axis=1)             # exact integer sum
-    v = (s.astype(np.float64) * 2.0 ** -24 - 6.0).astype(np.float32)
+    v = np.empty(count, dtype=np.float32)
+    chunk = 1 << 16                                               # values per pass (cache-sized)
+    for c0 in range(0, count, chunk):
+        n = min(chunk, count - c0)
+        w = words(key, 12 * (start + c0), 12 * n)
+        np.right_shift(w, _U64(40), out=w)
+        s = w.reshape(n, 12).sum(axis=1, dtype=np.uint64)        # exact integer sum
+        v[c0:c0 + n] = (s.astype(np.float64) * 2.0 ** -24 - 6.0).astype(np.float32)
     v = v * np.float32(sigma)
     if dtype == np.float32:
         return v
@@ -148,6 +161,26 @@ class LayerStreams:
         self.gate_b = base + 13    # ffn_gate_exps.bias (E, F)
         self.up_b = base + 14      # ffn_up_exps.bias (E, F)
         self.down_b = base + 15    # ffn_down_exps.bias (E, H)
+        self.attn_norm = base + 20  # attn_norm.weight (H,)
+        self.q_w = base + 21        # attn_q.weight (n_head*hd, H), bf16
+        self.q_b = base + 22        # attn_q.bias
+        self.k_w = base + 23        # attn_k.weight (n_kv*hd, H), bf16
+        self.k_b = base + 24
+        self.v_w = base + 25        # attn_v.weight (n_kv*hd, H), bf16
+        self.v_b = base + 26
+        self.o_w = base + 27        # attn_output.weight (H, n_head*hd), bf16
+        self.o_b = base + 28
+        self.sinks = base + 29      # attn_sinks.weight (n_head,)
+        self.k_cache = base + 30    # synthetic key history (n_kv, ctx, hd)
+        self.v_cache = base + 31    # synthetic value history
+
+
+class ModelStreams:
+    """Stream ids of a synthetic model's tensors outside the layers."""
+
+    token_embd = 1       # token_embd.weight (vocab, H), bf16
+    output_norm = 2      # output_norm.weight (H,)
+    output = 3           # output.weight (vocab, H), bf16
 
 
 # ----------------------------------------------------------------------------- device fill

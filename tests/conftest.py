@@ -34,3 +34,20 @@ def pytest_collection_modifyitems(config, items):
     for item in items:
         if "gpu" in item.keywords:
             item.add_marker(skip)
+
+
+def reference_path():
+    """The reference package to test the drop-in against: NS_REFERENCE_PATH, else baseline/_ref."""
+    p = os.environ.get("NS_REFERENCE_PATH") or str(ROOT / "baseline" / "_ref")
+    return p if os.path.isdir(os.path.join(p, "neurostream")) else None
+
+
+@pytest.fixture
+def reference(monkeypatch):
+    """Puts the reference package on sys.path (skips when it is not installed on this machine)."""
+    p = reference_path()
+    if p is None:
+        pytest.skip("reference package not installed (baseline/_ref or NS_REFERENCE_PATH)")
+    monkeypatch.syspath_prepend(p)
+    sys.dont_write_bytecode = True
+    return p

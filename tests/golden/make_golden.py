@@ -258,10 +258,73 @@ def golden_moe(out_path: Path):
     np.savez_compressed(out_path, **arrays)
 
 
+# --------------------------------------------------------------------------- whole decode steps
+
+MODEL_CASE = dict(name="gptoss_2layer", n_layer=2, vocab_size=4096, seed=3, ctx=300,
+                  tokens=[17, 4000, 123])
+
+
+def golden_model(out_path: Path):
+    """The reference's own ``GptOssModel.forward`` decoding 3 tokens on a 2-layer GPT-OSS-120B-wide model.
+
+    Widths are GPT-OSS-120B's (hidden 2880, 64 query / 8 kv heads of 64, 128 experts top-4, expert
+    ffn 2880, YaRN RoPE, sliding window 128 on even layers) with 2 layers and a 4096-token
+    vocabulary; every tensor comes from ``tests.model_twin.model_tensors`` (the device generator's
+    host twin).  The KV cache starts with ``ctx`` synthetic positions; the tokens are decoded at
+    positions ctx, ctx+1, ctx+2 (each appending to the cache).  Stores the logits and, per token and
+    layer, the routed expert ids the reference's ``_route`` chose.
+    """
+    import torch
+    from neurostream.model.gpt_oss import GptOssConfig, GptOssModel
+    from neurostream.model.qwen3 import KVCache
+    from neurostream.residency.cache import TieredCache
+
+    from nurostream_b200.shapes import GptOssShape
+    from tests.model_twin import kv_history, model_tensors
+
+    c = MODEL_CASE
+    shape = GptOssShape(n_layer=c["n_layer"], vocab_size=c["vocab_size"])
+    src = SynthSource(model_tensors(shape, c["seed"]))
+    cache = TieredCache(src, vram_budget=1 << 40)
+    for name, info in src.gguf.tensors.items():
+        if info.dtype.name in ("F32", "BF16"):
+            assert cache.admit_vram(name)
+    model = GptOssModel(cache, GptOssConfig(**shape.reference_config()), block_rows=512)
+    routed = []
+    orig_route = GptOssModel._route
+
+    def recording_route(self, h, layer):
+        out = orig_route(self, h, layer)
+        routed.append(out[1].numpy().astype(np.int64).copy())
+        return out
+
+    kv = KVCache(shape.n_layer)
+    for l, (k, v) in kv_history(shape, c["seed"], c["ctx"]).items():
+        kv.k[l], kv.v[l] = torch.from_numpy(k.copy()), torch.from_numpy(v.copy())
+    kv.length = c["ctx"]
+    logits = []
+    GptOssModel._route = recording_route
+    try:
+        with torch.no_grad():
+            for i, tok in enumerate(c["tokens"]):
+                y = model.forward(tokens=[tok], kv=kv, start_pos=c["ctx"] + i)
+                logits.append(y.numpy().astype(np.float32).reshape(-1))
+    finally:
+        GptOssModel._route = orig_route
+    meta = dict(c)
+    arrays = {
+        f"{c['name']}__meta": np.frombuffer(json.dumps(meta).encode(), dtype=np.uint8),
+        f"{c['name']}__logits": np.stack(logits),
+        f"{c['name']}__ids": np.stack(routed).reshape(len(c["tokens"]), shape.n_layer, -1),
+    }
+    np.savez_compressed(out_path, **arrays)
+    print(f"model {c['name']}: logits[0,:3]={logits[0][:3]} ids={arrays[c['name'] + '__ids'].tolist()}")
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", required=True, help="path of the reference checkout")
-    ap.add_argument("--only", choices=["dequant", "gemv", "moe"], default=None)
+    ap.add_argument("--only", choices=["dequant", "gemv", "moe", "model"], default=None)
     args = ap.parse_args()
     _import_reference(args.reference)
     import torch
@@ -272,6 +335,8 @@ def main():
         golden_gemv(HERE / "gemv.npz")
     if args.only in (None, "moe"):
         golden_moe(HERE / "moe.npz")
+    if args.only in (None, "model"):
+        golden_model(HERE / "model.npz")
 
 
 if __name__ == "__main__":

@@ -107,3 +107,44 @@ def test_tc_path_refuses_layers_it_does_not_take(path):
     with pytest.raises(_lib.NsError) as e:
         layer(torch.from_numpy(L.x).cuda())
     assert e.value.status == -2
+
+
+def _bf16(a):
+    return torch.from_numpy(np.ascontiguousarray(a)).to(torch.bfloat16).float().numpy()
+
+
+@pytest.mark.parametrize("kw", [
+    dict(),                                                    # the benchmarked layer: E=128, H=F=2880, top-4
+    dict(T=2, E=64, seed=5),
+    dict(E=32, k=4, H=1024, F=512, seed=13),
+    dict(arch="qwen3moe", E=32, k=8, H=1024, F=512, bias=False, norm=None, T=2, seed=9),
+])
+def test_tc_layer_with_bf16_router_matches_oracle(path, kw):
+    """bf16 router weights (what the benchmark's decoder holds) on the tensor-core kernel; the oracle
+    routes with the same bf16-rounded weights widened to fp32."""
+    L = goldens.SynthLayer(_cfg(**kw))
+    layer = layer_from_synth(L, router_dtype=torch.bfloat16)
+    path(2)
+    out, ids, w = run_layer(layer, L.x, add_residual=L.gptoss)
+    L.router_w = _bf16(L.router_w)
+    o_out, o_ids, o_w = _oracle_layer(L)
+    np.testing.assert_array_equal(ids, o_ids)
+    np.testing.assert_allclose(w, o_w, rtol=2e-6, atol=1e-7)
+    assert_rel_close(out, o_out, 1e-3, f"bf16 router {kw}")
+    assert_rel_close(out, o_out, 2e-5, f"bf16 router {kw} (tight)")
+
+
+@pytest.mark.parametrize("order", [(1, 3, 1, 3), (3, 1, 3, 1)])
+def test_tensor_core_and_cuda_core_kernels_alternate_on_one_workspace(order):
+    """T <= 2 takes the tensor-core kernel and T = 3 the CUDA-core kernel; their scratch layouts
+    overlap in one workspace (barrier word, counters vs logits), so alternating them in either
+    order must leave every call correct."""
+    c = _cfg(E=16, k=4, H=512, F=512, T=3, seed=31)
+    L = goldens.SynthLayer(c)
+    layer = layer_from_synth(L, max_tokens=3)
+    for T in order:
+        sub = goldens.SynthLayer(dict(c, T=T))
+        out, ids, _ = run_layer(layer, sub.x, add_residual=True)
+        o_out, o_ids, _ = _oracle_layer(sub)
+        np.testing.assert_array_equal(ids, o_ids)
+        assert_rel_close(out, o_out, 2e-5, f"T={T} in order {order}")

@@ -2,6 +2,7 @@
 drop-in operator surface and the installer."""
 import importlib.util
 import os
+from pathlib import Path
 import sys
 
 import numpy as np
@@ -69,13 +70,12 @@ def test_row_bytes():
         row_bytes(GGMLType.Q4_K, 1000)
 
 
-REF = os.environ.get("NS_REFERENCE_PATH", "/root/reference")
+# the reference package: NS_REFERENCE_PATH, else the copy installed into baseline/_ref
+REF = os.environ.get("NS_REFERENCE_PATH") or str(Path(__file__).resolve().parents[1] / "baseline" / "_ref")
 
 
 def _reference_importable():
-    if not os.path.isdir(os.path.join(REF, "neurostream")):
-        return False
-    return importlib.util.find_spec("gguf") is not None
+    return os.path.isdir(os.path.join(REF, "neurostream"))
 
 
 @pytest.mark.skipif(not _reference_importable(), reason="reference package not present on this machine")
@@ -137,3 +137,47 @@ def test_prefill_slices_cover_every_row_and_halve_on_refusal():
     assert [c[0] for c in calls] == [2, 2, 1]
     with pytest.raises(_lib.NsError):         # a refusal at one row is an error, not a loop
         Fake(GGMLType.Q8_0, 8, 0).prefill(x)
+
+
+def test_dropin_touches_cache_in_reference_order(reference):
+    """The fused drop-in looks its tensors up in the order the reference's neuron-block _ffn_block
+    does, so the VRAM-Q LRU order after a call is the reference's."""
+    import torch as _t
+    from neurostream.model.gpt_oss import GptOssConfig, GptOssModel
+    from neurostream.residency.cache import TieredCache
+
+    from nurostream_b200 import moe
+    from tests import goldens
+    from tests.golden.make_golden import SynthSource, layer_tensors
+
+    c = goldens.cases(goldens.load("moe"))["gptoss_small_bias_t3"]
+    common = dict(n_layer=1, n_embd=c["H"], n_head=1, n_head_kv=1, head_dim=c["H"], n_ffn=c["F"], vocab_size=8,
+                  rms_eps=1e-5, rope_base=10000.0, context_length=4096, n_expert=c["E"], n_expert_used=c["k"],
+                  n_ffn_expert=c["F"])
+    orders = []
+    for use_dropin in (False, True):
+        src = SynthSource(layer_tensors(c))
+        cache = TieredCache(src, vram_budget=1 << 40)
+        for name in sorted(src.gguf.tensors, reverse=True):
+            assert cache.admit_vram(name)
+        model = GptOssModel(cache, GptOssConfig(**common), block_rows=c["block_rows"])
+        x = _t.from_numpy(goldens.SynthLayer(c).x.copy())
+        if use_dropin:
+            moe._lookup(model, 0, gptoss=True)
+        else:
+            model._ffn_block(x, 0)
+        orders.append(list(cache._vram))
+    assert orders[0] == orders[1]
+
+
+def test_deferred_router_stats_fold_like_the_reference():
+    """Folding (T, k) ids gives the reference's counters (moe/router.py:183-198)."""
+    from nurostream_b200.moe import DeferredRouterStats, RouterStats
+
+    st = DeferredRouterStats(RouterStats())
+    st._fold(3, np.array([[5, 1], [1, 7], [5, 1]]))
+    assert st.tokens_routed == 3
+    assert dict(st.hits) == {(3, 1): 3, (3, 5): 2, (3, 7): 1}
+    assert st.expert_reads == 3
+    st.tokens_routed += 2                      # what the reference's fallback path does
+    assert st.tokens_routed == 5

@@ -70,3 +70,31 @@ def test_moe_layer_matches_reference(name):
     np.testing.assert_allclose(w, g[f"{name}__weights"], rtol=1e-6, atol=1e-7)
     want = g[f"{name}__out"]
     np.testing.assert_allclose(out, want, rtol=1e-5, atol=1e-5 * np.abs(want).max())
+
+
+def test_oracle_model_matches_reference_forward():
+    """The oracle's whole decode step against the reference's own GptOssModel.forward: 3 tokens
+    on a 2-layer GPT-OSS-120B-wide model with a 300-position KV history (tests/golden/model.npz)."""
+    import time
+
+    from nurostream_b200.shapes import GptOssShape
+    from oracle import model as omodel
+    from tests import goldens
+    from tests.model_twin import TwinWeights, kv_history
+
+    g = goldens.load("model")
+    c = goldens.cases(g)["gptoss_2layer"]
+    shape = GptOssShape(n_layer=c["n_layer"], vocab_size=c["vocab_size"])
+    W = TwinWeights(shape, c["seed"])
+    kv = kv_history(shape, c["seed"], c["ctx"])
+    cfg = W.config()
+    t0 = time.time()
+    for i, tok in enumerate(c["tokens"]):
+        trace = []
+        logits = omodel.forward_token(tok, W, cfg, kv, c["ctx"] + i, trace=trace)
+        for l, (ids, _, _) in enumerate(trace):
+            np.testing.assert_array_equal(ids[0], g["gptoss_2layer__ids"][i, l], err_msg=f"token {i} layer {l}")
+        want = g["gptoss_2layer__logits"][i]
+        err = np.abs(logits[0] - want).max() / np.abs(want).max()
+        assert err < 1e-5, f"token {i}: oracle logits differ from the reference by {err:.2e}"
+    assert time.time() - t0 < 300

@@ -71,3 +71,25 @@ def test_static_scratch_rejects_layers_beyond_its_size():
     with pytest.raises(_lib.NsError, match="NS_MOE_STATIC_SCRATCH_BYTES") as e:
         _lib.call("ns_moe_decode_layer_static", C.byref(p), None)
     assert e.value.status == -3
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("order", [(1, 3, 1), (3, 1, 3)])
+def test_static_scratch_alternates_tensor_core_and_cuda_core_kernels(order):
+    """The two layer kernels share the one static array (T <= 2: tensor-core kernel, T = 3: CUDA-core
+    kernel); alternating them on it, in either order, matches the workspace entry point each time."""
+    c = dict(name="alt", arch="gpt-oss", type=39, E=16, H=512, F=512, k=4, T=3, seed=31, bias=True,
+             norm="random", block_rows=512)
+    layer = layer_from_synth(goldens.SynthLayer(c), max_tokens=3)
+    stream = torch.cuda.current_stream().cuda_stream
+    for T in order:
+        x = torch.from_numpy(goldens.SynthLayer(dict(c, T=T)).x.copy()).cuda()
+        want = torch.empty_like(x)
+        p = layer._params(T, x, want, True, None, None)
+        _lib.call("ns_moe_decode_layer", C.byref(p), layer._ws_ptr, layer._ws_bytes, stream)
+        got = torch.full_like(x, float("nan"))
+        p = layer._params(T, x, got, True, None, None)
+        _lib.call("ns_moe_decode_layer_static", C.byref(p), stream)
+        torch.cuda.synchronize()
+        assert _lib.device_error() == 0
+        assert_rel_close(got.cpu().numpy(), want.cpu().numpy(), 1e-3, f"static T={T} in order {order}")
