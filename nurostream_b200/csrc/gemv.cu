@@ -372,8 +372,8 @@ extern "C" int ns_gemv(const uint8_t* w, size_t w_bytes, int ggml_type, int n_ro
                        ns_stream_t stream) {
   using namespace ns;
   if (ggml_type != NS_GGML_MXFP4 && ggml_type != NS_GGML_Q8_0 && ggml_type != NS_GGML_Q4_K &&
-      ggml_type != NS_GGML_Q6_K)
-    return fail(NS_ERR_UNSUPPORTED, "ns_gemv: ggml type %d has no fused GEMV (MXFP4, Q8_0, Q4_K, Q6_K)",
+      ggml_type != NS_GGML_Q6_K && ggml_type != NS_GGML_Q5_K && ggml_type != NS_GGML_Q4_0)
+    return fail(NS_ERR_UNSUPPORTED, "ns_gemv: ggml type %d has no fused GEMV (MXFP4, Q8_0, Q4_K, Q5_K, Q6_K, Q4_0)",
                 ggml_type);
   if (n_rows < 0 || K <= 0 || T < 1 || T > NS_MAX_TOKENS)
     return fail(NS_ERR_INVALID, "ns_gemv: bad shape n_rows=%d K=%d T=%d (T must be 1..%d)", n_rows, K, T,
@@ -424,6 +424,8 @@ extern "C" int ns_gemv(const uint8_t* w, size_t w_bytes, int ggml_type, int n_ro
     case NS_GGML_MXFP4: return dispatch_gemv_t<NS_GGML_MXFP4>(a, tile, grid, smem, s);
     case NS_GGML_Q8_0: return dispatch_gemv_t<NS_GGML_Q8_0>(a, tile, grid, smem, s);
     case NS_GGML_Q4_K: return dispatch_gemv_t<NS_GGML_Q4_K>(a, tile, grid, smem, s);
+    case NS_GGML_Q5_K: return dispatch_gemv_t<NS_GGML_Q5_K>(a, tile, grid, smem, s);
+    case NS_GGML_Q4_0: return dispatch_gemv_t<NS_GGML_Q4_0>(a, tile, grid, smem, s);
     default: return dispatch_gemv_t<NS_GGML_Q6_K>(a, tile, grid, smem, s);
   }
 }

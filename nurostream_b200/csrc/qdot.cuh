@@ -7,6 +7,10 @@
 //   Q8_0   block g (34 B): fp16 d + 32 int8.
 //   Q4_K   superblock g/8 (144 B), sub-block s = g%8: 32 bytes of qs at
 //          16 + 32*(s/2), nibble s%2; 6-bit scale/min from the 12 scale bytes.
+//   Q5_K   superblock g/8 (176 B), sub-block s = g%8: as Q4_K with qs at 48 + 32*(s/2) and the
+//          fifth bit of element l in bit s of qh byte 16 + l.
+//   Q4_0   block g (18 B): fp16 d + 16 bytes; byte j holds element j (low nibble) and
+//          j+16 (high nibble), both stored +8.
 //   Q6_K   superblock g/8 (210 B), half h = (g/4)%2, lane i = g%4: ql bytes at
 //          64h + 32*(i%2) (nibble i/2), qh bytes at 128 + 32h (bits 2i..2i+1),
 //          int8 scales at 192 + 8h + 2i (+1 for the second 16 elements), fp16 d at 208.
@@ -212,6 +216,93 @@ struct QGroup<NS_GGML_Q4_K> {
 };
 
 template <>
+struct QGroup<NS_GGML_Q5_K> {
+  static constexpr int kParts = 1;
+  uint32_t q[8];  // 5-bit codes 0..31, one per byte
+  float dsc, mmn;
+
+  // neurostream/compute/quant.py:59-81: d*sc*q - dmin*mn with q = nibble + 16 * (qh bit)
+  __device__ __forceinline__ void load(const uint8_t* row, int g) {
+    const uint8_t* p = row + 176 * (g >> 3);
+    const int s = g & 7;
+    uint32_t hd[4];
+    lds_words_unaligned<4>(p, hd);  // d | dmin | scales[0..11]
+    QGroup<NS_GGML_Q4_K> k4;
+    k4.scales(hd[0], hd[1], hd[2], hd[3], s);
+    dsc = k4.dsc;
+    mmn = k4.mmn;
+    uint32_t w[8], h[8];
+    lds_words_unaligned<8>(p + 48 + 32 * (s >> 1), w);
+    lds_words_unaligned<8>(p + 16, h);
+    const unsigned sh = (s & 1) ? 4u : 0u;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) q[i] = ((w[i] >> sh) & 0x0F0F0F0Fu) | (((h[i] >> (unsigned)s) & 0x01010101u) << 4);
+  }
+  template <int NT, int XG = 32>
+  static __device__ __forceinline__ void load_x(const float* x, int64_t xs, const int (&tok)[NT], int nt, int g,
+                                                int s, float (&xv)[NT][8]) {
+    QGroup<NS_GGML_Q8_0>::load_x<NT, XG>(x, xs, tok, nt, g, s, xv);
+  }
+  template <int NT>
+  __device__ __forceinline__ void fma(int s, const float (&xv)[NT][8], int nt, float (&part)[NT][kParts]) const {
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      float f = byte_as_float(q[2 * s + (j >> 2)], j & 3, k2p23);
+#pragma unroll
+      for (int t = 0; t < NT; ++t)
+        if (t < nt) part[t][0] = fmaf(xv[t][j], f, part[t][0]);
+    }
+  }
+  template <int NT>
+  __device__ __forceinline__ void finish(const float (&part)[NT][kParts], const float (&xsum)[NT], int nt,
+                                         float (&acc)[NT]) const {
+#pragma unroll
+    for (int t = 0; t < NT; ++t)
+      if (t < nt) acc[t] = fmaf(-mmn, xsum[t], fmaf(part[t][0], dsc, acc[t]));
+  }
+};
+
+template <>
+struct QGroup<NS_GGML_Q4_0> {
+  static constexpr int kParts = 1;
+  uint32_t q[4];  // payload bytes 0..15
+  float d;
+
+  // neurostream/compute/quant.py:118-126: d * (nibble - 8)
+  __device__ __forceinline__ void load(const uint8_t* row, int g) {
+    uint32_t w[5];
+    lds_words_unaligned<5>(row + 18 * g, w);
+    d = f16_bits_to_float(w[0]);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) q[i] = __funnelshift_r(w[i], w[i + 1], 16);
+  }
+  // sub-chunk s: payload bytes 4s..4s+3 -> elements {4s+i, 16+4s+i} (the MXFP4 pairing)
+  template <int NT, int XG = 32>
+  static __device__ __forceinline__ void load_x(const float* x, int64_t xs, const int (&tok)[NT], int nt, int g,
+                                                int s, float (&xv)[NT][8]) {
+    QGroup<NS_GGML_MXFP4>::load_x<NT, XG>(x, xs, tok, nt, g, s, xv);
+  }
+  template <int NT>
+  __device__ __forceinline__ void fma(int s, const float (&xv)[NT][8], int nt, float (&part)[NT][kParts]) const {
+    const uint32_t lo = q[s] & 0x0F0F0F0Fu, hi = (q[s] >> 4) & 0x0F0F0F0Fu;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float fl = byte_as_float(lo, i, k2p23 + 8.0f), fh = byte_as_float(hi, i, k2p23 + 8.0f);
+#pragma unroll
+      for (int t = 0; t < NT; ++t)
+        if (t < nt) part[t][0] = fmaf(xv[t][2 * i + 1], fh, fmaf(xv[t][2 * i], fl, part[t][0]));
+    }
+  }
+  template <int NT>
+  __device__ __forceinline__ void finish(const float (&part)[NT][kParts], const float (&)[NT], int nt,
+                                         float (&acc)[NT]) const {
+#pragma unroll
+    for (int t = 0; t < NT; ++t)
+      if (t < nt) acc[t] = fmaf(part[t][0], d, acc[t]);
+  }
+};
+
+template <>
 struct QGroup<NS_GGML_Q6_K> {
   static constexpr int kParts = 2;  // elements 0..15 and 16..31 have their own scale
   uint32_t q[8];
@@ -296,7 +387,7 @@ __device__ __forceinline__ void dot_rows(const uint8_t* const (&rows)[R], int nr
     for (int s = 0; s < 4; ++s) {
       float xv[NT][8];
       G::template load_x<NT, XG>(x, xs, tok, nt, g, s, xv);
-      if (FMT == NS_GGML_Q4_K) {
+      if (FMT == NS_GGML_Q4_K || FMT == NS_GGML_Q5_K) {
 #pragma unroll
         for (int t = 0; t < NT; ++t)
           if (t < nt)

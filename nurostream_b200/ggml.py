@@ -36,9 +36,14 @@ TYPE_LAYOUT: dict[GGMLType, tuple[int, int]] = {
     GGMLType.Q6_K: (256, 210),
 }
 
-# Quantized formats the fused GEMV reads directly (the reference's Triton set,
-# ``neurostream/compute/triton_kernels.py:177-186``).
-FUSED_TYPES = frozenset({GGMLType.MXFP4, GGMLType.Q8_0, GGMLType.Q4_K, GGMLType.Q6_K})
+# Quantized formats the fused GEMV reads directly: the reference's Triton set
+# (``neurostream/compute/triton_kernels.py:177-186``: MXFP4, Q8_0, Q4_K, Q6_K) plus Q5_K and Q4_0,
+# which the reference can only dequantize (``neurostream/compute/quant.py:59-81, 118-126``).
+FUSED_TYPES = frozenset({GGMLType.MXFP4, GGMLType.Q8_0, GGMLType.Q4_K, GGMLType.Q6_K, GGMLType.Q5_K,
+                         GGMLType.Q4_0})
+
+# Expert formats of the fused MoE layer (ns_moe_decode_layer).
+MOE_TYPES = frozenset({GGMLType.MXFP4, GGMLType.Q8_0, GGMLType.Q4_K, GGMLType.Q6_K})
 
 # Formats the device dequantizer expands (``neurostream/compute/quant.py:143-150``
 # plus the three float types handled inline at ``quant.py:166-171``).

@@ -24,7 +24,7 @@ import torch
 
 from . import _lib
 from .fused import ns_dtype, stream_of
-from .ggml import FUSED_TYPES, GGMLType, as_ggml_type, row_bytes
+from .ggml import MOE_TYPES, GGMLType, as_ggml_type, row_bytes
 
 
 @dataclass
@@ -76,7 +76,7 @@ class MoeLayer:
                  route_mode: int = _lib.NS_ROUTE_TOPK_SOFTMAX, act_mode: int = _lib.NS_ACT_CLAMPED_SWIGLU,
                  alpha: float = 1.702, limit: float = 7.0, rms_eps: float = 1e-5, max_tokens: int = 1):
         self.t = as_ggml_type(ggml_type)
-        if self.t not in FUSED_TYPES:
+        if self.t not in MOE_TYPES:
             raise NotImplementedError(f"no fused MoE kernel for {self.t.name}")
         self.H, self.F, self.E, self.k = H, F, n_expert, k
         self.lo = expert_lo
@@ -341,7 +341,7 @@ def _layer_for(model, layer: int, gptoss: bool) -> MoeLayer | None:
     if hits is None:
         return None
     t = GGMLType(int(hits[0][1]))
-    if t not in FUSED_TYPES:
+    if t not in MOE_TYPES:
         return None
     cache = getattr(model, "_ns_layers", None)
     if cache is None:

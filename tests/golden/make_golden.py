@@ -158,6 +158,10 @@ GEMV_CASES = [
     ("q6_k_13x512", GGMLType.Q6_K, 13, 512, 1, 14, 512),
     ("mxfp4_t3_600x1024", GGMLType.MXFP4, 600, 1024, 3, 15, 512),
     ("q4_k_t2_1x256", GGMLType.Q4_K, 1, 256, 2, 16, 512),
+    ("q5_k_29x1024", GGMLType.Q5_K, 29, 1024, 1, 17, 512),
+    ("q4_0_21x2880", GGMLType.Q4_0, 21, 2880, 1, 18, 512),
+    ("q5_k_t3_300x512", GGMLType.Q5_K, 300, 512, 3, 19, 128),
+    ("q4_0_t2_70x1024", GGMLType.Q4_0, 70, 1024, 2, 20, 32),
 ]
 
 

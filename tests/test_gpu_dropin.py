@@ -112,7 +112,8 @@ def test_reference_moe_ffn_runs_fused_and_matches_golden(reference):
         assert dict(model.router_stats.hits) == _expected_hits(g[f"{name}__ids"])
 
 
-@pytest.mark.parametrize("case", ["mxfp4_19x2880", "q8_0_19x2880", "q4_k_37x4096", "q6_k_13x512",
+@pytest.mark.parametrize("case", ["mxfp4_19x2880", "q8_0_19x2880", "q4_k_37x4096", "q6_k_13x512", "q5_k_29x1024",
+                                  "q4_0_21x2880", "q5_k_t3_300x512",
                                   "mxfp4_t3_600x1024"])
 def test_reference_stream_linear_and_linear_on_ns_gemv(reference, case):
     import nurostream_b200

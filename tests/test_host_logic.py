@@ -45,12 +45,13 @@ def test_can_fuse_gates_on_device_and_type():
     assert not fused.can_fuse(GGMLType.MXFP4, x)            # CPU tensor
     assert not fused.can_fuse(GGMLType.Q5_K, x)
     assert not fused.can_fuse(12345, x)
-    assert FUSED_TYPES == {GGMLType.MXFP4, GGMLType.Q8_0, GGMLType.Q4_K, GGMLType.Q6_K}
+    assert FUSED_TYPES == {GGMLType.MXFP4, GGMLType.Q8_0, GGMLType.Q4_K, GGMLType.Q6_K, GGMLType.Q5_K,
+                           GGMLType.Q4_0}
 
 
 def test_fused_gemv_errors_like_reference():
     with pytest.raises(KeyError):
-        fused.fused_gemv(torch.zeros(176, dtype=torch.uint8), GGMLType.Q5_K, torch.zeros(1, 256), 1, 256)
+        fused.fused_gemv(torch.zeros(512, dtype=torch.uint8), GGMLType.BF16, torch.zeros(1, 256), 1, 256)
     with pytest.raises(TypeError):
         fused.fused_gemv(torch.zeros(17, dtype=torch.uint8), GGMLType.MXFP4, torch.zeros(1, 32), 1, 32)
 

@@ -38,8 +38,8 @@ def _err(lib):
 
 
 def test_gemv_rejects_bad_arguments_before_launching(lib):
-    # unsupported type (Q5_K has no fused GEMV, like the reference's _KERNELS)
-    assert lib.ns_gemv(1, 176, int(GGMLType.Q5_K), 1, 256, 1, 0, 256, 1, 1, 0, 1, None) == -2
+    # unsupported type (a float type has no fused GEMV, like the reference's _KERNELS)
+    assert lib.ns_gemv(1, 512, int(GGMLType.BF16), 1, 256, 1, 0, 256, 1, 1, 0, 1, None) == -2
     assert "no fused GEMV" in _err(lib)
     # T outside 1..8
     assert lib.ns_gemv(1, 4352, int(GGMLType.Q8_0), 1, 4096, 1, 0, 4096, 9, 1, 0, 1, None) == -1
@@ -107,7 +107,7 @@ def test_synth_fill_validation(lib):
 
 def test_errors_raise_with_message():
     with pytest.raises(_lib.NsError, match="no fused GEMV"):
-        _lib.call("ns_gemv", 1, 176, int(GGMLType.Q5_K), 1, 256, 1, 0, 256, 1, 1, 0, 1, None)
+        _lib.call("ns_gemv", 1, 512, int(GGMLType.BF16), 1, 256, 1, 0, 256, 1, 1, 0, 1, None)
 
 
 def test_missing_library_fails_loudly(tmp_path):
