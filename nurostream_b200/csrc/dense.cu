@@ -259,7 +259,10 @@ __global__ void __launch_bounds__(kDenseThreads, 1) dense_gemv_kernel(DenseArgs 
 template <int NCH>
 static int launch_dense(const DenseArgs& a, int grid, size_t smem, cudaStream_t s) {
   auto kern = dense_gemv_kernel<NCH>;
-  NS_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+  // the kernel's whole budget, not this launch's size: one function serves launches of several sizes,
+  // and a captured graph replays each of them against the attribute's value at replay time
+  NS_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                   (int)std::max(smem, (size_t)kDenseSmemBudget)));
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(grid);
   cfg.blockDim = dim3(kDenseThreads);

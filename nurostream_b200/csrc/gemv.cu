@@ -350,7 +350,9 @@ __global__ void __launch_bounds__((W + 1) * 32, 1) gemv_kernel(GemvArgs a) {
 template <int FMT, int NT, int TILE, int W, int RS>
 static int launch_gemv(const GemvArgs& a, int grid, size_t smem, cudaStream_t stream) {
   auto kern = gemv_kernel<FMT, NT, TILE, W, RS>;
-  NS_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+  // the kernel's whole budget, not this launch's size (see dense.cu: graphs replay against the attribute)
+  NS_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                   (int)std::max(smem, (size_t)kSmemBudget)));
   kern<<<grid, (W + 1) * 32, smem, stream>>>(a);
   NS_CUDA_TRY(cudaGetLastError());
   return NS_OK;

@@ -936,7 +936,9 @@ __global__ void __launch_bounds__(kMoeThreads, 1) moe_layer_kernel(MoeArgs a) {
 template <int FMT, int NT>
 static int launch_moe(const MoeArgs& a, int grid, size_t smem, cudaStream_t stream) {
   auto kern = moe_layer_kernel<FMT, NT>;
-  NS_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+  // the kernel's whole budget, not this launch's size (see dense.cu: graphs replay against the attribute)
+  NS_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                   (int)std::max(smem, (size_t)kMoeSmemBudget)));
   int per_sm = 0;
   NS_CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kMoeThreads, smem));
   if (per_sm < 1) return fail(NS_ERR_UNSUPPORTED, "ns_moe_decode_layer: kernel does not fit on an SM");

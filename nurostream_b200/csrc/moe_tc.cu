@@ -1225,7 +1225,9 @@ static bool g_tc_pdl = true;  // programmatic dependent launch accepted so far
 template <int NT>
 static int launch_moe_tc(const MoeTcArgs& a, int grid, size_t smem, cudaStream_t stream) {
   auto kern = moe_tc_kernel<NT>;
-  NS_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+  // the kernel's whole budget, not this launch's size (see dense.cu: graphs replay against the attribute)
+  NS_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                   (int)std::max(smem, (size_t)kTcSmemBudget)));
   int per_sm = 0;
   NS_CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kTcThreads, smem));
   if (per_sm < 1) return fail(NS_ERR_UNSUPPORTED, "ns_moe_decode_layer: tensor-core kernel does not fit on an SM");
