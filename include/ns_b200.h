@@ -28,7 +28,7 @@
 extern "C" {
 #endif
 
-#define NS_ABI_VERSION 1
+#define NS_ABI_VERSION 2
 #define NS_MAX_TOKENS 8     /* tokens per fused GEMV or MoE-decode call */
 #define NS_MAX_TOPK 16      /* experts used per token */
 #define NS_MAX_EXPERTS 512  /* experts in one stacked tensor */
@@ -137,6 +137,20 @@ int ns_moe_route(const void* h, int h_dtype, int T, int H,
  * summing `out` over ranks (with residual added on one rank only) gives the
  * full layer.
  */
+/*
+ * Byte ranges a kernel asks L2 to fetch while it runs (cp.async.bulk.prefetch.L2,
+ * a hint: nothing waits for it, nothing is written).  Meant for the weights of
+ * the kernels that follow in the stream, so that HBM works while this kernel is
+ * latency-bound (routing, split merges) and they find their weights in L2.  Each
+ * CTA prefetches an equal share.  Ranges start on 16 bytes; unused slots have
+ * bytes = 0.  No reference counterpart (the reference has no device pipeline).
+ */
+#define NS_L2_PREFETCH_RANGES 4
+typedef struct ns_l2_prefetch {
+  const void* ptr[NS_L2_PREFETCH_RANGES];
+  uint64_t bytes[NS_L2_PREFETCH_RANGES];
+} ns_l2_prefetch_t;
+
 typedef struct ns_moe_layer {
   int T;            /* tokens, 1..NS_MAX_TOKENS */
   int H;            /* hidden size (n_embd) */
@@ -166,6 +180,7 @@ typedef struct ns_moe_layer {
   float* out;             /* T x H fp32 */
   int32_t* ids;           /* T x k int32 routed experts, or NULL */
   float* weights;         /* T x k fp32 routing weights, or NULL */
+  ns_l2_prefetch_t l2;    /* L2 prefetch hint (zeros: none) */
 } ns_moe_layer_t;
 
 /* Workspace bytes a layer call with 1..p->T tokens needs (zeroed once with
@@ -238,6 +253,7 @@ typedef struct ns_dense_gemv {
   const float* x;         /* K fp32 */
   const float* norm_w;    /* K fp32 RMSNorm weight, or NULL */
   float rms_eps;
+  ns_l2_prefetch_t l2;    /* L2 prefetch hint (zeros: none) */
 } ns_dense_gemv_t;
 
 int ns_dense_gemv(const ns_dense_gemv_t* p, ns_stream_t stream);
@@ -270,10 +286,12 @@ typedef struct ns_attn_decode {
   float* k_cache;           /* n_head_kv x max_ctx x head_dim fp32 */
   float* v_cache;
   float* out;               /* n_head*head_dim fp32 */
+  ns_l2_prefetch_t l2;      /* L2 prefetch hint (zeros: none) */
 } ns_attn_decode_t;
 
-/* Workspace of ns_attn_decode: zeroed once (ns_moe_workspace_init clears any
- * buffer); calls ordered on one stream may share one. */
+/* Workspace of ns_attn_decode: currently 0 bytes (the key splits of a kv head
+ * form one thread-block cluster and merge through distributed shared memory);
+ * the argument is kept so that a later version may ask for one. */
 int ns_attn_workspace_bytes(const ns_attn_decode_t* p, size_t* bytes);
 int ns_attn_decode(const ns_attn_decode_t* p, void* workspace, size_t workspace_bytes, ns_stream_t stream);
 

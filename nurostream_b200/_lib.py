@@ -14,6 +14,8 @@ LIB_PATH = PKG / "libns_b200.so"
 HEADER = PKG.parent / "include" / "ns_b200.h"
 
 NS_OK = 0
+ABI_VERSION = 2
+NS_L2_PREFETCH_RANGES = 4
 NS_F32, NS_F16, NS_BF16 = 0, 1, 2
 NS_ROUTE_TOPK_SOFTMAX, NS_ROUTE_SOFTMAX_TOPK_NORM = 0, 1
 NS_ACT_CLAMPED_SWIGLU, NS_ACT_SILU_MUL = 0, 1
@@ -33,6 +35,19 @@ class NsError(RuntimeError):
         self.status = status
 
 
+class L2Prefetch(C.Structure):
+    """Mirror of ns_l2_prefetch_t."""
+
+    _fields_ = [("ptr", C.c_void_p * NS_L2_PREFETCH_RANGES), ("bytes", C.c_uint64 * NS_L2_PREFETCH_RANGES)]
+
+    def set(self, tensors) -> "L2Prefetch":
+        """Prefetch these tensors' bytes (at most NS_L2_PREFETCH_RANGES)."""
+        for i, t in enumerate(list(tensors)[:NS_L2_PREFETCH_RANGES]):
+            self.ptr[i] = t.data_ptr()
+            self.bytes[i] = t.numel() * t.element_size()
+        return self
+
+
 class MoeLayerParams(C.Structure):
     """Mirror of ns_moe_layer_t."""
 
@@ -46,7 +61,7 @@ class MoeLayerParams(C.Structure):
         ("router_w", C.c_void_p), ("router_dtype", C.c_int), ("router_b", C.c_void_p),
         ("gate_w", C.c_void_p), ("up_w", C.c_void_p), ("down_w", C.c_void_p),
         ("gate_b", C.c_void_p), ("up_b", C.c_void_p), ("down_b", C.c_void_p),
-        ("out", C.c_void_p), ("ids", C.c_void_p), ("weights", C.c_void_p),
+        ("out", C.c_void_p), ("ids", C.c_void_p), ("weights", C.c_void_p), ("l2", L2Prefetch),
     ]
 
 
@@ -64,7 +79,7 @@ class DenseGemvParams(C.Structure):
     """Mirror of ns_dense_gemv_t."""
 
     _fields_ = [("K", C.c_int), ("w_dtype", C.c_int), ("n_seg", C.c_int), ("seg", DenseSeg * NS_DENSE_MAX_SEG),
-                ("x", C.c_void_p), ("norm_w", C.c_void_p), ("rms_eps", C.c_float)]
+                ("x", C.c_void_p), ("norm_w", C.c_void_p), ("rms_eps", C.c_float), ("l2", L2Prefetch)]
 
 
 class AttnDecodeParams(C.Structure):
@@ -73,7 +88,7 @@ class AttnDecodeParams(C.Structure):
     _fields_ = [("n_head", C.c_int), ("n_head_kv", C.c_int), ("head_dim", C.c_int), ("max_ctx", C.c_int),
                 ("window", C.c_int), ("scale", C.c_float), ("pos", C.c_void_p), ("qkv", C.c_void_p),
                 ("rope_cos", C.c_void_p), ("rope_sin", C.c_void_p), ("sinks", C.c_void_p),
-                ("k_cache", C.c_void_p), ("v_cache", C.c_void_p), ("out", C.c_void_p)]
+                ("k_cache", C.c_void_p), ("v_cache", C.c_void_p), ("out", C.c_void_p), ("l2", L2Prefetch)]
 
 
 _P, _I, _I64, _U64, _SZ, _F = C.c_void_p, C.c_int, C.c_int64, C.c_uint64, C.c_size_t, C.c_float
@@ -122,8 +137,8 @@ def load(path: Path | str | None = None) -> C.CDLL:
         fn = getattr(lib, name)
         fn.restype = res
         fn.argtypes = args
-    if lib.ns_abi_version() != 1:
-        raise RuntimeError(f"{p}: ABI version {lib.ns_abi_version()} != 1")
+    if lib.ns_abi_version() != ABI_VERSION:
+        raise RuntimeError(f"{p}: ABI version {lib.ns_abi_version()} != {ABI_VERSION}")
     if path is None:
         _lib = lib
     return lib

@@ -11,9 +11,10 @@
 // query heads that share kv head g (GQA); within a 64-key block lane j scores keys j and j + 32
 // against its head's rotated q held in registers, and accumulates p * V for dims 2j, 2j + 1.  Keys
 // are walked in blocks of 64 with an online softmax (running max, sum and output), double-buffered
-// in shared memory by cp.async.  Each CTA leaves (max, sum, output) per head in the workspace; the
-// last CTA of kv head g to finish (an atomic count, reset by that CTA) merges the splits in split
-// order together with the sinks, so the result does not depend on CTA timing.
+// in shared memory by cp.async.  The splits of kv head g are one thread-block cluster: each CTA leaves
+// (max, sum, output) per head in its shared memory and the cluster's rank-0 CTA merges them, in split
+// order and together with the sinks, through distributed shared memory (no global round trip, and a
+// result that does not depend on CTA timing).
 //
 // The token's own key and value come from the projection output (rotated here); the CTA of the last
 // split also writes them into the cache at slot pos for later tokens.  Under programmatic dependent
@@ -29,12 +30,33 @@ constexpr int kAttnBlock = 64;          // keys per block
 constexpr int kAttnKPitch = 68;         // floats per K row in shared memory: 16-byte loads stay conflict-free
 constexpr int kAttnMaxRep = 8;          // query heads per kv head (warps per CTA)
 constexpr int kAttnThreads = kAttnMaxRep * 32;
+constexpr int kAttnMaxSplits = 16;      // key splits of one kv head = CTAs of one cluster
+
+__device__ __forceinline__ uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+// Barrier over every thread of every CTA of the cluster, ordering shared-memory writes before it
+// against reads after it (a launch without clusters is a cluster of one CTA).
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n barrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+// Address of the same shared-memory variable in the CTA of cluster rank r.
+__device__ __forceinline__ uint32_t mapa_shared(uint32_t addr, int r) {
+  uint32_t out;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(out) : "r"(addr), "r"(r));
+  return out;
+}
+__device__ __forceinline__ float ld_cluster_f32(uint32_t addr) {
+  float v;
+  asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(addr) : "memory");
+  return v;
+}
 
 struct AttnArgs {
   ns_attn_decode_t p;
-  int splits;
-  float* part;        // [n_kv][splits][n_rep][2 + hd]: max, sum, output
-  unsigned* count;    // [n_kv] CTAs of kv head g done (reset by the merging CTA)
+  int splits;         // key splits per kv head (the cluster size)
 };
 
 __device__ __forceinline__ void cp_async16(void* smem_dst, const void* gsrc) {
@@ -57,6 +79,8 @@ struct AttnSmem {
   float sq[kAttnMaxRep][kAttnHd];        // rotated q of the group's heads
   float snew[2][kAttnHd];                // rotated new key, new value
   float sp[kAttnMaxRep][kAttnBlock];     // probabilities of the current block
+  float pm[kAttnMaxRep], pl[kAttnMaxRep];  // this split's running max and sum per head
+  float pacc[kAttnMaxRep][kAttnHd];        // and its unnormalised output
 };
 
 __global__ void __launch_bounds__(kAttnThreads, 1) attn_decode_kernel(AttnArgs a) {
@@ -68,7 +92,6 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attn_decode_kernel(AttnArgs a
   auto& sq = S.sq;
   auto& snew = S.snew;
   auto& sp = S.sp;
-  __shared__ int s_last;
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int g = blockIdx.x / a.splits, s = blockIdx.x % a.splits;
@@ -103,6 +126,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attn_decode_kernel(AttnArgs a
     cp_async_commit();
   };
   if (n_blocks > 0) load_block(0);
+  if (tid == 0) l2_prefetch_share(p.l2, blockIdx.x, gridDim.x);  // the next kernels' weights (hint)
 
   griddep_wait();
   // rotated q of this group's heads, the new key (rotated) and value
@@ -190,47 +214,78 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attn_decode_kernel(AttnArgs a
     __syncthreads();  // the buffer of block b is refilled by load_block(b + 2)
   }
 
-  // this split's partial result per head
-  const int stride = 2 + kAttnHd;
-  float* part = a.part + (((int64_t)g * a.splits + s) * kAttnMaxRep) * stride;
+  // this split's partial result per head, in shared memory; the splits of kv head g form one thread
+  // block cluster, and its rank-0 CTA merges them through distributed shared memory
   if (head_ok) {
-    float* ph = part + warp * stride;
     if (lane == 0) {
-      ph[0] = m;
-      ph[1] = l;
+      S.pm[warp] = m;
+      S.pl[warp] = l;
     }
-    ph[2 + 2 * lane] = acc0;
-    ph[3 + 2 * lane] = acc1;
+    S.pacc[warp][2 * lane] = acc0;
+    S.pacc[warp][2 * lane + 1] = acc1;
   }
-  __threadfence();
-  __syncthreads();
-  if (tid == 0) s_last = atomicAdd(&a.count[g], 1u) == (unsigned)(a.splits - 1);
-  __syncthreads();
-  if (!s_last) return;
-  __threadfence();
-  // merge the splits of kv head g in split order, with each head's sink as one more logit
-  if (head_ok) {
+  cluster_sync_all();
+  if (cluster_rank() == 0 && head_ok) {
+    // merge in split order, with each head's sink as one more logit
     const int h = g * n_rep + warp;
-    const float* base = a.part + ((int64_t)g * a.splits * kAttnMaxRep) * stride;
+    const uint32_t pm = smem_addr(&S.pm[warp]), pl = smem_addr(&S.pl[warp]);
+    const uint32_t pa = smem_addr(&S.pacc[warp][2 * lane]);
+    float ms[kAttnMaxSplits], ls[kAttnMaxSplits], a0[kAttnMaxSplits], a1[kAttnMaxSplits];
+#pragma unroll
+    for (int t = 0; t < kAttnMaxSplits; ++t)
+      if (t < a.splits) {  // all remote loads first
+        ms[t] = ld_cluster_f32(mapa_shared(pm, t));
+        ls[t] = ld_cluster_f32(mapa_shared(pl, t));
+        a0[t] = ld_cluster_f32(mapa_shared(pa, t));
+        a1[t] = ld_cluster_f32(mapa_shared(pa + 4, t));
+      }
     float mt = p.sinks ? p.sinks[h] : -INFINITY;
-    for (int t = 0; t < a.splits; ++t) mt = fmaxf(mt, __ldcg(base + ((int64_t)t * kAttnMaxRep + warp) * stride));
+#pragma unroll
+    for (int t = 0; t < kAttnMaxSplits; ++t)
+      if (t < a.splits) mt = fmaxf(mt, ms[t]);
     float lt = p.sinks ? expf(p.sinks[h] - mt) : 0.f, o0 = 0.f, o1 = 0.f;
-    for (int t = 0; t < a.splits; ++t) {
-      const float* ph = base + ((int64_t)t * kAttnMaxRep + warp) * stride;
-      const float mt_s = __ldcg(ph);
-      if (mt_s == -INFINITY) continue;  // a split with no keys
-      const float f = expf(mt_s - mt);
-      lt = fmaf(__ldcg(ph + 1), f, lt);
-      o0 = fmaf(__ldcg(ph + 2 + 2 * lane), f, o0);
-      o1 = fmaf(__ldcg(ph + 3 + 2 * lane), f, o1);
-    }
+#pragma unroll
+    for (int t = 0; t < kAttnMaxSplits; ++t)
+      if (t < a.splits && ms[t] != -INFINITY) {  // a split with no keys adds nothing
+        const float f = expf(ms[t] - mt);
+        lt = fmaf(ls[t], f, lt);
+        o0 = fmaf(a0[t], f, o0);
+        o1 = fmaf(a1[t], f, o1);
+      }
     p.out[(int64_t)h * kAttnHd + 2 * lane] = o0 / lt;
     p.out[(int64_t)h * kAttnHd + 2 * lane + 1] = o1 / lt;
   }
-  if (tid == 0) a.count[g] = 0u;  // ready for the next launch (stream-ordered)
+  cluster_sync_all();  // every CTA's shared memory stays alive until rank 0 has read it
 }
 
-static int attn_plan(const ns_attn_decode_t* p, int* splits, size_t* ws) {
+static int g_attn_max_cluster = 0;  // largest cluster the device schedules for this kernel (8 or 16)
+
+static int attn_max_cluster() {
+  if (g_attn_max_cluster) return g_attn_max_cluster;
+  int best = 8;
+  if (cudaFuncSetAttribute(attn_decode_kernel, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) == cudaSuccess &&
+      cudaFuncSetAttribute(attn_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sizeof(AttnSmem)) ==
+          cudaSuccess) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(kAttnMaxSplits);
+    cfg.blockDim = dim3(kAttnThreads);
+    cfg.dynamicSmemBytes = sizeof(AttnSmem);
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = kAttnMaxSplits;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    int n = 0;
+    if (cudaOccupancyMaxActiveClusters(&n, attn_decode_kernel, &cfg) == cudaSuccess && n >= 1) best = kAttnMaxSplits;
+  }
+  (void)cudaGetLastError();
+  g_attn_max_cluster = best;
+  return best;
+}
+
+static int attn_plan(const ns_attn_decode_t* p, int* splits) {
   if (!p) return fail(NS_ERR_INVALID, "ns_attn_decode: null parameters");
   if (p->head_dim != kAttnHd) return fail(NS_ERR_UNSUPPORTED, "ns_attn_decode: head_dim %d (only 64)", p->head_dim);
   if (p->n_head_kv < 1 || p->n_head < p->n_head_kv || p->n_head % p->n_head_kv ||
@@ -238,13 +293,9 @@ static int attn_plan(const ns_attn_decode_t* p, int* splits, size_t* ws) {
     return fail(NS_ERR_UNSUPPORTED, "ns_attn_decode: %d query heads over %d kv heads (at most %d per kv head)",
                 p->n_head, p->n_head_kv, kAttnMaxRep);
   if (p->max_ctx < 1 || p->window < 0) return fail(NS_ERR_INVALID, "ns_attn_decode: bad max_ctx / window");
-  int nsm = 0;
-  int st = num_sms(&nsm);
-  if (st) return st;
-  const int keys = p->window > 0 ? std::min(p->window, p->max_ctx) : p->max_ctx;
-  *splits = std::max(1, std::min(std::max(1, nsm / p->n_head_kv), (keys + kAttnBlock - 1) / kAttnBlock));
-  *ws = align_up((size_t)p->n_head_kv * 4, 256) +
-        (size_t)p->n_head_kv * *splits * kAttnMaxRep * (2 + kAttnHd) * 4;
+  // keys per split <= one 64-key block where the cluster size allows it
+  const int keys = p->window > 0 ? std::min(p->window + 1, p->max_ctx) : p->max_ctx;
+  *splits = std::max(1, std::min(attn_max_cluster(), (keys + kAttnBlock - 1) / kAttnBlock));
   return NS_OK;
 }
 
@@ -254,39 +305,45 @@ extern "C" int ns_attn_workspace_bytes(const ns_attn_decode_t* p, size_t* bytes)
   using namespace ns;
   if (!bytes) return fail(NS_ERR_INVALID, "ns_attn_workspace_bytes: null output");
   int splits = 0;
-  return attn_plan(p, &splits, bytes);
+  int st = attn_plan(p, &splits);
+  if (st) return st;
+  *bytes = 0;  // the splits merge through distributed shared memory
+  return NS_OK;
 }
 
 extern "C" int ns_attn_decode(const ns_attn_decode_t* p, void* workspace, size_t workspace_bytes, ns_stream_t stream) {
   using namespace ns;
+  (void)workspace;
+  (void)workspace_bytes;
   int splits = 0;
-  size_t need = 0;
-  int st = attn_plan(p, &splits, &need);
+  int st = attn_plan(p, &splits);
   if (st) return st;
-  if (!workspace || workspace_bytes < need)
-    return fail(NS_ERR_SIZE, "ns_attn_decode: workspace of %zu bytes, need %zu", workspace_bytes, need);
-  if (reinterpret_cast<uintptr_t>(workspace) & 255) return fail(NS_ERR_INVALID, "ns_attn_decode: workspace not 256-byte aligned");
   if (!p->pos || !p->qkv || !p->rope_cos || !p->rope_sin || !p->k_cache || !p->v_cache || !p->out)
     return fail(NS_ERR_INVALID, "ns_attn_decode: null pointer");
   if ((reinterpret_cast<uintptr_t>(p->k_cache) | reinterpret_cast<uintptr_t>(p->v_cache)) & 15)
     return fail(NS_ERR_INVALID, "ns_attn_decode: caches must be 16-byte aligned");
+  for (int i = 0; i < NS_L2_PREFETCH_RANGES; ++i)
+    if (p->l2.bytes[i] && (reinterpret_cast<uintptr_t>(p->l2.ptr[i]) & 15))
+      return fail(NS_ERR_INVALID, "ns_attn_decode: L2 prefetch range %d not 16-byte aligned", i);
   AttnArgs a;
   a.p = *p;
   a.splits = splits;
-  a.count = reinterpret_cast<unsigned*>(workspace);
-  a.part = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(workspace) + align_up((size_t)p->n_head_kv * 4, 256));
+  NS_CUDA_TRY(cudaFuncSetAttribute(attn_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                   (int)sizeof(AttnSmem)));
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(p->n_head_kv * splits);
   cfg.blockDim = dim3(kAttnThreads);
   cfg.dynamicSmemBytes = sizeof(AttnSmem);
-  NS_CUDA_TRY(cudaFuncSetAttribute(attn_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                   (int)sizeof(AttnSmem)));
   cfg.stream = reinterpret_cast<cudaStream_t>(stream);
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
+  attr[1].id = cudaLaunchAttributeClusterDimension;
+  attr[1].val.clusterDim.x = splits;
+  attr[1].val.clusterDim.y = 1;
+  attr[1].val.clusterDim.z = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = 2;
   NS_CUDA_TRY(cudaLaunchKernelEx(&cfg, attn_decode_kernel, a));
   return NS_OK;
 }

@@ -277,6 +277,27 @@ __device__ __forceinline__ void griddep_launch_dependents() { asm volatile("grid
 
 inline size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 
+// ----------------------------------------------------------------------------- L2 prefetch hints
+
+__device__ __forceinline__ void prefetch_l2_bulk(const void* src, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
+}
+
+// CTA `cta` of `ncta` asks L2 for its equal share of every range of `pf` (one thread calls this).
+// Shares start and end on 16-byte boundaries; pieces of at most 64 KB.
+__device__ __forceinline__ void l2_prefetch_share(const ns_l2_prefetch_t& pf, int cta, int ncta) {
+#pragma unroll 1
+  for (int i = 0; i < NS_L2_PREFETCH_RANGES; ++i) {
+    const uint64_t n = pf.bytes[i];
+    if (!n || !pf.ptr[i]) continue;
+    const uint64_t lo = (n * (uint64_t)cta / (uint64_t)ncta) & ~uint64_t(15);
+    const uint64_t hi = cta + 1 == ncta ? (n & ~uint64_t(15)) : ((n * (uint64_t)(cta + 1) / (uint64_t)ncta) & ~uint64_t(15));
+    const uint8_t* base = static_cast<const uint8_t*>(pf.ptr[i]);
+    for (uint64_t o = lo; o < hi; o += 65536u)
+      prefetch_l2_bulk(base + o, (uint32_t)(hi - o < 65536u ? hi - o : 65536u));
+  }
+}
+
 // ----------------------------------------------------------------------------- warp utilities
 
 __device__ __forceinline__ float warp_sum(float v) {

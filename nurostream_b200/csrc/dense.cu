@@ -30,6 +30,7 @@ constexpr int kDenseThreads = (kDenseWarps + 1) * 32;  // + one producer warp
 constexpr int kDenseTileRows = 8;
 constexpr int kDenseMaxStages = 8;
 constexpr int kDenseSmemBudget = 220 * 1024;
+constexpr int kDensePreRows = 1024;  // rows per CTA whose bias / residual are staged in shared memory
 
 struct DenseArgs {
   ns_dense_gemv_t p;
@@ -38,6 +39,7 @@ struct DenseArgs {
   int stages;
   int stage_bytes;
   int tile_rows;  // rows per stage, <= kDenseTileRows (fewer for wide K, so that 2+ stages fit)
+  int pre;        // stage the CTA's biases / residuals (its rows fit kDensePreRows and some are given)
 };
 
 // Sum of 8 per-lane values across a warp, one row per lane group: after the butterfly, lane l
@@ -95,6 +97,8 @@ __global__ void __launch_bounds__(kDenseThreads, 1) dense_gemv_kernel(DenseArgs 
   uint64_t* empty = full + kDenseMaxStages;
   float* red = reinterpret_cast<float*>(empty + kDenseMaxStages);  // [2][warp][row]
   float* ssq = red + 2 * kDenseWarps * kDenseTileRows;              // [warp]
+  float* pre_b = ssq + kDenseWarps;                                  // [row - r_begin]: bias (0 if none)
+  float* pre_r = pre_b + kDensePreRows;                              // [row - r_begin]: residual (0 if none)
   __shared__ int s_issued;              // tiles the producer issued (fewer only when a wait ran out)
   __shared__ volatile int s_prod_done;  // the producer has left its loop
 
@@ -119,7 +123,12 @@ __global__ void __launch_bounds__(kDenseThreads, 1) dense_gemv_kernel(DenseArgs 
     // ---- producer: static weights only, so the first stages go out before the wait
     if (lane == 0) {
       int i = 0;
+      bool hinted = false;
       for (; i < n_tiles; ++i) {
+        if (i == nst && !hinted) {  // the ring is full: the later kernels' weights next (L2 hint)
+          l2_prefetch_share(a.p.l2, blockIdx.x, gridDim.x);
+          hinted = true;
+        }
         const int slot = i % nst;
         // a wait that runs out means the compute warps gave up on an earlier tile: issue no more
         if (i >= nst && !mbar_wait_bounded(&empty[slot], (uint32_t)((i / nst - 1) & 1))) break;
@@ -141,6 +150,7 @@ __global__ void __launch_bounds__(kDenseThreads, 1) dense_gemv_kernel(DenseArgs 
           }
         }
       }
+      if (!hinted) l2_prefetch_share(a.p.l2, blockIdx.x, gridDim.x);
       s_issued = i;
       __threadfence_block();
       s_prod_done = 1;
@@ -188,6 +198,19 @@ __global__ void __launch_bounds__(kDenseThreads, 1) dense_gemv_kernel(DenseArgs 
         for (int j = 0; j < 8; ++j) xv[c][j] = __fmul_rn(__fmul_rn(xv[c][j], r), wn[j]);  // (x * r) * w
       }
     }
+  }
+  // biases and residuals of this CTA's rows, staged once (one load latency instead of one per tile)
+  if (a.pre) {
+    for (int i = tid; i < r_end - r_begin; i += kDenseWarps * 32) {
+      const int row = r_begin + i;
+      int s = 0;
+      while (s + 1 < a.p.n_seg && row >= a.seg_start[s + 1]) ++s;
+      const ns_dense_seg_t& sg = a.p.seg[s];
+      const int lr = row - a.seg_start[s];
+      pre_b[i] = sg.bias ? sg.bias[lr] : 0.f;
+      pre_r[i] = sg.residual ? sg.residual[lr] : 0.f;
+    }
+    named_sync(1, kDenseWarps * 32);
   }
   griddep_launch_dependents();
 
@@ -239,8 +262,15 @@ __global__ void __launch_bounds__(kDenseThreads, 1) dense_gemv_kernel(DenseArgs 
         while (s + 1 < a.p.n_seg && row >= a.seg_start[s + 1]) ++s;
         const ns_dense_seg_t& sg = a.p.seg[s];
         const int lr = row - a.seg_start[s];
-        float y = sg.bias ? sum + sg.bias[lr] : sum;
-        if (sg.residual) y = sg.residual[lr] + y;
+        float y;
+        if (a.pre) {
+          const int i = row - r_begin;
+          y = sg.bias ? sum + pre_b[i] : sum;
+          if (sg.residual) y = pre_r[i] + y;
+        } else {
+          y = sg.bias ? sum + sg.bias[lr] : sum;
+          if (sg.residual) y = sg.residual[lr] + y;
+        }
         sg.y[lr] = y;
       }
     }
@@ -288,6 +318,9 @@ extern "C" int ns_dense_gemv(const ns_dense_gemv_t* p, ns_stream_t stream) {
   if (p->n_seg < 1 || p->n_seg > NS_DENSE_MAX_SEG)
     return fail(NS_ERR_INVALID, "ns_dense_gemv: n_seg=%d outside 1..%d", p->n_seg, NS_DENSE_MAX_SEG);
   if (!p->x) return fail(NS_ERR_INVALID, "ns_dense_gemv: null x");
+  for (int i = 0; i < NS_L2_PREFETCH_RANGES; ++i)
+    if (p->l2.bytes[i] && (reinterpret_cast<uintptr_t>(p->l2.ptr[i]) & 15))
+      return fail(NS_ERR_INVALID, "ns_dense_gemv: L2 prefetch range %d not 16-byte aligned", i);
   auto al16 = [](const void* q) { return (reinterpret_cast<uintptr_t>(q) & 15) == 0; };
   if (!al16(p->x) || (p->norm_w && !al16(p->norm_w)))
     return fail(NS_ERR_INVALID, "ns_dense_gemv: x and norm_w must be 16-byte aligned");
@@ -307,11 +340,15 @@ extern "C" int ns_dense_gemv(const ns_dense_gemv_t* p, ns_stream_t stream) {
   int nsm = 0;
   int st = num_sms(&nsm);
   if (st) return st;
-  const size_t fixed = 2 * kDenseMaxStages * 8 + (2 * kDenseWarps * kDenseTileRows + kDenseWarps) * 4 + 128;
+  bool any_extra = false;
+  for (int s = 0; s < p->n_seg; ++s) any_extra |= p->seg[s].bias != nullptr || p->seg[s].residual != nullptr;
+  const size_t fixed = 2 * kDenseMaxStages * 8 + (2 * kDenseWarps * kDenseTileRows + kDenseWarps) * 4 +
+                       (size_t)2 * kDensePreRows * 4 + 128;
   a.tile_rows = kDenseTileRows;
   while (a.tile_rows > 1 && (size_t)3 * a.tile_rows * p->K * 2 > kDenseSmemBudget - fixed) a.tile_rows /= 2;
   const int grid = std::max(1, std::min(nsm, (total + a.tile_rows - 1) / a.tile_rows));
   a.stage_bytes = a.tile_rows * p->K * 2;
+  a.pre = any_extra && (total + grid - 1) / grid <= kDensePreRows;
   a.stages = (int)std::min<size_t>(kDenseMaxStages, (kDenseSmemBudget - fixed) / a.stage_bytes);
   if (a.stages < 2) return fail(NS_ERR_UNSUPPORTED, "ns_dense_gemv: K=%d leaves fewer than 2 stages", p->K);
   const size_t smem = (size_t)a.stages * a.stage_bytes + fixed;

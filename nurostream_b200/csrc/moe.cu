@@ -374,6 +374,7 @@ __global__ void __launch_bounds__(kMoeThreads, 1) moe_layer_kernel(MoeArgs a) {
   extern __shared__ __align__(128) uint8_t smem[];
   const ns_moe_layer_t& p = a.p;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  if (tid == 0) l2_prefetch_share(a.p.l2, blockIdx.x, gridDim.x);  // the next kernels' weights (hint)
   const int G = gridDim.x, c = blockIdx.x;
   const int T = p.T, H = p.H, F = p.F, E = p.n_expert, k = p.k;
 
@@ -1009,6 +1010,9 @@ static int moe_validate(const ns_moe_layer_t* p, MoePlan* plan) {
   if (p->ggml_type != NS_GGML_MXFP4 && p->ggml_type != NS_GGML_Q8_0 && p->ggml_type != NS_GGML_Q4_K &&
       p->ggml_type != NS_GGML_Q6_K)
     return fail(NS_ERR_UNSUPPORTED, "ns_moe: expert type %d has no fused kernel", p->ggml_type);
+  for (int i = 0; i < NS_L2_PREFETCH_RANGES; ++i)
+    if (p->l2.bytes[i] && (reinterpret_cast<uintptr_t>(p->l2.ptr[i]) & 15))
+      return fail(NS_ERR_INVALID, "ns_moe: L2 prefetch range %d not 16-byte aligned", i);
   if (row_bytes_of(p->ggml_type, p->H) < 0 || row_bytes_of(p->ggml_type, p->F) < 0)
     return fail(NS_ERR_INVALID, "ns_moe: H=%d / F=%d not whole blocks of type %d", p->H, p->F, p->ggml_type);
   plan->pairs_max = p->T * p->k;

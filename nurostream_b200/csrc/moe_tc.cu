@@ -357,6 +357,8 @@ __global__ void __launch_bounds__(kTcThreads, 1) moe_tc_kernel(const __grid_cons
   // producer overwrites it only after b1_ready
   float* h = reinterpret_cast<float*>(raw + (TcRaw<NT>::kStages - 1) * kTcRawBytes);
   const bool own_expert = c < E;
+  // the next kernels' weights into L2 while this layer routes (a hint; static data, so before the wait)
+  if (tid == kTcThreads - 1) l2_prefetch_share(p.l2, blockIdx.x, gridDim.x);
   float wv[8], rv[8];
 #pragma unroll
   for (int u = 0; u < 8; ++u) {

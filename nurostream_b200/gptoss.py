@@ -192,17 +192,30 @@ class GptOssDecoder:
     # ------------------------------------------------------------------ launches of one step
 
     def _build_params(self):
-        """ctypes parameter blocks of every launch, built once (the pointers never change)."""
+        """ctypes parameter blocks of every launch, built once (the pointers never change).
+
+        L2 prefetch hints chain the weight stream across kernels: the MoE block of layer l asks
+        L2 for layer l+1's q/k/v weights (the last layer for the head of the LM head) while it
+        routes, and the attention kernel of layer l for the o-proj weights that follow it; HBM
+        then works while those kernels are latency-bound, and the dense kernels find their
+        weights in L2.
+        """
         sh = self.shape
+        for l in range(sh.n_layer):
+            if l + 1 < sh.n_layer:
+                nxt = self.attn[l + 1]
+                self.moe[l].l2_prefetch = [nxt.q_w, nxt.k_w, nxt.v_w]
+            else:
+                self.moe[l].l2_prefetch = [self.out_w.view(-1)[: 32 << 20]]
         self._p = []
         cur = self.xs[0]
         for l in range(sh.n_layer):
             A = self.attn[l]
             xa = self.xa[l % len(self.xa)]
             nxt = self.xs[(l + 1) % len(self.xs)]
-            self._p.append((A.qkv_params(cur, self.qkv),
-                            A.attn_params(self.pos, self.qkv, self.rope_cos, self.rope_sin, self.attn_out),
-                            A.oproj_params(self.attn_out, cur, xa), xa, nxt))
+            pa = A.attn_params(self.pos, self.qkv, self.rope_cos, self.rope_sin, self.attn_out)
+            pa.l2.set([A.o_w])
+            self._p.append((A.qkv_params(cur, self.qkv), pa, A.oproj_params(self.attn_out, cur, xa), xa, nxt))
             cur = nxt
         self.x_final = cur
         head = _lib.DenseGemvParams()

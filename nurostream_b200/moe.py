@@ -93,6 +93,7 @@ class MoeLayer:
         self.alpha, self.limit, self.rms_eps = alpha, limit, rms_eps
         self.max_tokens = max_tokens
         self._slice = 0  # rows per launch that prefill settled on
+        self.l2_prefetch: list = []  # tensors whose bytes the layer kernel asks L2 to fetch (a hint)
         p = self._params(max_tokens, None, None, True, None, None)
         n = C.c_size_t(0)
         _lib.call("ns_moe_workspace_bytes", C.byref(p), C.byref(n))
@@ -144,6 +145,7 @@ class MoeLayer:
         p.gate_w, p.up_w, p.down_w = self.gate.data_ptr(), self.up.data_ptr(), self.down.data_ptr()
         p.gate_b, p.up_b, p.down_b = _ptr(self.gate_b), _ptr(self.up_b), _ptr(self.down_b)
         p.out, p.ids, p.weights = _ptr(out), _ptr(ids), _ptr(weights)
+        p.l2.set(getattr(self, "l2_prefetch", []))
         return p
 
     def __call__(self, x: torch.Tensor, out: torch.Tensor | None = None, add_residual: bool = True,

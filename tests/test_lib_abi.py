@@ -22,7 +22,7 @@ def test_exports_every_header_symbol(lib):
 
 
 def test_abi_version(lib):
-    assert lib.ns_abi_version() == 1
+    assert lib.ns_abi_version() == _lib.ABI_VERSION == 2
 
 
 def test_type_layouts_match_gguf(lib):
