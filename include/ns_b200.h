@@ -296,6 +296,50 @@ int ns_attn_workspace_bytes(const ns_attn_decode_t* p, size_t* bytes);
 int ns_attn_decode(const ns_attn_decode_t* p, void* workspace, size_t workspace_bytes, ns_stream_t stream);
 
 /*
+ * A whole attention block for one decode token as ONE cooperative launch:
+ * out = x + W_o attn(rope(q), rope(k), v) + b_o with q, k, v = W_{q,k,v}
+ * rms_norm(x, norm_w) + b -- ns_dense_gemv (q/k/v), ns_attn_decode and
+ * ns_dense_gemv (o-proj) without the kernel boundaries; one ring of
+ * shared-memory stages per SM streams its q/k/v rows, its share of the key /
+ * value history and its o-proj rows back to back.
+ * Replaces neurostream/model/gpt_oss.py:101-114 `GptOssModel._attention_block`
+ * (with rms_norm, _biased_linear, apply_rope, KVCache.append, repeat_kv and
+ * sink_attention).  head_dim 64; at most 8 query heads per kv head; H and
+ * n_head*64 at most 4096 columns.  The workspace (ns_attn_block_workspace_bytes,
+ * 256-byte aligned) is zeroed once; calls ordered on one stream may share it.
+ */
+typedef struct ns_attn_block {
+  int H;                    /* hidden size */
+  int n_head;
+  int n_head_kv;
+  int head_dim;
+  int max_ctx;              /* positions each cache holds */
+  int window;               /* 0: full causal attention; > 0: sliding window */
+  float rms_eps;
+  float scale;              /* 1 / sqrt(head_dim) */
+  const float* x;           /* H fp32 residual stream */
+  const float* norm_w;      /* H fp32 (attn_norm) */
+  const void* wq;           /* n_head*head_dim x H bf16 */
+  const void* wk;           /* n_head_kv*head_dim x H bf16 */
+  const void* wv;           /* n_head_kv*head_dim x H bf16 */
+  const float* bq;          /* fp32 biases, or NULL */
+  const float* bk;
+  const float* bv;
+  const void* wo;           /* H x n_head*head_dim bf16 */
+  const float* bo;          /* H fp32, or NULL */
+  const float* sinks;       /* n_head fp32 sink logits, or NULL */
+  const int32_t* pos;       /* device int32: position of the token */
+  const float* rope_cos;    /* max_ctx x head_dim fp32 */
+  const float* rope_sin;
+  float* k_cache;           /* n_head_kv x max_ctx x head_dim fp32 */
+  float* v_cache;
+  float* out;               /* H fp32 */
+} ns_attn_block_t;
+
+int ns_attn_block_workspace_bytes(const ns_attn_block_t* p, size_t* bytes);
+int ns_attn_block(const ns_attn_block_t* p, void* workspace, size_t workspace_bytes, ns_stream_t stream);
+
+/*
  * The embedding row of the token *token (device int32) widened to fp32:
  * neurostream/model/qwen3.py:266-275 `Qwen3Model.embed` (`W[tokens]`).
  * table: rows x H of dtype (NS_F32 / NS_F16 / NS_BF16).

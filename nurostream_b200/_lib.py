@@ -91,6 +91,18 @@ class AttnDecodeParams(C.Structure):
                 ("k_cache", C.c_void_p), ("v_cache", C.c_void_p), ("out", C.c_void_p), ("l2", L2Prefetch)]
 
 
+class AttnBlockParams(C.Structure):
+    """Mirror of ns_attn_block_t."""
+
+    _fields_ = [("H", C.c_int), ("n_head", C.c_int), ("n_head_kv", C.c_int), ("head_dim", C.c_int),
+                ("max_ctx", C.c_int), ("window", C.c_int), ("rms_eps", C.c_float), ("scale", C.c_float),
+                ("x", C.c_void_p), ("norm_w", C.c_void_p), ("wq", C.c_void_p), ("wk", C.c_void_p),
+                ("wv", C.c_void_p), ("bq", C.c_void_p), ("bk", C.c_void_p), ("bv", C.c_void_p),
+                ("wo", C.c_void_p), ("bo", C.c_void_p), ("sinks", C.c_void_p), ("pos", C.c_void_p),
+                ("rope_cos", C.c_void_p), ("rope_sin", C.c_void_p), ("k_cache", C.c_void_p),
+                ("v_cache", C.c_void_p), ("out", C.c_void_p)]
+
+
 _P, _I, _I64, _U64, _SZ, _F = C.c_void_p, C.c_int, C.c_int64, C.c_uint64, C.c_size_t, C.c_float
 
 SIGNATURES = {
@@ -112,6 +124,8 @@ SIGNATURES = {
     "ns_attn_workspace_bytes": (_I, [C.POINTER(AttnDecodeParams), C.POINTER(_SZ)]),
     "ns_attn_decode": (_I, [C.POINTER(AttnDecodeParams), _P, _SZ, _P]),
     "ns_embed": (_I, [_P, _I, _I64, _I, _P, _P, _P]),
+    "ns_attn_block_workspace_bytes": (_I, [C.POINTER(AttnBlockParams), C.POINTER(_SZ)]),
+    "ns_attn_block": (_I, [C.POINTER(AttnBlockParams), _P, _SZ, _P]),
 }
 
 _lib = None

@@ -7,4 +7,5 @@
 #include "attn.cu"
 #include "gemv.cu"
 #include "moe.cu"
+#include "attn_block.cu"
 #include "synth.cu"

@@ -10,10 +10,11 @@ and runs one decode token as the reference's ``GptOssModel.forward`` does
                      x = x + sum_e w_e expert_e(rms_norm(x))                    (_ffn_block)
     logits = output(rms_norm(x))
 
-with four launches per layer (``ns_dense_gemv`` q/k/v with the RMSNorm fused, ``ns_attn_decode``,
-``ns_dense_gemv`` output projection + bias + residual, ``ns_moe_decode_layer``) plus the
-embedding and the LM head, all chained with programmatic dependent launch and captured once into
-a CUDA graph.  The token id and its position live in device memory, so the same graph decodes
+with two launches per layer -- ``ns_attn_block`` (RMSNorm, q/k/v, RoPE, KV append, sink attention,
+o-proj and residual as one cooperative kernel) and ``ns_moe_decode_layer`` -- plus the embedding and
+the LM head, all chained with programmatic dependent launch and captured once into a CUDA graph.
+(``fused_attention=False`` runs the attention block as its three separate kernels instead:
+``ns_dense_gemv`` q/k/v, ``ns_attn_decode``, ``ns_dense_gemv`` o-proj.)  The token id and its position live in device memory, so the same graph decodes
 any token at any position.
 
 Expert parallelism (``world > 1``): rank r holds experts [r*E/world, (r+1)*E/world) of every
@@ -122,6 +123,20 @@ class AttnLayer:
                                                 self.v_cache.data_ptr(), out.data_ptr())
         return a
 
+    def block_params(self, x, pos, rope_cos, rope_sin, out) -> _lib.AttnBlockParams:
+        """Parameters of the whole block as one launch (ns_attn_block): x -> out."""
+        sh = self.shape
+        b = _lib.AttnBlockParams()
+        b.H, b.n_head, b.n_head_kv, b.head_dim = sh.n_embd, sh.n_head, sh.n_head_kv, sh.head_dim
+        b.max_ctx, b.window, b.rms_eps, b.scale = self.k_cache.shape[1], self.window, sh.rms_eps, 1.0 / math.sqrt(sh.head_dim)
+        b.x, b.norm_w = x.data_ptr(), self.norm_w.data_ptr()
+        b.wq, b.wk, b.wv = self.q_w.data_ptr(), self.k_w.data_ptr(), self.v_w.data_ptr()
+        b.bq, b.bk, b.bv = self.q_b.data_ptr(), self.k_b.data_ptr(), self.v_b.data_ptr()
+        b.wo, b.bo, b.sinks = self.o_w.data_ptr(), self.o_b.data_ptr(), self.sinks.data_ptr()
+        b.pos, b.rope_cos, b.rope_sin = pos.data_ptr(), rope_cos.data_ptr(), rope_sin.data_ptr()
+        b.k_cache, b.v_cache, b.out = self.k_cache.data_ptr(), self.v_cache.data_ptr(), out.data_ptr()
+        return b
+
     def oproj_params(self, attn_out, residual, y) -> _lib.DenseGemvParams:
         sh = self.shape
         p = _lib.DenseGemvParams()
@@ -144,7 +159,7 @@ class GptOssDecoder:
 
     def __init__(self, shape: GptOssShape | None = None, device="cuda", seed: int = 0, ctx: int = 2048,
                  max_ctx: int | None = None, rank: int = 0, world: int = 1, group=None, use_graph: bool = True,
-                 keep_layer_outputs: bool = False):
+                 keep_layer_outputs: bool = False, l2_prefetch: bool = False, fused_attention: bool = True):
         self.shape = shape = shape or GptOssShape()
         self.device = dev = torch.device(device)
         self.seed, self.ctx = seed, ctx
@@ -184,10 +199,12 @@ class GptOssDecoder:
         self.attn_ws_bytes = max(n.value, n2.value)
         self.attn_ws = torch.zeros(self.attn_ws_bytes + 256, dtype=torch.uint8, device=dev)
         self._attn_ws_ptr = self.attn_ws.data_ptr() + (-self.attn_ws.data_ptr()) % 256
+        self.l2_prefetch = l2_prefetch
+        self.fused_attention = fused_attention
         self._build_params()
         self.graph = None
         self.use_graph = use_graph
-        self.launches_per_step = 2 + 4 * shape.n_layer
+        self.launches_per_step = 2 + (2 if fused_attention else 4) * shape.n_layer
 
     # ------------------------------------------------------------------ launches of one step
 
@@ -202,21 +219,35 @@ class GptOssDecoder:
         """
         sh = self.shape
         for l in range(sh.n_layer):
-            if l + 1 < sh.n_layer:
+            if not self.l2_prefetch:
+                self.moe[l].l2_prefetch = []
+            elif l + 1 < sh.n_layer:
                 nxt = self.attn[l + 1]
                 self.moe[l].l2_prefetch = [nxt.q_w, nxt.k_w, nxt.v_w]
             else:
                 self.moe[l].l2_prefetch = [self.out_w.view(-1)[: 32 << 20]]
         self._p = []
+        self._blk = []
         cur = self.xs[0]
         for l in range(sh.n_layer):
             A = self.attn[l]
             xa = self.xa[l % len(self.xa)]
             nxt = self.xs[(l + 1) % len(self.xs)]
             pa = A.attn_params(self.pos, self.qkv, self.rope_cos, self.rope_sin, self.attn_out)
-            pa.l2.set([A.o_w])
+            if self.l2_prefetch:
+                pa.l2.set([A.o_w])
             self._p.append((A.qkv_params(cur, self.qkv), pa, A.oproj_params(self.attn_out, cur, xa), xa, nxt))
+            self._blk.append(A.block_params(cur, self.pos, self.rope_cos, self.rope_sin, xa))
             cur = nxt
+        n = C.c_size_t(0)
+        if self.fused_attention:
+            ws = 0
+            for b in self._blk:
+                _lib.call("ns_attn_block_workspace_bytes", C.byref(b), C.byref(n))
+                ws = max(ws, n.value)
+            self.block_ws = torch.zeros(ws + 256, dtype=torch.uint8, device=self.device)
+            self._block_ws_ptr = self.block_ws.data_ptr() + (-self.block_ws.data_ptr()) % 256
+            self._block_ws_bytes = ws
         self.x_final = cur
         head = _lib.DenseGemvParams()
         head.K, head.w_dtype, head.n_seg = sh.n_embd, _lib.NS_BF16, 1
@@ -231,9 +262,12 @@ class GptOssDecoder:
         _lib.call("ns_embed", self.embd.data_ptr(), _lib.NS_BF16, sh.vocab_size, sh.n_embd, self.token.data_ptr(),
                   self.xs[0].data_ptr(), stream)
         for l, (pq, pa, po, xa, nxt) in enumerate(self._p):
-            _lib.call("ns_dense_gemv", C.byref(pq), stream)
-            _lib.call("ns_attn_decode", C.byref(pa), self._attn_ws_ptr, self.attn_ws_bytes, stream)
-            _lib.call("ns_dense_gemv", C.byref(po), stream)
+            if self.fused_attention:
+                _lib.call("ns_attn_block", C.byref(self._blk[l]), self._block_ws_ptr, self._block_ws_bytes, stream)
+            else:
+                _lib.call("ns_dense_gemv", C.byref(pq), stream)
+                _lib.call("ns_attn_decode", C.byref(pa), self._attn_ws_ptr, self.attn_ws_bytes, stream)
+                _lib.call("ns_dense_gemv", C.byref(po), stream)
             self.moe[l](xa.view(1, -1), out=nxt.view(1, -1), add_residual=(self.rank == 0), ids=self.ids[l:l + 1])
             if self.world > 1:
                 torch.distributed.all_reduce(nxt, group=self.group)

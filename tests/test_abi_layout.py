@@ -14,6 +14,7 @@ STRUCTS = {
     "ns_dense_gemv_t": _lib.DenseGemvParams,
     "ns_attn_decode_t": _lib.AttnDecodeParams,
     "ns_l2_prefetch_t": _lib.L2Prefetch,
+    "ns_attn_block_t": _lib.AttnBlockParams,
 }
 
 

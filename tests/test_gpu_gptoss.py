@@ -155,19 +155,21 @@ def test_embedding_row_is_exact():
     assert torch.equal(out, tab[777].float())
 
 
-def _golden_decoder(use_graph):
+def _golden_decoder(use_graph, fused=True):
     g = goldens.load("model")
     c = goldens.cases(g)["gptoss_2layer"]
     shape = GptOssShape(n_layer=c["n_layer"], vocab_size=c["vocab_size"])
-    dec = GptOssDecoder(shape, "cuda", seed=c["seed"], ctx=c["ctx"], max_ctx=512, use_graph=use_graph)
+    dec = GptOssDecoder(shape, "cuda", seed=c["seed"], ctx=c["ctx"], max_ctx=512, use_graph=use_graph,
+                        fused_attention=fused)
     assert dec.capture() == use_graph
     return g, c, dec
 
 
-@pytest.mark.parametrize("use_graph", [True, False])
-def test_decoder_matches_reference_forward(use_graph):
-    """Three consecutive tokens (each appending to the KV cache) against the reference's own forward."""
-    g, c, dec = _golden_decoder(use_graph)
+@pytest.mark.parametrize("use_graph,fused", [(True, True), (False, True), (True, False)])
+def test_decoder_matches_reference_forward(use_graph, fused):
+    """Three consecutive tokens (each appending to the KV cache) against the reference's own forward,
+    with the attention block as one cooperative kernel (fused) or as its three kernels."""
+    g, c, dec = _golden_decoder(use_graph, fused)
     for i, tok in enumerate(c["tokens"]):
         dec.set_token(tok, c["ctx"] + i)
         logits = dec.step().cpu().numpy()
@@ -189,3 +191,52 @@ def test_decoder_end_to_end_from_host_and_repeatable():
     again = dec.decode(tok, pos_host=pos).numpy()
     assert np.array_equal(first, again)
     dec.release()
+
+
+@pytest.mark.parametrize("window,pos,max_ctx,n_head,n_kv", [
+    (0, 2048, 2112, 64, 8),       # GPT-OSS full layer at 2k context
+    (128, 2048, 2112, 64, 8),     # GPT-OSS sliding layer
+    (128, 50, 128, 64, 8),        # fewer keys than the window
+    (0, 0, 64, 64, 8),            # the first token
+    (0, 5, 64, 16, 2),            # fewer keys than splits
+    (0, 700, 1024, 32, 8),        # 4 query heads per kv head
+])
+def test_attention_block_matches_oracle(window, pos, max_ctx, n_head, n_kv):
+    """ns_attn_block (one cooperative launch) against the oracle's attention block on the same
+    weights and history: the output row, the appended key/value and an untouched history."""
+    from tests.model_twin import TwinWeights, kv_history
+
+    H = 2880
+    shape = GptOssShape(n_layer=1, n_embd=H, n_head=n_head, n_head_kv=n_kv, sliding_window=max(window, 1))
+    seed = 40 + pos
+    from nurostream_b200.gptoss import AttnLayer
+    A = AttnLayer(shape, 0, torch.device("cuda"), seed, max_ctx, pos)
+    A.window = window
+    x = _f32(H, seed, 99)
+    out = torch.full((H,), float("nan"), device="cuda")
+    cos, sin = yarn_tables(shape, max_ctx)
+    cos_d, sin_d = cos.cuda(), sin.cuda()
+    posd = torch.tensor([pos], dtype=torch.int32, device="cuda")
+    b = A.block_params(x, posd, cos_d, sin_d, out)
+    n = C.c_size_t(0)
+    _lib.call("ns_attn_block_workspace_bytes", C.byref(b), C.byref(n))
+    ws = torch.zeros(n.value + 256, dtype=torch.uint8, device="cuda")
+    wp = ws.data_ptr() + (-ws.data_ptr()) % 256
+    _lib.call("ns_attn_block", C.byref(b), wp, n.value, torch.cuda.current_stream().cuda_stream)
+    torch.cuda.synchronize()
+    assert _lib.device_error() == 0
+    W = TwinWeights(shape, seed)
+    kv = kv_history(shape, seed, pos)
+    cfg = W.config()
+    cfg["sliding_window"] = window  # the oracle's layer 0 slides by this window (0: full attention)
+    want = omodel.attention_block(x.cpu().numpy()[None, :], W, 0, cfg, kv, pos, acc=np.float64)[0]
+    assert_rel_close(out.cpu().numpy(), want, 2e-5, f"block pos={pos} window={window}")
+    k_new = kv[0][0][:, pos]
+    assert_rel_close(A.k_cache[:, pos].cpu().numpy(), k_new, 1e-5, "appended key")
+    if pos:
+        np.testing.assert_array_equal(A.k_cache[:, :pos].cpu().numpy(), kv_history(shape, seed, pos)[0][0])
+    # a second launch from the same state gives the same bits
+    first = out.clone()
+    _lib.call("ns_attn_block", C.byref(b), wp, n.value, torch.cuda.current_stream().cuda_stream)
+    torch.cuda.synchronize()
+    assert torch.equal(first, out)
