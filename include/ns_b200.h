@@ -359,7 +359,8 @@ int ns_moe_select_kernel(int path);
 /*
  * Phase tracer of the fused layer (profiling aid; no reference counterpart --
  * the reference times with time.perf_counter around whole calls).  While set,
- * every ns_moe_decode_layer launch on the current device writes, per CTA,
+ * every ns_moe_decode_layer and ns_attn_block launch on the current device
+ * writes, per CTA,
  * NS_TRACE_EVENTS globaltimer stamps (ns) to buf[cta * NS_TRACE_EVENTS + event].
  * buf = NULL switches tracing off.  buf must hold grid * NS_TRACE_EVENTS uint64.
  */

@@ -51,7 +51,11 @@ struct AbArgs {
   float* yqkv;                               // q, k, v (workspace)
   float* part;                               // [kv head][split][query head][2 + hd] (workspace)
   float* attn;                               // merged attention output, n_head * hd (workspace)
+  unsigned long long* trace;                 // per-CTA phase stamps (ns_moe_set_trace), or null
 };
+
+// Phase stamps of the tracer (per CTA, NS_TRACE_EVENTS slots).
+enum { kAbEvStart = 0, kAbEvNorm, kAbEvPhaseA, kAbEvBar1, kAbEvPhaseB, kAbEvBar2, kAbEvPhaseC, kAbEvBar3, kAbEvEnd };
 
 // Tiles of one CTA's byte stream: 0 = q/k/v rows, 1 = a key/value block, 2 = o-proj rows.
 struct AbPlan {
@@ -185,6 +189,7 @@ __global__ void __launch_bounds__(kAbThreads, 1) attn_block_kernel(const __grid_
   const int nT = pl.nA + pl.nB + pl.nD;
 
   if (tid == 0) {
+    stamp(a.trace, kAbEvStart);
     S.issued = 0;
     S.prod_done = 0;
     S.ok = pos_ok ? 1 : 0;
@@ -306,6 +311,7 @@ __global__ void __launch_bounds__(kAbThreads, 1) attn_block_kernel(const __grid_
     }
   }
   griddep_launch_dependents();
+  if (tid == 0) stamp(a.trace, kAbEvNorm);
 
   // ---- phase A: q, k, v rows of this CTA
   bool alive = *okp != 0;
@@ -323,8 +329,10 @@ __global__ void __launch_bounds__(kAbThreads, 1) attn_block_kernel(const __grid_
   }
   {  // every CTA arrives at every grid barrier, also after a failure of its own, so that no other
     // CTA waits for it until its limit
+    if (tid == 0) stamp(a.trace, kAbEvPhaseA);
     const bool synced = ab_grid_sync(a.bar, G, tid, okp);
     alive = alive && synced;
+    if (tid == 0) stamp(a.trace, kAbEvBar1);
   }
 
   // ---- phase B: this CTA's key split of one kv head
@@ -424,33 +432,60 @@ __global__ void __launch_bounds__(kAbThreads, 1) attn_block_kernel(const __grid_
   }
   {  // every CTA arrives at every grid barrier, also after a failure of its own, so that no other
     // CTA waits for it until its limit
+    if (tid == 0) stamp(a.trace, kAbEvPhaseB);
     const bool synced = ab_grid_sync(a.bar, G, tid, okp);
     alive = alive && synced;
+    if (tid == 0) stamp(a.trace, kAbEvBar2);
   }
 
-  // ---- phase C: one query head per CTA merges its splits with the sink
+  // ---- phase C: one query head per CTA merges its splits with the sink.  The splits' records are
+  // loaded 16 at a time, all loads of a group in flight together (one L2 round trip per group), and
+  // merged with a running maximum, in split order.
   if (alive && c < p.n_head && warp == 0) {
     const int h = c, g = h / n_rep, r = h % n_rep;
     const float* base = a.part + ((int64_t)g * a.splits * kAbMaxRep + r) * kAbPartStride;
+    constexpr int kGrp = 16;
     float mt = p.sinks ? p.sinks[h] : -INFINITY;
-    for (int t = 0; t < a.splits; ++t) mt = fmaxf(mt, __ldcg(base + (int64_t)t * kAbMaxRep * kAbPartStride));
-    float lt = p.sinks ? expf(p.sinks[h] - mt) : 0.f, o0 = 0.f, o1 = 0.f;
-    for (int t = 0; t < a.splits; ++t) {
-      const float* ph = base + (int64_t)t * kAbMaxRep * kAbPartStride;
-      const float ms = __ldcg(ph);
-      if (ms == -INFINITY) continue;  // a split with no keys
-      const float f = expf(ms - mt);
-      lt = fmaf(__ldcg(ph + 1), f, lt);
-      o0 = fmaf(__ldcg(ph + 2 + 2 * lane), f, o0);
-      o1 = fmaf(__ldcg(ph + 3 + 2 * lane), f, o1);
+    float lt = p.sinks ? 1.0f : 0.f, o0 = 0.f, o1 = 0.f;  // relative to mt
+    for (int t0 = 0; t0 < a.splits; t0 += kGrp) {
+      float ms[kGrp], ls[kGrp], x0[kGrp], x1[kGrp];
+#pragma unroll
+      for (int u = 0; u < kGrp; ++u) {
+        const int t = t0 + u;
+        const float* ph = base + (int64_t)t * kAbMaxRep * kAbPartStride;
+        const bool in = t < a.splits;
+        ms[u] = in ? __ldcg(ph) : -INFINITY;
+        ls[u] = in ? __ldcg(ph + 1) : 0.f;
+        x0[u] = in ? __ldcg(ph + 2 + 2 * lane) : 0.f;
+        x1[u] = in ? __ldcg(ph + 3 + 2 * lane) : 0.f;
+      }
+      float mg = mt;
+#pragma unroll
+      for (int u = 0; u < kGrp; ++u) mg = fmaxf(mg, ms[u]);
+      if (mg != mt) {  // rescale what was merged so far to the new maximum
+        const float f = mt == -INFINITY ? 0.f : expf(mt - mg);
+        lt *= f;
+        o0 *= f;
+        o1 *= f;
+        mt = mg;
+      }
+#pragma unroll
+      for (int u = 0; u < kGrp; ++u)
+        if (ms[u] != -INFINITY) {  // a split with no keys adds nothing
+          const float f = expf(ms[u] - mt);
+          lt = fmaf(ls[u], f, lt);
+          o0 = fmaf(x0[u], f, o0);
+          o1 = fmaf(x1[u], f, o1);
+        }
     }
     a.attn[(int64_t)h * hd + 2 * lane] = o0 / lt;
     a.attn[(int64_t)h * hd + 2 * lane + 1] = o1 / lt;
   }
-  {  // every CTA arrives at every grid barrier, also after a failure of its own, so that no other
-    // CTA waits for it until its limit
+  {
+    if (tid == 0) stamp(a.trace, kAbEvPhaseC);
     const bool synced = ab_grid_sync(a.bar, G, tid, okp);
     alive = alive && synced;
+    if (tid == 0) stamp(a.trace, kAbEvBar3);
   }
 
   // ---- phase D: o-proj rows of this CTA, + bias, + residual
@@ -481,6 +516,7 @@ __global__ void __launch_bounds__(kAbThreads, 1) attn_block_kernel(const __grid_
     }
   }
 
+  if (tid == 0) stamp(a.trace, kAbEvEnd);
   if (!alive && tid == 0) {
     // let the copies still in flight land before the CTA's shared memory goes away (bounded waits)
     raise_device_error(NS_DEVERR_COPY_WAIT);
@@ -587,6 +623,7 @@ extern "C" int ns_attn_block(const ns_attn_block_t* p, void* workspace, size_t w
   a.yqkv = reinterpret_cast<float*>(ws + oy);
   a.part = reinterpret_cast<float*>(ws + op);
   a.attn = reinterpret_cast<float*>(ws + oa);
+  a.trace = g_trace_buf[trace_slot()];
   const int na = (p->H / 8 + kAbWarps * 32 - 1) / (kAbWarps * 32), nd = (a.qd / 8 + kAbWarps * 32 - 1) / (kAbWarps * 32);
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   if (na == 1 && nd == 1) return launch_ab<1, 1>(a, nsm, s);
