@@ -2,9 +2,8 @@
 //
 //   q, k, v = W_{q,k,v} rms_norm(x) + b          (phase A, every CTA a slice of the rows)
 //   --- grid barrier ---
-//   per (kv head g, key split s): RoPE, KV append, online-softmax partial over the split's keys
-//   --- grid barrier ---                          (phase B)
-//   per query head: merge of the splits with the sink    (phase C)
+//   per (kv head g, key split s): RoPE, KV append, online-softmax partial over the split's keys;
+//   the last split of kv head g to finish merges all of them with the sinks (phase B)
 //   --- grid barrier ---
 //   out = x + W_o attn + b_o                      (phase D, every CTA a slice of the rows)
 //
@@ -51,11 +50,12 @@ struct AbArgs {
   float* yqkv;                               // q, k, v (workspace)
   float* part;                               // [kv head][split][query head][2 + hd] (workspace)
   float* attn;                               // merged attention output, n_head * hd (workspace)
+  unsigned* cnt;                             // per kv head: splits done (reset by the merging CTA)
   unsigned long long* trace;                 // per-CTA phase stamps (ns_moe_set_trace), or null
 };
 
 // Phase stamps of the tracer (per CTA, NS_TRACE_EVENTS slots).
-enum { kAbEvStart = 0, kAbEvNorm, kAbEvPhaseA, kAbEvBar1, kAbEvPhaseB, kAbEvBar2, kAbEvPhaseC, kAbEvBar3, kAbEvEnd };
+enum { kAbEvStart = 0, kAbEvNorm, kAbEvPhaseA, kAbEvBar1, kAbEvPhaseB, kAbEvBar2, kAbEvEnd };
 
 // Tiles of one CTA's byte stream: 0 = q/k/v rows, 1 = a key/value block, 2 = o-proj rows.
 struct AbPlan {
@@ -102,17 +102,20 @@ __device__ __forceinline__ void ab_copy(uint8_t* dst, const uint8_t* src, uint32
 __device__ __forceinline__ bool ab_grid_sync(unsigned long long* bar, int G, int tid, volatile int* ok) {
   named_sync(1, kAbWarps * 32);
   if (tid == 0) {
-    __threadfence();
-    const unsigned long long old = atomicAdd(bar, 1ull);
+    // one release add (orders this CTA's writes, which the CTA barrier gathered, before it), then
+    // acquire loads until every CTA has arrived
+    unsigned long long old;
+    asm volatile("atom.add.release.gpu.global.u64 %0, [%1], 1;" : "=l"(old) : "l"(bar) : "memory");
     const unsigned long long target = (old / (unsigned)G + 1ull) * (unsigned)G;
-    const uint64_t t0 = globaltimer_ns();
-    while (ld_acquire_u64(bar) < target) {
-      if (globaltimer_ns() - t0 > kWaitLimitNs) {
-        raise_device_error(NS_DEVERR_GRID_WAIT);
-        *ok = 0;
-        break;
+    if (ld_acquire_u64(bar) < target) {
+      const uint64_t t0 = globaltimer_ns();
+      while (ld_acquire_u64(bar) < target) {
+        if (globaltimer_ns() - t0 > kWaitLimitNs) {
+          raise_device_error(NS_DEVERR_GRID_WAIT);
+          *ok = 0;
+          break;
+        }
       }
-      __nanosleep(32);
     }
   }
   named_sync(1, kAbWarps * 32);
@@ -169,6 +172,7 @@ struct AbSmem {
   int issued;
   int prod_done;
   int ok;
+  int last;  // this CTA merges its kv head's splits
 };
 
 template <int NCH_A, int NCH_D>
@@ -181,19 +185,15 @@ __global__ void __launch_bounds__(kAbThreads, 1) attn_block_kernel(const __grid_
   const int G = gridDim.x, c = blockIdx.x;
   const int H = p.H, hd = kAbHd, n_rep = p.n_head / p.n_head_kv;
 
-  // the token's position: written before this step's kernels (chain invariant)
-  int pos = *p.pos;
-  const bool pos_ok = pos >= 0 && pos < p.max_ctx;
-  if (!pos_ok) pos = 0;
-  const AbPlan pl = ab_plan(a, pos, c, G);
-  const int nT = pl.nA + pl.nB + pl.nD;
+  // the token's position (written before this step's kernels: chain invariant).  The load is issued
+  // here and first waited for where the key split is planned, after the q/k/v rows are requested.
+  const int pos_raw = *p.pos;
 
   if (tid == 0) {
     stamp(a.trace, kAbEvStart);
     S.issued = 0;
     S.prod_done = 0;
-    S.ok = pos_ok ? 1 : 0;
-    if (!pos_ok && c == 0) raise_device_error(NS_DEVERR_ROUTE);
+    S.ok = 1;
     for (int i = 0; i < kAbStages; ++i) {
       mbar_init(&S.full[i], 1);
       mbar_init(&S.empty[i], kAbWarps);
@@ -204,27 +204,40 @@ __global__ void __launch_bounds__(kAbThreads, 1) attn_block_kernel(const __grid_
 
   if (warp == kAbWarps) {
     // ================================================================= producer: the byte stream
-    if (lane == 0 && S.ok) {
+    if (lane == 0) {
       const uint8_t* wseg[3] = {static_cast<const uint8_t*>(p.wq), static_cast<const uint8_t*>(p.wk),
                                 static_cast<const uint8_t*>(p.wv)};
       const int seg0[4] = {0, a.qd, a.qd + a.kvd, a.qkv_rows};
-      const int64_t cache_g = (int64_t)pl.g * p.max_ctx * hd;
+      // the q/k/v tiles do not depend on the position: they go out first, the rest once it is known
+      AbPlan pl = ab_plan(a, 0, c, G);
       int i = 0;
-      for (; i < nT; ++i) {
+      bool stop = false;
+      auto next_slot = [&](int i) -> int {
         const int slot = i % kAbStages;
-        if (i >= kAbStages && !mbar_wait_bounded(&S.empty[slot], (uint32_t)((i / kAbStages - 1) & 1))) break;
+        if (i >= kAbStages && !mbar_wait_bounded(&S.empty[slot], (uint32_t)((i / kAbStages - 1) & 1))) stop = true;
+        return slot;
+      };
+      for (; i < pl.nA; ++i) {  // q/k/v rows (three matrices, one concatenated row space)
+        const int slot = next_slot(i);
+        if (stop) break;
         uint8_t* dst = ring + (size_t)slot * kAbStageBytes;
-        if (i < pl.nA) {  // q/k/v rows (three matrices, one concatenated row space)
-          const int r0 = pl.a0 + i * kAbTileRows, r1 = min(r0 + kAbTileRows, pl.a1);
-          mbar_arrive_expect_tx(&S.full[slot], (uint32_t)((r1 - r0) * H * 2));
-          for (int sg = 0; sg < 3; ++sg) {
-            const int lo = max(r0, seg0[sg]), hi = min(r1, seg0[sg + 1]);
-            if (lo < hi)
-              ab_copy(dst + (size_t)(lo - r0) * H * 2, wseg[sg] + (int64_t)(lo - seg0[sg]) * H * 2,
-                      (uint32_t)((hi - lo) * H * 2), &S.full[slot]);
-          }
-        } else if (i < pl.nA + pl.nB) {  // keys / values of one block (slots below pos only)
-          const int b = i - pl.nA;
+        const int r0 = pl.a0 + i * kAbTileRows, r1 = min(r0 + kAbTileRows, pl.a1);
+        mbar_arrive_expect_tx(&S.full[slot], (uint32_t)((r1 - r0) * H * 2));
+        for (int sg = 0; sg < 3; ++sg) {
+          const int lo = max(r0, seg0[sg]), hi = min(r1, seg0[sg + 1]);
+          if (lo < hi)
+            ab_copy(dst + (size_t)(lo - r0) * H * 2, wseg[sg] + (int64_t)(lo - seg0[sg]) * H * 2,
+                    (uint32_t)((hi - lo) * H * 2), &S.full[slot]);
+        }
+      }
+      const int pos = pos_raw;
+      if (!stop && pos >= 0 && pos < p.max_ctx) {
+        pl = ab_plan(a, pos, c, G);
+        const int64_t cache_g = (int64_t)pl.g * p.max_ctx * hd;
+        for (int b = 0; b < pl.nB; ++b, ++i) {  // keys / values of one block (slots below pos only)
+          const int slot = next_slot(i);
+          if (stop) break;
+          uint8_t* dst = ring + (size_t)slot * kAbStageBytes;
           const int kb = pl.j0 + b * kAbKeyBlock, ke = min(kb + kAbKeyBlock, pl.j1), kc = min(ke, pos);
           const uint32_t n = kc > kb ? (uint32_t)((kc - kb) * hd * 4) : 0u;
           mbar_arrive_expect_tx(&S.full[slot], 2 * n);
@@ -233,10 +246,13 @@ __global__ void __launch_bounds__(kAbThreads, 1) attn_block_kernel(const __grid_
             ab_copy(dst + kAbKeyBlock * hd * 4, reinterpret_cast<const uint8_t*>(p.v_cache + cache_g + (int64_t)kb * hd),
                     n, &S.full[slot]);
           }
-        } else {  // o-proj rows
-          const int t = i - pl.nA - pl.nB;
+        }
+        const int kq = p.n_head * hd;
+        for (int t = 0; t < pl.nD && !stop; ++t, ++i) {  // o-proj rows
+          const int slot = next_slot(i);
+          if (stop) break;
+          uint8_t* dst = ring + (size_t)slot * kAbStageBytes;
           const int r0 = pl.d0 + t * kAbTileRows, r1 = min(r0 + kAbTileRows, pl.d1);
-          const int kq = p.n_head * hd;
           mbar_arrive_expect_tx(&S.full[slot], (uint32_t)((r1 - r0) * kq * 2));
           ab_copy(dst, static_cast<const uint8_t*>(p.wo) + (int64_t)r0 * kq * 2, (uint32_t)((r1 - r0) * kq * 2),
                   &S.full[slot]);
@@ -260,36 +276,52 @@ __global__ void __launch_bounds__(kAbThreads, 1) attn_block_kernel(const __grid_
     if (lane == 0) mbar_arrive(&S.empty[i % kAbStages]);
   };
 
+  AbPlan pl = ab_plan(a, 0, c, G);  // the row ranges (the key split is planned once pos is known)
   griddep_wait();
-  // ---- x, RMSNorm, staged epilogue data
+  // ---- x, RMSNorm weight, staged epilogue data: every load issued before any is used
   float xv[NCH_A][8];
   {
     const int nchunk = H / 8;
-    float ss = 0.f;
+    float wn[NCH_A][8];
 #pragma unroll
     for (int cc = 0; cc < NCH_A; ++cc) {
       const int ch = tid + cc * kAbWarps * 32;
-      if (ch < nchunk) {
-        const float4 lo = reinterpret_cast<const float4*>(p.x)[2 * ch];
-        const float4 hi = reinterpret_cast<const float4*>(p.x)[2 * ch + 1];
-        xv[cc][0] = lo.x; xv[cc][1] = lo.y; xv[cc][2] = lo.z; xv[cc][3] = lo.w;
-        xv[cc][4] = hi.x; xv[cc][5] = hi.y; xv[cc][6] = hi.z; xv[cc][7] = hi.w;
-      } else {
-#pragma unroll
-        for (int j = 0; j < 8; ++j) xv[cc][j] = 0.f;
-      }
-#pragma unroll
-      for (int j = 0; j < 8; ++j) ss = fmaf(xv[cc][j], xv[cc][j], ss);
+      const bool in = ch < nchunk;
+      const float4 z = make_float4(0.f, 0.f, 0.f, 0.f);
+      const float4 lo = in ? reinterpret_cast<const float4*>(p.x)[2 * ch] : z;
+      const float4 hi = in ? reinterpret_cast<const float4*>(p.x)[2 * ch + 1] : z;
+      const float4 wl = in ? reinterpret_cast<const float4*>(p.norm_w)[2 * ch] : z;
+      const float4 wh = in ? reinterpret_cast<const float4*>(p.norm_w)[2 * ch + 1] : z;
+      xv[cc][0] = lo.x; xv[cc][1] = lo.y; xv[cc][2] = lo.z; xv[cc][3] = lo.w;
+      xv[cc][4] = hi.x; xv[cc][5] = hi.y; xv[cc][6] = hi.z; xv[cc][7] = hi.w;
+      wn[cc][0] = wl.x; wn[cc][1] = wl.y; wn[cc][2] = wl.z; wn[cc][3] = wl.w;
+      wn[cc][4] = wh.x; wn[cc][5] = wh.y; wn[cc][6] = wh.z; wn[cc][7] = wh.w;
     }
-    for (int i = tid; i < pl.a1 - pl.a0; i += kAbWarps * 32) {
-      const int row = pl.a0 + i;
+    float ba = 0.f, bd = 0.f, rd = 0.f;  // one staged row each (a CTA owns < 256 rows of either)
+    const int ia = tid, id = tid;
+    if (ia < pl.a1 - pl.a0) {
+      const int row = pl.a0 + ia;
       const float* b = row < a.qd ? p.bq : row < a.qd + a.kvd ? p.bk : p.bv;
       const int lr = row < a.qd ? row : row < a.qd + a.kvd ? row - a.qd : row - a.qd - a.kvd;
-      S.bias_a[i] = b ? b[lr] : 0.f;
+      ba = b ? b[lr] : 0.f;
     }
-    for (int i = tid; i < pl.d1 - pl.d0; i += kAbWarps * 32) {
-      S.bias_d[i] = p.bo ? p.bo[pl.d0 + i] : 0.f;
-      S.resid[i] = p.x[pl.d0 + i];
+    if (id < pl.d1 - pl.d0) {
+      bd = p.bo ? p.bo[pl.d0 + id] : 0.f;
+      rd = p.x[pl.d0 + id];
+    }
+    float ss = 0.f;
+#pragma unroll
+    for (int cc = 0; cc < NCH_A; ++cc)
+#pragma unroll
+      for (int j = 0; j < 8; ++j) ss = fmaf(xv[cc][j], xv[cc][j], ss);
+    if (ia < pl.a1 - pl.a0) S.bias_a[ia] = ba;
+    if (id < pl.d1 - pl.d0) {
+      S.bias_d[id] = bd;
+      S.resid[id] = rd;
+    }
+    if (tid == 0 && !(pos_raw >= 0 && pos_raw < p.max_ctx)) {  // a position outside the cache: no work
+      *okp = 0;
+      if (c == 0) raise_device_error(NS_DEVERR_ROUTE);
     }
     ss = warp_sum(ss);
     if (lane == 0) S.ssq[warp] = ss;
@@ -299,16 +331,9 @@ __global__ void __launch_bounds__(kAbThreads, 1) attn_block_kernel(const __grid_
     for (int w = 0; w < kAbWarps; ++w) tot += S.ssq[w];
     const float r = 1.0f / sqrtf(tot / (float)H + p.rms_eps);
 #pragma unroll
-    for (int cc = 0; cc < NCH_A; ++cc) {
-      const int ch = tid + cc * kAbWarps * 32;
-      if (ch < nchunk) {
-        const float4 lo = reinterpret_cast<const float4*>(p.norm_w)[2 * ch];
-        const float4 hi = reinterpret_cast<const float4*>(p.norm_w)[2 * ch + 1];
-        const float wn[8] = {lo.x, lo.y, lo.z, lo.w, hi.x, hi.y, hi.z, hi.w};
+    for (int cc = 0; cc < NCH_A; ++cc)
 #pragma unroll
-        for (int j = 0; j < 8; ++j) xv[cc][j] = __fmul_rn(__fmul_rn(xv[cc][j], r), wn[j]);  // (x * r) * w
-      }
-    }
+      for (int j = 0; j < 8; ++j) xv[cc][j] = __fmul_rn(__fmul_rn(xv[cc][j], r), wn[cc][j]);  // (x * r) * w
   }
   griddep_launch_dependents();
   if (tid == 0) stamp(a.trace, kAbEvNorm);
@@ -336,6 +361,8 @@ __global__ void __launch_bounds__(kAbThreads, 1) attn_block_kernel(const __grid_
   }
 
   // ---- phase B: this CTA's key split of one kv head
+  const int pos = alive ? pos_raw : 0;
+  pl = ab_plan(a, pos, c, G);
   if (alive && pl.item >= 0) {
     const float* cs = p.rope_cos + (int64_t)pos * hd;
     const float* sn = p.rope_sin + (int64_t)pos * hd;
@@ -428,64 +455,66 @@ __global__ void __launch_bounds__(kAbThreads, 1) attn_block_kernel(const __grid_
       ph[2 + 2 * lane] = acc0;
       ph[3 + 2 * lane] = acc1;
     }
+    // the last split of kv head g to finish merges all of them (no grid barrier for the merge)
+    named_sync(1, kAbWarps * 32);
+    if (tid == 0) {
+      __threadfence();
+      S.last = atom_add_acq_rel(a.cnt + g, 1u) == (unsigned)(a.splits - 1);
+    }
+    named_sync(1, kAbWarps * 32);
+    if (S.last) {
+      __threadfence();
+      if (head_ok) {
+        // the splits' records, 16 at a time with all loads of a group in flight, merged with a
+        // running maximum in split order, together with the head's sink
+        const int h = g * n_rep + warp;
+        const float* base = a.part + ((int64_t)g * a.splits * kAbMaxRep + warp) * kAbPartStride;
+        constexpr int kGrp = 16;
+        float mt = p.sinks ? p.sinks[h] : -INFINITY;
+        float lt = p.sinks ? 1.0f : 0.f, o0 = 0.f, o1 = 0.f;  // relative to mt
+        for (int t0 = 0; t0 < a.splits; t0 += kGrp) {
+          float ms[kGrp], ls[kGrp], x0[kGrp], x1[kGrp];
+#pragma unroll
+          for (int u = 0; u < kGrp; ++u) {
+            const int t = t0 + u;
+            const float* q = base + (int64_t)t * kAbMaxRep * kAbPartStride;
+            const bool in = t < a.splits;
+            ms[u] = in ? __ldcg(q) : -INFINITY;
+            ls[u] = in ? __ldcg(q + 1) : 0.f;
+            x0[u] = in ? __ldcg(q + 2 + 2 * lane) : 0.f;
+            x1[u] = in ? __ldcg(q + 3 + 2 * lane) : 0.f;
+          }
+          float mg = mt;
+#pragma unroll
+          for (int u = 0; u < kGrp; ++u) mg = fmaxf(mg, ms[u]);
+          if (mg != mt) {  // rescale what was merged so far to the new maximum
+            const float f = mt == -INFINITY ? 0.f : expf(mt - mg);
+            lt *= f;
+            o0 *= f;
+            o1 *= f;
+            mt = mg;
+          }
+#pragma unroll
+          for (int u = 0; u < kGrp; ++u)
+            if (ms[u] != -INFINITY) {  // a split with no keys adds nothing
+              const float f = expf(ms[u] - mt);
+              lt = fmaf(ls[u], f, lt);
+              o0 = fmaf(x0[u], f, o0);
+              o1 = fmaf(x1[u], f, o1);
+            }
+        }
+        a.attn[(int64_t)h * hd + 2 * lane] = o0 / lt;
+        a.attn[(int64_t)h * hd + 2 * lane + 1] = o1 / lt;
+      }
+      if (tid == 0) a.cnt[g] = 0u;  // ready for the next launch (stream-ordered)
+    }
     alive = *okp != 0;
   }
-  {  // every CTA arrives at every grid barrier, also after a failure of its own, so that no other
-    // CTA waits for it until its limit
+  {
     if (tid == 0) stamp(a.trace, kAbEvPhaseB);
     const bool synced = ab_grid_sync(a.bar, G, tid, okp);
     alive = alive && synced;
     if (tid == 0) stamp(a.trace, kAbEvBar2);
-  }
-
-  // ---- phase C: one query head per CTA merges its splits with the sink.  The splits' records are
-  // loaded 16 at a time, all loads of a group in flight together (one L2 round trip per group), and
-  // merged with a running maximum, in split order.
-  if (alive && c < p.n_head && warp == 0) {
-    const int h = c, g = h / n_rep, r = h % n_rep;
-    const float* base = a.part + ((int64_t)g * a.splits * kAbMaxRep + r) * kAbPartStride;
-    constexpr int kGrp = 16;
-    float mt = p.sinks ? p.sinks[h] : -INFINITY;
-    float lt = p.sinks ? 1.0f : 0.f, o0 = 0.f, o1 = 0.f;  // relative to mt
-    for (int t0 = 0; t0 < a.splits; t0 += kGrp) {
-      float ms[kGrp], ls[kGrp], x0[kGrp], x1[kGrp];
-#pragma unroll
-      for (int u = 0; u < kGrp; ++u) {
-        const int t = t0 + u;
-        const float* ph = base + (int64_t)t * kAbMaxRep * kAbPartStride;
-        const bool in = t < a.splits;
-        ms[u] = in ? __ldcg(ph) : -INFINITY;
-        ls[u] = in ? __ldcg(ph + 1) : 0.f;
-        x0[u] = in ? __ldcg(ph + 2 + 2 * lane) : 0.f;
-        x1[u] = in ? __ldcg(ph + 3 + 2 * lane) : 0.f;
-      }
-      float mg = mt;
-#pragma unroll
-      for (int u = 0; u < kGrp; ++u) mg = fmaxf(mg, ms[u]);
-      if (mg != mt) {  // rescale what was merged so far to the new maximum
-        const float f = mt == -INFINITY ? 0.f : expf(mt - mg);
-        lt *= f;
-        o0 *= f;
-        o1 *= f;
-        mt = mg;
-      }
-#pragma unroll
-      for (int u = 0; u < kGrp; ++u)
-        if (ms[u] != -INFINITY) {  // a split with no keys adds nothing
-          const float f = expf(ms[u] - mt);
-          lt = fmaf(ls[u], f, lt);
-          o0 = fmaf(x0[u], f, o0);
-          o1 = fmaf(x1[u], f, o1);
-        }
-    }
-    a.attn[(int64_t)h * hd + 2 * lane] = o0 / lt;
-    a.attn[(int64_t)h * hd + 2 * lane + 1] = o1 / lt;
-  }
-  {
-    if (tid == 0) stamp(a.trace, kAbEvPhaseC);
-    const bool synced = ab_grid_sync(a.bar, G, tid, okp);
-    alive = alive && synced;
-    if (tid == 0) stamp(a.trace, kAbEvBar3);
   }
 
   // ---- phase D: o-proj rows of this CTA, + bias, + residual
@@ -535,7 +564,7 @@ static int ab_check(const ns_attn_block_t* p, int nsm, int* splits) {
   if (p->H < 8 || p->H % 8 || 8 * p->H * 2 > kAbStageBytes || 8 * p->n_head * kAbHd * 2 > kAbStageBytes)
     return fail(NS_ERR_UNSUPPORTED, "ns_attn_block: H=%d, n_head=%d outside the stage size", p->H, p->n_head);
   if (p->max_ctx < 1 || p->window < 0) return fail(NS_ERR_INVALID, "ns_attn_block: bad max_ctx / window");
-  if (p->n_head > nsm) return fail(NS_ERR_UNSUPPORTED, "ns_attn_block: more query heads than SMs");
+  if (p->n_head_kv > 48) return fail(NS_ERR_UNSUPPORTED, "ns_attn_block: more than 48 kv heads");
   const int qkv = p->n_head * kAbHd + 2 * p->n_head_kv * kAbHd;
   if ((qkv + nsm - 1) / nsm > kAbMaxRows || (p->H + nsm - 1) / nsm > kAbMaxRows)
     return fail(NS_ERR_UNSUPPORTED, "ns_attn_block: more than %d rows per SM", kAbMaxRows);
@@ -545,7 +574,7 @@ static int ab_check(const ns_attn_block_t* p, int nsm, int* splits) {
 }
 
 static size_t ab_ws_layout(const ns_attn_block_t* p, int splits, size_t* off_y, size_t* off_part, size_t* off_attn) {
-  size_t off = 256;  // barrier counter
+  size_t off = 256;  // barrier counter at 0, per-kv-head split counters at 64
   *off_y = off;
   off += align_up((size_t)(p->n_head + 2 * p->n_head_kv) * kAbHd * 4, 256);
   *off_part = off;
@@ -623,6 +652,7 @@ extern "C" int ns_attn_block(const ns_attn_block_t* p, void* workspace, size_t w
   a.yqkv = reinterpret_cast<float*>(ws + oy);
   a.part = reinterpret_cast<float*>(ws + op);
   a.attn = reinterpret_cast<float*>(ws + oa);
+  a.cnt = reinterpret_cast<unsigned*>(ws + 64);
   a.trace = g_trace_buf[trace_slot()];
   const int na = (p->H / 8 + kAbWarps * 32 - 1) / (kAbWarps * 32), nd = (a.qd / 8 + kAbWarps * 32 - 1) / (kAbWarps * 32);
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
