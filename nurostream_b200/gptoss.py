@@ -159,7 +159,7 @@ class GptOssDecoder:
 
     def __init__(self, shape: GptOssShape | None = None, device="cuda", seed: int = 0, ctx: int = 2048,
                  max_ctx: int | None = None, rank: int = 0, world: int = 1, group=None, use_graph: bool = True,
-                 keep_layer_outputs: bool = False, l2_prefetch: bool = False, fused_attention: bool = True):
+                 keep_layer_outputs: bool = False, l2_prefetch: bool = False, fused_attention: bool = False):
         self.shape = shape = shape or GptOssShape()
         self.device = dev = torch.device(device)
         self.seed, self.ctx = seed, ctx

@@ -232,7 +232,7 @@ def test_attention_block_matches_oracle(window, pos, max_ctx, n_head, n_kv):
     want = omodel.attention_block(x.cpu().numpy()[None, :], W, 0, cfg, kv, pos, acc=np.float64)[0]
     assert_rel_close(out.cpu().numpy(), want, 2e-5, f"block pos={pos} window={window}")
     k_new = kv[0][0][:, pos]
-    assert_rel_close(A.k_cache[:, pos].cpu().numpy(), k_new, 2e-5, "appended key")
+    assert_rel_close(A.k_cache[:, pos].cpu().numpy(), k_new, 1e-4, "appended key (a projection output)")
     if pos:
         np.testing.assert_array_equal(A.k_cache[:, :pos].cpu().numpy(), kv_history(shape, seed, pos)[0][0])
     # a second launch from the same state gives the same bits
