@@ -46,15 +46,15 @@ UNIT = "tok/s"
 KERNEL = "moe_tc_kernel"
 
 
-def workload_config(shape, world):
+def workload_config(shape, world, batch=1):
     if shape.arch == "qwen3":
         return {
             "workload": (f"qwen3-235b-a22b-shape MoE decode path: {shape.n_layer} layers x (router softmax "
                          f"top-{shape.top_k}/{shape.n_expert} renormalised + Q4_K gate/up/down "
-                         f"{shape.hidden}x{shape.expert_ffn} + silu*up + weighted combine + residual), batch 1"),
+                         f"{shape.hidden}x{shape.expert_ffn} + silu*up + weighted combine + residual), batch {batch}"),
             "layers": shape.n_layer, "experts": shape.n_expert, "top_k": shape.top_k, "hidden": shape.hidden,
             "expert_ffn": shape.expert_ffn, "expert_format": "Q4_K (GGUF bytes, HBM-resident)",
-            "router": "bf16 weight, no bias", "global_batch": 1, "seq_len": 1,
+            "router": "bf16 weight, no bias", "global_batch": batch, "seq_len": 1,
             "parallelism": f"ep{world}" if world > 1 else "single",
             "l2": "inputs larger than L2 (expert bytes per step far above L2 126 MB)",
         }
@@ -248,13 +248,14 @@ def run_ours(args, rank, world, local_rank, group):
     dev = torch.device("cuda", local_rank)
     torch.cuda.set_device(dev)
     shape = bench_shape(args)
-    dec = MoeDecoder(shape, dev, rank, world, group, use_graph=not args.no_graph)
+    B = args.batch
+    dec = MoeDecoder(shape, dev, rank, world, group, use_graph=not args.no_graph, batch=B)
     H = shape.hidden
     npool = 64
-    pool = torch.empty((npool, 1, H), device=dev, dtype=torch.float32)
+    pool = torch.empty((npool, B, H), device=dev, dtype=torch.float32)
     synth.fill_float(pool.view(-1), 777, 1)
     host_pool = pool.cpu().pin_memory()
-    out_host = torch.empty((1, H), dtype=torch.float32, pin_memory=True)
+    out_host = torch.empty((B, H), dtype=torch.float32, pin_memory=True)
     graphed = dec.capture()
 
     def barrier():
@@ -307,21 +308,27 @@ def run_ours(args, rank, world, local_rank, group):
     if rank != 0:
         return None
     step_ms = ms / args.steps
-    tok_s = 1000.0 / step_ms
+    tok_s = 1000.0 * B / step_ms
     peak, peak_kind = measured_peaks()
     bytes_layer = shape.layer_bytes_per_token()
+    uniq = None
+    if B > 1:  # the step reads each distinct routed expert once: count them on the last step's routing
+        ids = dec.ids.view(shape.n_layer, -1).cpu()
+        uniq = [len(set(r.tolist())) for r in ids]
+        bytes_layer += (sum(uniq) / len(uniq) - shape.top_k) * shape.expert_bytes + (B - 1) * 4 * H * 3
     per_launch_s = step_ms / 1000.0 / shape.n_layer
     achieved = bytes_layer / per_launch_s / 1e9 if world == 1 else bytes_layer / per_launch_s / 1e9
     line = {
-        "metric": METRIC if shape.arch == "gpt-oss" else "decode tok/s at batch 1 (Qwen3-235B-A22B shape, MoE layers)",
+        "metric": METRIC if shape.arch == "gpt-oss" and B == 1 else
+                  f"decode tok/s at batch {B} ({'GPT-OSS-120B' if shape.arch == 'gpt-oss' else 'Qwen3-235B-A22B'} shape, MoE layers)",
         "value": round(tok_s, 2), "unit": UNIT, "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round(step_ms, 4), "higher_is_better": True,
         "scaling": "strong", "vs_baseline": None,
         "dtype": f"{GGMLType(shape.ggml_type).name.lower()} weights, fp32 accumulate",
         "data": "synthetic (seeded splitmix64 GGUF bytes generated in HBM)",
-        "config": workload_config(shape, world),
-        "e2e": {"value": round(1000.0 * args.steps / ms_e2e, 2), "unit": UNIT,
-                "h2d_bytes_per_step": H * 4, "d2h_bytes_per_step": H * 4},
+        "config": workload_config(shape, world, B),
+        "e2e": {"value": round(1000.0 * B * args.steps / ms_e2e, 2), "unit": UNIT,
+                "h2d_bytes_per_step": B * H * 4, "d2h_bytes_per_step": B * H * 4},
         "gpu_launches": shape.n_layer * args.steps,
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                      "frac": round(achieved / (peak * (1 if world == 1 else world)), 4),
@@ -334,6 +341,8 @@ def run_ours(args, rank, world, local_rank, group):
         "cuda_graph": graphed,
         "routing_identical_on_all_ranks": ids_ok,
     }
+    if uniq is not None:
+        line["roofline"]["unique_experts_per_layer"] = round(sum(uniq) / len(uniq), 2)
     traffic = ROOT / "profiles" / "moe_tc_kernel_traffic.json"
     if traffic.exists() and shape.arch == "gpt-oss":
         try:
@@ -352,6 +361,65 @@ def run_ours(args, rank, world, local_rank, group):
                        f"reference CPU path, expert matrices on a {threads}-thread pool"),
         }
     return line
+
+
+def run_stream(args):
+    """Streamed (host-resident) weights: x @ W.T with W's GGUF bytes in page-locked host memory.
+
+    One step = one pass over a 1 GiB MXFP4 matrix (K = 4096): blocks uploaded on a copy stream while
+    the previous block's GEMV runs (``nurostream_b200.stream.StreamedGemv``).  value: weight GB/s
+    through the host link + GEMV; the same pass with upload and GEMV serialised is reported beside it.
+    """
+    import torch
+
+    from nurostream_b200 import _lib, synth
+    from nurostream_b200.ggml import GGMLType, row_bytes
+    from nurostream_b200.stream import StreamedGemv
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    t, K = GGMLType.MXFP4, 4096
+    rb = row_bytes(t, K)
+    n = (1 << 30) // rb
+    w_dev = torch.empty(n * rb, dtype=torch.uint8, device=dev)
+    synth.fill_quant(w_dev, t, 0, 950, 0)
+    host = w_dev.cpu().pin_memory()
+    del w_dev
+    x = torch.empty((1, K), device=dev)
+    synth.fill_float(x.view(-1), 0, 951, 0)
+    y = torch.empty((1, n), device=dev)
+    ex = StreamedGemv(dev, block_bytes=8 << 20, depth=3)
+    for _ in range(args.warmup):
+        ex(host, t, x, n, K, out=y)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        ex(host, t, x, n, K, out=y)
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / args.steps
+    # serialised: the whole upload, then the GEMV over the device copy
+    buf = torch.empty(n * rb, dtype=torch.uint8, device=dev)
+    f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    f0.record()
+    for _ in range(args.steps):
+        buf.copy_(host, non_blocking=True)
+        _lib.call("ns_gemv", buf.data_ptr(), buf.numel(), int(t), n, K, x.data_ptr(), _lib.NS_F32, K, 1,
+                  y.data_ptr(), _lib.NS_F32, n, torch.cuda.current_stream(dev).cuda_stream)
+    f1.record()
+    torch.cuda.synchronize()
+    ms_serial = f0.elapsed_time(f1) / args.steps
+    gbs = n * rb / (ms / 1000.0) / 1e9
+    return {
+        "metric": "streamed GEMV GB/s (host-resident MXFP4 weights, batch 1)", "value": round(gbs, 1), "unit": "GB/s",
+        "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 3), "higher_is_better": True,
+        "dtype": "mxfp4 weights, fp32 accumulate", "data": "synthetic",
+        "config": {"workload": f"x @ W.T, W {n}x{K} MXFP4 ({n * rb >> 20} MiB) in page-locked host memory, "
+                               "8 MiB blocks on a copy stream, 3 in flight"},
+        "serialised_ms_per_step": round(ms_serial, 3),
+        "serialised_gbs": round(n * rb / (ms_serial / 1000.0) / 1e9, 1),
+    }
 
 
 def full_decode_config(shape, world, ctx):
@@ -920,8 +988,9 @@ def main():
     ap.add_argument("--ref-layers", type=int, default=2)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-graph", action="store_true")
-    ap.add_argument("--workload", choices=["decode", "moe", "gemv", "qwen3", "prefill"], default="decode")
+    ap.add_argument("--workload", choices=["decode", "moe", "gemv", "qwen3", "prefill", "stream"], default="decode")
     ap.add_argument("--ctx", type=int, default=2048, help="KV-cache positions before the decoded token")
+    ap.add_argument("--batch", type=int, default=1, help="token rows per decode step (--workload moe / qwen3)")
     ap.add_argument("--prefill-tokens", type=int, default=512)
     ap.add_argument("--gemv-case", default="", help="run one GEMV case only, e.g. MXFP4:14336")
     args = ap.parse_args()
@@ -936,6 +1005,9 @@ def main():
     if args.workload == "gemv":
         for line in run_gemv_sweep(args):
             print(json.dumps(line), flush=True)
+        return
+    if args.workload == "stream":
+        print(json.dumps(run_stream(args)), flush=True)
         return
     if args.workload == "prefill" and args.impl == "ours" and world == 1:
         print(json.dumps(run_prefill(args)), flush=True)

@@ -69,19 +69,23 @@ def synth_moe_layer(sh: MoeShape, l: int, dev, lo: int, hi: int, max_tokens: int
 
 class MoeDecoder:
     def __init__(self, shape: MoeShape, device: torch.device | str = "cuda", rank: int = 0, world: int = 1,
-                 group=None, use_graph: bool = True, max_tokens: int = 1, keep_layer_outputs: bool = False):
+                 group=None, use_graph: bool = True, max_tokens: int = 1, keep_layer_outputs: bool = False,
+                 batch: int = 1):
         self.shape = shape
+        self.batch = batch            # token rows of one decode step (each layer one fused launch over all)
+        max_tokens = max(max_tokens, batch)
         self.max_tokens = max_tokens  # rows per fused launch (prefill runs slices of this many)
         self.device = torch.device(device)
         self.rank, self.world, self.group = rank, world, group
         self.lo, self.hi = expert_range(rank, world, shape.n_expert)
         self.layers = [self._make_layer(l) for l in range(shape.n_layer)]
         H = shape.hidden
-        self.x = torch.zeros((1, H), device=self.device, dtype=torch.float32)
+        self.x = torch.zeros((batch, H), device=self.device, dtype=torch.float32)
         # two ping-pong output buffers, or one per layer when every layer's output is kept (tests)
         nbuf = shape.n_layer if keep_layer_outputs else 2
-        self.bufs = [torch.empty((1, H), device=self.device, dtype=torch.float32) for _ in range(nbuf)]
-        self.ids = torch.zeros((shape.n_layer, shape.top_k), device=self.device, dtype=torch.int32)
+        self.bufs = [torch.empty((batch, H), device=self.device, dtype=torch.float32) for _ in range(nbuf)]
+        ids_shape = (shape.n_layer, shape.top_k) if batch == 1 else (shape.n_layer, batch, shape.top_k)
+        self.ids = torch.zeros(ids_shape, device=self.device, dtype=torch.int32)
         self.out = None
         self.graph = None
         self.use_graph = use_graph
@@ -121,7 +125,8 @@ class MoeDecoder:
         return True
 
     def step(self, x: torch.Tensor | None = None) -> torch.Tensor:
-        """One decode token through all layers; x (1, H) fp32 on device (copied into the input buffer)."""
+        """One decode step (``batch`` token rows) through all layers; x (batch, H) fp32 on device (copied
+        into the input buffer)."""
         if x is not None:
             self.x.copy_(x, non_blocking=True)
         if self.graph is not None:

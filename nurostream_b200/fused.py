@@ -69,6 +69,11 @@ def can_fuse(dtype, x: torch.Tensor) -> bool:
     )
 
 
+def can_fuse_rows(x: torch.Tensor) -> bool:
+    """x has 1..NS_MAX_TOKENS activation rows of a supported float type (the GEMV's batch limit)."""
+    return x.dim() >= 1 and 1 <= (x.shape[0] if x.dim() > 1 else 1) <= MAX_TOKENS and x.dtype in _TORCH_TO_NS
+
+
 def fused_gemv(
     raw: torch.Tensor,
     dtype,

@@ -40,8 +40,14 @@ class Installation:
         self.uninstall()
 
 
-def install(package: str = "neurostream") -> Installation:
-    """Patch an importable reference package; returns a handle that undoes it."""
+def install(package: str = "neurostream", streamed: bool = False) -> Installation:
+    """Patch an importable reference package; returns a handle that undoes it.
+
+    streamed=True also routes ``compute.blockffn.stream_linear`` calls on RAM-tier quantized tensors
+    (CUDA device, fused type, up to NS_MAX_TOKENS rows, no callback or shared prefetcher) to
+    ``nurostream_b200.stream.streamed_linear``, which overlaps each block's upload with the previous
+    block's GEMV; every other call keeps the reference's own ``stream_linear``.
+    """
     tk = importlib.import_module(f"{package}.compute.triton_kernels")
     quant = importlib.import_module(f"{package}.compute.quant")
     cache_mod = importlib.import_module(f"{package}.residency.cache")
@@ -74,4 +80,22 @@ def install(package: str = "neurostream") -> Installation:
     patch(gpt_oss.GptOssModel, "_route", lambda self, h, layer: moe.gptoss_route(self, h, layer))
     patch(gpt_oss.GptOssModel, "_ffn_block", lambda self, x, layer: moe.gptoss_ffn_block(self, x, layer))
     patch(router, "moe_ffn", moe.moe_ffn)
+    if streamed:
+        from . import stream
+        blockffn = importlib.import_module(f"{package}.compute.blockffn")
+        ref_stream_linear = blockffn.stream_linear
+
+        def stream_linear(provider, name, x, block_rows=1024, device="cpu", dtype=None, callback=None, out=None,
+                          row_start=0, row_end=None, lookahead=2, prefetcher=None):
+            import torch
+            dt = torch.float32 if dtype is None else dtype
+            if (callback is None and prefetcher is None and x.is_cuda and fused.can_fuse_rows(x)
+                    and torch.device(device).type == "cuda"):
+                y = stream.streamed_linear(provider, name, x, block_rows, device, dt, out, row_start, row_end)
+                if y is not None:
+                    return y
+            return ref_stream_linear(provider, name, x, block_rows, device, dt, callback, out, row_start, row_end,
+                                     lookahead, prefetcher)
+
+        patch(blockffn, "stream_linear", stream_linear)
     return Installation(patches)

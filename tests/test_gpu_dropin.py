@@ -139,3 +139,40 @@ def test_reference_stream_linear_and_linear_on_ns_gemv(reference, case):
         model = Qwen3Model(cache, cfg, device="cuda", dtype=torch.float32)
         y = model._linear("w", xt)
         assert_rel_close(y.cpu().numpy(), want, 1e-4, f"{case} Qwen3Model._linear")
+
+
+@pytest.mark.parametrize("case", ["mxfp4_t3_600x1024", "q4_k_37x4096", "q5_k_t3_300x512"])
+def test_streamed_path_for_ram_tier_tensors(reference, case):
+    """install(streamed=True): the reference's stream_linear on a RAM-tier (host-resident, quantized)
+    tensor goes through the copy-stream executor -- blocks uploaded while the previous block's GEMV
+    runs -- and gives the reference's golden result; the RAM-tier hit is counted as the reference does."""
+    import nurostream_b200
+    from neurostream.compute import blockffn
+    from neurostream.residency.cache import TieredCache
+    from nurostream_b200 import stream
+    from nurostream_b200.ggml import GGMLType
+    from tests.golden.make_golden import SynthSource, quant_producer
+
+    g = goldens.load("gemv")
+    meta = goldens.cases(g)[case]
+    t = GGMLType(meta["type"])
+    src = SynthSource({"w": ((meta["n_rows"], meta["K"]), t, quant_producer(t, meta["seed"], meta["w_stream"]))})
+    cache = TieredCache(src, device="cuda", compute_dtype=torch.float32, ram_budget=1 << 40)
+    assert cache.admit_ram("w")
+    _, x = goldens.gemv_inputs(meta)
+    xt = torch.from_numpy(x.copy()).cuda()
+    want = g[f"{case}__y"]
+    with nurostream_b200.install(streamed=True):
+        for br in (7, 64, 512):
+            hits = cache.stats.ram_hits
+            y = blockffn.stream_linear(cache, "w", xt, block_rows=br, device="cuda", dtype=torch.float32)
+            torch.cuda.synchronize()
+            assert cache.stats.ram_hits == hits + 1
+            assert_rel_close(y.cpu().numpy(), want, 1e-5, f"{case} streamed block_rows={br}")
+        # a row window, as stream_expert_ffn asks for one expert
+        n = meta["n_rows"]
+        lo, hi = n // 3, n - n // 4
+        y = blockffn.stream_linear(cache, "w", xt, block_rows=16, device="cuda", dtype=torch.float32,
+                                   row_start=lo, row_end=hi)
+        assert_rel_close(y.cpu().numpy(), want[:, lo:hi], 1e-5, f"{case} window")
+    assert torch.device("cuda", torch.cuda.current_device()).index in {k[1] for k in stream._EXECUTORS}

@@ -75,9 +75,10 @@ def test_fused_layer_gpt_oss_120b_shape():
     assert_rel_close(out, o_out, 2e-5, "gpt-oss-120b layer")
 
 
-@pytest.mark.parametrize("T", [1, 2])
+@pytest.mark.parametrize("T", [1, 2, 8])
 def test_fused_layer_qwen3_235b_shape(T):
-    """A layer of the Qwen3-235B-A22B shape: 128 experts, top-8, H=4096, F=1536, Q4_K."""
+    """A layer of the Qwen3-235B-A22B shape: 128 experts, top-8, H=4096, F=1536, Q4_K; T=8 is the
+    batch-8 decode step (up to 64 distinct experts in one launch)."""
     L = goldens.SynthLayer(_cfg(arch="qwen3moe", type=12, H=4096, F=1536, k=8, T=T, bias=False, norm=None))
     out, ids, w = run_layer(layer_from_synth(L), L.x, add_residual=False)
     o_out, o_ids, o_w = _oracle_layer(L)
@@ -149,3 +150,28 @@ def test_prefill_slices_match_oracle(kw):
     o_out, o_ids, _ = _oracle_layer(L)
     np.testing.assert_array_equal(ids.cpu().numpy().astype(np.int64), o_ids)
     assert_rel_close(out.cpu().numpy(), o_out, 2e-5, f"prefill {kw}")
+
+
+def test_decoder_batch8_qwen3_shape_matches_per_token_layers():
+    """MoeDecoder at batch 8 (one fused launch per layer over all 8 rows) equals running each row
+    alone through the same layers: tokens are independent through the MoE step."""
+    from nurostream_b200.decoder import MoeDecoder, MoeShape
+    from nurostream_b200.ggml import GGMLType
+    from nurostream_b200 import synth
+
+    shape = MoeShape(n_layer=3, hidden=4096, expert_ffn=1536, n_expert=128, top_k=8, ggml_type=int(GGMLType.Q4_K),
+                     arch="qwen3")
+    dec8 = MoeDecoder(shape, "cuda", use_graph=True, batch=8)
+    assert dec8.capture()
+    x = torch.empty((8, 4096), device="cuda")
+    synth.fill_float(x.view(-1), 91, 2)
+    y8 = dec8.step(x).clone()
+    ids8 = dec8.ids.clone()
+    dec1 = MoeDecoder(shape, "cuda", use_graph=False, batch=1)
+    for t in range(8):
+        y1 = dec1.step(x[t:t + 1])
+        torch.cuda.synchronize()
+        np.testing.assert_array_equal(dec1.ids.cpu().numpy(), ids8[:, t].cpu().numpy())
+        assert_rel_close(y8[t].cpu().numpy(), y1[0].cpu().numpy(), 1e-5, f"row {t}")
+    assert _lib.device_error() == 0
+    dec8.release()
