@@ -100,7 +100,10 @@ class MoeDecoder:
         cur = self.x
         for l, layer in enumerate(self.layers):
             nxt = self.bufs[l % len(self.bufs)]
-            layer(cur, out=nxt, add_residual=(self.rank == 0), ids=self.ids[l])
+            if self.batch == 1:
+                layer(cur, out=nxt, add_residual=(self.rank == 0), ids=self.ids[l])
+            else:  # as many rows per launch as the layer's kernel takes (halved if its activations overflow)
+                layer.prefill(cur, out=nxt, add_residual=(self.rank == 0), ids=self.ids[l])
             if self.world > 1:
                 torch.distributed.all_reduce(nxt, group=self.group)
             cur = nxt

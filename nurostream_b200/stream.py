@@ -130,6 +130,8 @@ _EXECUTORS: dict = {}
 
 def executor(device) -> StreamedGemv:
     dev = torch.device(device)
+    if dev.index is None:
+        dev = torch.device(dev.type, torch.cuda.current_device())
     key = (dev.type, dev.index)
     if key not in _EXECUTORS:
         _EXECUTORS[key] = StreamedGemv(dev)
