@@ -49,7 +49,7 @@ KERNEL = "moe_tc_kernel"
 def workload_config(shape, world, batch=1):
     if shape.arch == "qwen3":
         return {
-            "workload": (f"qwen3-235b-a22b-shape MoE decode path: {shape.n_layer} layers x (router softmax "
+            "workload": (f"qwen3-235b-a22b-shape MoE decode path: {shape.n_layer} layers x (RMSNorm + router softmax "
                          f"top-{shape.top_k}/{shape.n_expert} renormalised + Q4_K gate/up/down "
                          f"{shape.hidden}x{shape.expert_ffn} + silu*up + weighted combine + residual), batch {batch}"),
             "layers": shape.n_layer, "experts": shape.n_expert, "top_k": shape.top_k, "hidden": shape.hidden,
@@ -645,88 +645,139 @@ def run_gemv_sweep(args):
     return lines
 
 
-def run_prefill(args):
+def run_prefill(args, rank=0, world=1, local_rank=0, group=None):
     """Prefill of ``--prefill-tokens`` prompt tokens through the GPT-OSS-shaped MoE layers (config 5).
 
-    Each layer runs as slices of 2 tokens through the tensor-core layer kernel (``MoeLayer.prefill``), all
-    launches of a step captured in one CUDA graph.  Algorithmic bytes per layer: every expert that the
-    step's tokens route to, read once (at T = 512 that is all 128), plus the router and activations.
+    Each layer is one grouped expert GEMM on the tensor cores (``MoeLayer.prefill_grouped``: route,
+    bucket, planes, gate/up + activation, down, combine), every launch of a step captured in one CUDA
+    graph; at N > 1 every rank holds 1/N of the experts and the layer outputs are summed by one NCCL
+    all-reduce per layer.  Algorithmic bytes per layer: every expert that the step's tokens route to,
+    read once (at T = 512 that is all 128), plus the router and the activations in and out.
     """
     import torch
+    import torch.distributed as dist
 
     from nurostream_b200 import synth
     from nurostream_b200.decoder import MoeDecoder
 
-    dev = torch.device("cuda", 0)
+    dev = torch.device("cuda", local_rank)
     torch.cuda.set_device(dev)
     shape = bench_shape(args)
     T, H = args.prefill_tokens, shape.hidden
-    dec = MoeDecoder(shape, dev, 0, 1, None, use_graph=False, max_tokens=8)
+    dec = MoeDecoder(shape, dev, rank, world, group, use_graph=False, max_tokens=2)
     x = torch.empty((T, H), device=dev, dtype=torch.float32)
     synth.fill_float(x.view(-1), 778, 1)
     x_host = x.cpu().pin_memory()
     out_host = torch.empty((T, H), dtype=torch.float32, pin_memory=True)
     bufs = [torch.empty_like(x) for _ in range(2)]
-    dec.prefill(x, bufs)                         # warm-up outside capture (settles the slice size)
+
+    def barrier():
+        if world > 1:
+            dist.barrier(group=group)
+
+    dec.prefill(x, bufs)                         # warm-up outside capture (workspaces, communicator)
     torch.cuda.synchronize()
-    sl = dec.layers[0]._slice
-    n_launch = -(-T // sl)
-    g = torch.cuda.CUDAGraph()
-    with torch.cuda.graph(g):
-        y = dec.prefill(x, bufs)
+    g = None
+    if not args.no_graph:
+        g = torch.cuda.CUDAGraph()
+        try:
+            with torch.cuda.graph(g):
+                y = dec.prefill(x, bufs)
+        except Exception:
+            g = None
+            torch.cuda.synchronize()
+
+    graphed = g is not None
+
+    def step():
+        if g is not None:
+            g.replay()
+            return y
+        return dec.prefill(x, bufs)
+
     for _ in range(args.warmup):
-        g.replay()
+        step()
     torch.cuda.synchronize()
     dec.check_device_errors()
-    clocks = ClockSampler(0)
+    clocks = ClockSampler(local_rank)
     clocks.start()
+    barrier()
+    torch.cuda.synchronize()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record()
     for _ in range(args.steps):
-        g.replay()
+        yy = step()
     e1.record()
     torch.cuda.synchronize()
+    barrier()
     ms = e0.elapsed_time(e1) / args.steps
     # end to end: prompt in from pinned host memory, hidden states back, every step
     f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier()
+    torch.cuda.synchronize()
     f0.record()
     for _ in range(args.steps):
         x.copy_(x_host, non_blocking=True)
-        g.replay()
-        out_host.copy_(y, non_blocking=True)
+        yy = step()
+        out_host.copy_(yy, non_blocking=True)
     f1.record()
     torch.cuda.synchronize()
+    barrier()
     ms_e2e = f0.elapsed_time(f1) / args.steps
+    # one layer alone, outside the graph: the grouped GEMM's six launches (CUDA events on this stream)
+    layer = dec.layers[0]
+    l0, l1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    reps = 5
+    l0.record()
+    for _ in range(reps):
+        layer.prefill_grouped(x, out=bufs[0], add_residual=(rank == 0))
+    l1.record()
+    torch.cuda.synchronize()
+    layer_ms = l0.elapsed_time(l1) / reps
     clk = clocks.stop()
     dec.check_device_errors()
+    if world > 1:
+        t = torch.tensor([ms, ms_e2e, layer_ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX, group=group)
+        ms, ms_e2e, layer_ms = float(t[0]), float(t[1]), float(t[2])
+    g = None
+    dec.release()
+    if rank != 0:
+        return None
     peak, peak_kind = measured_peaks()
     E = shape.n_expert
+    n_local = dec.hi - dec.lo
     expert_bytes = shape.expert_bytes                      # one expert's gate + up + down rows
-    layer_bytes = E * expert_bytes + E * H * 2 + 2 * T * H * 4   # all experts (T = 512 touches all 128)
-    per_layer_s = ms / 1000.0 / shape.n_layer
-    achieved = layer_bytes / per_layer_s / 1e9
+    # the busiest rank's bytes: its experts (T = 512 touches all of them), the router, x in and out
+    layer_bytes = n_local * expert_bytes + E * H * 2 + 2 * T * H * 4
+    achieved = layer_bytes / (layer_ms / 1000.0) / 1e9
+    flops = 2.0 * T * shape.top_k * 3 * H * shape.expert_ffn * n_local / E
     line = {
         "metric": "prefill tok/s (GPT-OSS-120B shape, 512-token prompt, MoE layers)", "value": round(T * 1000.0 / ms, 1),
-        "unit": "tok/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 3),
+        "unit": "tok/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 3),
         "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
-        "dtype": "mxfp4 weights, fp32 accumulate", "data": "synthetic (seeded splitmix64 GGUF bytes generated in HBM)",
-        "config": {"workload": f"gpt-oss-120b-shape MoE prefill: {T} tokens x {shape.n_layer} layers, each layer as "
-                               f"{n_launch} fused launches of {sl} tokens", "tokens": T, "layers": shape.n_layer,
-                   "experts": E, "top_k": shape.top_k, "parallelism": "single",
-                   "l2": "inputs larger than L2 (every layer streams its experts from HBM)"},
+        "dtype": "mxfp4 weights x 24-bit activation digit planes (mxf4 tensor cores), fp32 accumulate",
+        "data": "synthetic (seeded splitmix64 GGUF bytes generated in HBM)",
+        "config": {"workload": f"gpt-oss-120b-shape MoE prefill: {T} tokens x {shape.n_layer} layers, each layer one "
+                               f"grouped expert GEMM (6 launches: route, bucket, planes, gate/up+SwiGLU, down, combine)"
+                               + (f" + NCCL all-reduce of the layer output over {world} ranks" if world > 1 else ""),
+                   "tokens": T, "layers": shape.n_layer, "experts": E, "top_k": shape.top_k,
+                   "parallelism": f"ep{world}" if world > 1 else "single",
+                   "l2": "inputs larger than L2 (every layer streams its experts, 1.7 GB, from HBM)"},
         "e2e": {"value": round(T * 1000.0 / ms_e2e, 1), "unit": "tok/s", "h2d_bytes_per_step": T * H * 4,
                 "d2h_bytes_per_step": T * H * 4},
-        "gpu_launches": shape.n_layer * n_launch * args.steps,
+        "gpu_launches": shape.n_layer * 6 * args.steps,
+        "cuda_graph": graphed,
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                      "frac": round(achieved / peak, 4), "traffic": None, "peak_kind": peak_kind,
-                     "kernel": "moe_tc_kernel" if sl <= 2 else "moe_layer_kernel",
-                     "algorithmic_bytes_per_layer": layer_bytes,
-                     "note": "each slice streams the experts its tokens route to, so an expert is read once per "
-                             "slice that uses it: HBM traffic is many times the algorithmic bytes"},
+                     "kernel": "pf_gemm_kernel<0>/<1> with route, bucket, planes and combine (one layer's six launches)",
+                     "algorithmic_bytes_per_layer": layer_bytes, "layer_ms": round(layer_ms, 4),
+                     "layer_ms_from": "CUDA events around 5 back-to-back calls of one layer, outside the graph",
+                     "mxf4_tflops": round(flops * 8 / (layer_ms / 1000.0) / 1e12, 1),
+                     "mxf4_tflops_note": "8 digit planes per activation: MMA work is 8x the algorithmic 2*T*k*3*H*F"},
     }
     if clk:
         line["clocks"] = clk
-    g = None
     return line
 
 
@@ -1009,9 +1060,6 @@ def main():
     if args.workload == "stream":
         print(json.dumps(run_stream(args)), flush=True)
         return
-    if args.workload == "prefill" and args.impl == "ours" and world == 1:
-        print(json.dumps(run_prefill(args)), flush=True)
-        return
     if args.impl == "reference":
         line = run_reference(args, rank, world)
     else:
@@ -1026,6 +1074,8 @@ def main():
             group = dist.group.WORLD
         if args.workload == "decode":
             line = run_full_decode(args, rank, world, local_rank, group)
+        elif args.workload == "prefill":
+            line = run_prefill(args, rank, world, local_rank, group)
         else:
             line = run_ours(args, rank, world, local_rank, group)
         if world > 1:

@@ -225,6 +225,24 @@ int ns_moe_decode_layer(const ns_moe_layer_t* p, void* workspace, size_t workspa
 int ns_moe_decode_layer_static(const ns_moe_layer_t* p, ns_stream_t stream);
 
 /*
+ * MoE prefill of T tokens (1..65536) as a grouped expert GEMM on the tcgen05
+ * tensor cores: RMSNorm -> router -> top-k -> tokens grouped by expert (<= 16
+ * per group) -> gate/up (+bias) -> activation -> down (+bias) -> weighted
+ * combine in ascending expert order (+ residual).  Same parameters, results
+ * (to fp32 rounding) and expert-parallel contract as ns_moe_decode_layer, for
+ * any T; every expert's weights stream from HBM once per group of its tokens.
+ * Replaces the prefill walk of neurostream/compute/blockffn.py:171-176, 220-229
+ * (per-expert dequantize + matmul over blocks) and neurostream/moe/router.py:
+ * 158-166.  MXFP4 experts only (NS_ERR_UNSUPPORTED otherwise); H and F
+ * multiples of 64 up to 8192; expert tensors, x and out 16-byte aligned.
+ * Workspace: ns_moe_prefill_workspace_bytes, 256-byte aligned, no
+ * initialisation needed.  Six stream-ordered launches, no host synchronisation.
+ */
+int ns_moe_prefill_workspace_bytes(const ns_moe_layer_t* p, size_t* bytes);
+int ns_moe_prefill_grouped(const ns_moe_layer_t* p, void* workspace, size_t workspace_bytes,
+                           ns_stream_t stream);
+
+/*
  * Dense projection with bf16 weights, fp32 activations and fp32 accumulation
  * (batch 1): for each segment s, y_s = residual_s + (W_s @ x' + bias_s), where
  * x' = rms_norm(x, norm_w) (x * rsqrt(mean(x^2) + eps) * norm_w) when norm_w is

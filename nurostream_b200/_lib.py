@@ -117,6 +117,8 @@ SIGNATURES = {
     "ns_moe_workspace_init": (_I, [_P, _SZ, _P]),
     "ns_moe_decode_layer": (_I, [C.POINTER(MoeLayerParams), _P, _SZ, _P]),
     "ns_moe_decode_layer_static": (_I, [C.POINTER(MoeLayerParams), _P]),
+    "ns_moe_prefill_workspace_bytes": (_I, [C.POINTER(MoeLayerParams), C.POINTER(_SZ)]),
+    "ns_moe_prefill_grouped": (_I, [C.POINTER(MoeLayerParams), _P, _SZ, _P]),
     "ns_synth_fill": (_I, [_P, _U64, _I, _U64, _U64, _U64, _F, _I, _I, _F, _P]),
     "ns_moe_set_trace": (_I, [_P, _SZ]),
     "ns_moe_select_kernel": (_I, [_I]),

@@ -31,7 +31,7 @@ namespace ns {
 
 constexpr int kMaxPairs = NS_MAX_TOKENS * NS_MAX_TOPK;  // (slot, token) pairs
 constexpr int kWsHeader = 1024;  // workspace: barrier counter at 0, activation maxima at 64
-constexpr int kMaxTiles = 256;
+constexpr int kMaxTiles = 320;  // T=8 x k=8 Q4_K (Qwen3-235B batch 8) needs ~280
 constexpr int kMoeSmemBudget = 225 * 1024;
 
 // ----------------------------------------------------------------------------- routing helpers
@@ -181,6 +181,8 @@ struct MoeArgs {
   int tr;                  // phase-2 rows per tile (<= 24)
   int rows_cta_max;        // phase-2 output rows per CTA, upper bound
   int sc_stride;           // floats of each warp's scale buffer
+  int act_global;          // CUDA-core path: phase 2 reads the activation rows from the workspace (L2)
+                           // instead of a shared-memory copy (pairs x F floats beyond shared memory)
   // shared-memory layout (byte offsets)
   int off_oacc, off_red, off_sc, off_stages, off_bars, off_shared, off_bias;
   unsigned long long* trace;  // per-CTA phase stamps, or nullptr
@@ -787,8 +789,9 @@ __global__ void __launch_bounds__(kMoeThreads, 1) moe_layer_kernel(MoeArgs a) {
       }
     } else {
       const int nf = np * F;
-      for (int i = tid * 4; i < nf; i += kComputeThreads * 4)
-        *reinterpret_cast<float4*>(region + i) = __ldcg(reinterpret_cast<const float4*>(a.act + i));
+      if (!a.act_global)
+        for (int i = tid * 4; i < nf; i += kComputeThreads * 4)
+          *reinterpret_cast<float4*>(region + i) = __ldcg(reinterpret_cast<const float4*>(a.act + i));
       for (int pr = tid; pr < np; pr += kComputeThreads) S.fac_pair[pr] = 1.0f;
     }
     named_sync(1, kComputeThreads);
@@ -865,7 +868,9 @@ __global__ void __launch_bounds__(kMoeThreads, 1) moe_layer_kernel(MoeArgs a) {
         } else {
 #pragma unroll
           for (int t = 0; t < NT; ++t) tok[t] = t;
-          x = region + (int64_t)pr0 * F;
+          // rows written by every CTA's phase-1 epilogue before the grid barrier; this SM has not
+          // read them before, so its loads miss L1 and see L2
+          x = (a.act_global ? a.act : region) + (int64_t)pr0 * F;
           xs = F;
         }
         unit_cuda_core<FMT, NT>(tl.phase, gi, kc, s0base, s1base, nvalid, rb, nb, x, xs, tok, nt, red, lane);
@@ -1028,14 +1033,16 @@ static int moe_validate(const ns_moe_layer_t* p, MoePlan* plan) {
 }
 
 // Shared-memory layout of one launch; returns total bytes, or 0 if it cannot fit.
-static size_t moe_layout(const ns_moe_layer_t* p, const MoePlan& plan, int grid, MoeArgs* a) {
+static size_t moe_layout(const ns_moe_layer_t* p, const MoePlan& plan, int grid, MoeArgs* a,
+                         bool act_global = false) {
   const bool mma = p->ggml_type == NS_GGML_MXFP4;
+  a->act_global = act_global && !mma;
   const int nb_h = p->H / 32, nb_f = p->F / 32;
   // region: phase 1 = h (+ h images), phase 2 = activation images (or fp32 activations)
   const size_t img_h = (size_t)2 * (nb_h * 4 + 4) * 16, img_f = (size_t)2 * (nb_f * 4 + 4) * 16;
   const size_t h_bytes = align_up((size_t)p->T * p->H * 4, 128);
   const size_t r1 = h_bytes + (mma ? p->T * img_h : 0);
-  const size_t r2 = mma ? plan.pairs_max * img_f : (size_t)plan.pairs_max * p->F * 4;
+  const size_t r2 = mma ? plan.pairs_max * img_f : a->act_global ? 0 : (size_t)plan.pairs_max * p->F * 4;
   const size_t region = align_up(std::max(r1, r2), 128);
   a->rows_cta_max = (p->H + grid - 1) / grid + 1;
   const size_t oacc = align_up((size_t)p->T * a->rows_cta_max * 4, 128);
@@ -1188,7 +1195,9 @@ static int moe_launch(const ns_moe_layer_t* p, const MoePlan& plan, uint8_t* ws,
   a.trace = g_trace_buf[trace_slot()];
 
   const int grid = nsm;
-  const size_t smem = moe_layout(p, plan, grid, &a);
+  size_t smem = moe_layout(p, plan, grid, &a);
+  if ((smem == 0 || smem > (size_t)kMoeSmemBudget) && p->ggml_type != NS_GGML_MXFP4)
+    smem = moe_layout(p, plan, grid, &a, true);  // activation rows stay in the workspace
   if (smem == 0 || smem > (size_t)kMoeSmemBudget)
     return fail(NS_ERR_UNSUPPORTED,
                 "ns_moe_decode_layer: T=%d x k=%d activation rows of F=%d do not fit in shared memory; "

@@ -7,5 +7,6 @@
 #include "attn.cu"
 #include "gemv.cu"
 #include "moe.cu"
+#include "prefill.cu"
 #include "attn_block.cu"
 #include "synth.cu"

@@ -26,8 +26,8 @@ from .shapes import MoeShape, expert_range  # noqa: F401  (re-exported)
 def synth_moe_layer(sh: MoeShape, l: int, dev, lo: int, hi: int, max_tokens: int = 1) -> MoeLayer:
     """MoE layer ``l`` of the synthetic model ``sh``, generated in HBM, holding experts [lo, hi).
 
-    GPT-OSS: norm weight 1 + 0.1 N(0,1), router (``sh.router_dtype``) N(0, 0.02) with an fp32 bias,
-    fp32 expert biases N(0, ``sh.bias_sigma``); Qwen3: router only.  The host twin of every tensor is
+    Norm weight 1 + 0.1 N(0,1) and router (``sh.router_dtype``) N(0, 0.02); GPT-OSS adds an fp32
+    router bias and fp32 expert biases N(0, ``sh.bias_sigma``).  The host twin of every tensor is
     ``nurostream_b200.synth`` with the same (seed, stream, offset).
     """
     s = synth.LayerStreams(l)
@@ -45,15 +45,17 @@ def synth_moe_layer(sh: MoeShape, l: int, dev, lo: int, hi: int, max_tokens: int
         synth.fill_float(buf, sh.seed, stream, start, sigma)
         return buf
 
+    norm = flt(H, s.norm_w, 0.1) + 1.0
     if sh.arch == "qwen3":
+        # the decoder layer's post-attention RMSNorm feeds moe_ffn (neurostream/model/qwen3.py); the
+        # MoE itself has no biases
         return MoeLayer(
-            H=H, F=F, n_expert=E, k=sh.top_k, ggml_type=t,
+            H=H, F=F, n_expert=E, k=sh.top_k, ggml_type=t, norm_w=norm, rms_eps=1e-6,
             router_w=flt(E * H, s.router_w, 0.02, sh.router_dtype).reshape(E, H),
             gate=quant(s.gate, F, H), up=quant(s.up, F, H), down=quant(s.down, H, F),
             expert_lo=lo, expert_hi=hi, max_tokens=max_tokens,
             route_mode=_lib.NS_ROUTE_SOFTMAX_TOPK_NORM, act_mode=_lib.NS_ACT_SILU_MUL,
         )
-    norm = flt(H, s.norm_w, 0.1) + 1.0
     return MoeLayer(
         H=H, F=F, n_expert=E, k=sh.top_k, ggml_type=t,
         router_w=flt(E * H, s.router_w, 0.02, sh.router_dtype).reshape(E, H),
@@ -149,15 +151,20 @@ class MoeDecoder:
 
     # ------------------------------------------------------------------ many tokens
 
-    def prefill(self, x: torch.Tensor, bufs: list[torch.Tensor] | None = None) -> torch.Tensor:
-        """T tokens (T, H) fp32 on device through every layer, each layer as slices of max_tokens
-        rows (``MoeLayer.prefill``); bufs: two (T, H) fp32 ping-pong buffers (allocated if None)."""
+    def prefill(self, x: torch.Tensor, bufs: list[torch.Tensor] | None = None, grouped: bool = True) -> torch.Tensor:
+        """T tokens (T, H) fp32 on device through every layer; bufs: two (T, H) fp32 ping-pong buffers
+        (allocated if None).  grouped: each layer as one grouped expert GEMM
+        (``MoeLayer.prefill_grouped``, MXFP4 experts); otherwise, or for other expert types, as slices
+        of max_tokens rows through the decode layer kernel (``MoeLayer.prefill``)."""
         if bufs is None:
             bufs = [torch.empty_like(x) for _ in range(2)]
         cur = x
         for l, layer in enumerate(self.layers):
             nxt = bufs[l % 2]
-            layer.prefill(cur, out=nxt, add_residual=(self.rank == 0))
+            if grouped and layer.t == GGMLType.MXFP4:
+                layer.prefill_grouped(cur, out=nxt, add_residual=(self.rank == 0))
+            else:
+                layer.prefill(cur, out=nxt, add_residual=(self.rank == 0))
             if self.world > 1:
                 torch.distributed.all_reduce(nxt, group=self.group)
             cur = nxt

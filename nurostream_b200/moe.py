@@ -93,6 +93,7 @@ class MoeLayer:
         self.alpha, self.limit, self.rms_eps = alpha, limit, rms_eps
         self.max_tokens = max_tokens
         self._slice = 0  # rows per launch that prefill settled on
+        self._pf_ws = None  # workspace of the grouped prefill (grown on demand)
         self.l2_prefetch: list = []  # tensors whose bytes the layer kernel asks L2 to fetch (a hint)
         p = self._params(max_tokens, None, None, True, None, None)
         n = C.c_size_t(0)
@@ -160,6 +161,29 @@ class MoeLayer:
             out = torch.empty_like(x)
         p = self._params(T, x, out, add_residual, ids, weights)
         _lib.call("ns_moe_decode_layer", C.byref(p), self._ws_ptr, self._ws_bytes, stream_of(x))
+        return out
+
+    def prefill_grouped(self, x: torch.Tensor, out: torch.Tensor | None = None, add_residual: bool = True,
+                        ids: torch.Tensor | None = None, weights: torch.Tensor | None = None) -> torch.Tensor:
+        """T tokens (any T) through ``ns_moe_prefill_grouped``: the routed experts as a grouped GEMM on
+        the tensor cores, each expert's rows streamed once per group of up to 16 of its tokens.
+
+        The prefill of ``blockffn.py:171-176, 220-229`` / ``router.py:158-166`` (per-expert dequantize
+        and matmul) with the same results as the per-token layer; MXFP4 experts only.  The workspace
+        is allocated on the first call for a larger T (outside any graph capture).
+        """
+        if x.dtype != torch.float32 or not x.is_contiguous() or x.dim() != 2:
+            raise TypeError("x must be a contiguous (T, H) float32 tensor")
+        T = x.shape[0]
+        if out is None:
+            out = torch.empty_like(x)
+        p = self._params(T, x, out, add_residual, ids, weights)
+        n = C.c_size_t(0)
+        _lib.call("ns_moe_prefill_workspace_bytes", C.byref(p), C.byref(n))
+        if self._pf_ws is None or self._pf_ws.numel() < n.value + 256:
+            self._pf_ws = torch.empty(n.value + 256, device=self.device, dtype=torch.uint8)
+        ptr = self._pf_ws.data_ptr() + (-self._pf_ws.data_ptr()) % 256
+        _lib.call("ns_moe_prefill_grouped", C.byref(p), ptr, n.value, stream_of(x))
         return out
 
     def prefill(self, x: torch.Tensor, out: torch.Tensor | None = None, add_residual: bool = True,

@@ -78,20 +78,22 @@ def test_fused_layer_gpt_oss_120b_shape():
 @pytest.mark.parametrize("T", [1, 2, 8])
 def test_fused_layer_qwen3_235b_shape(T):
     """A layer of the Qwen3-235B-A22B shape: 128 experts, top-8, H=4096, F=1536, Q4_K; T=8 is the
-    batch-8 decode step (up to 64 distinct experts in one launch)."""
+    batch-8 decode step (up to 64 distinct experts in one launch; its 64 activation rows of 1536
+    floats exceed shared memory, so phase 2 reads them from the workspace)."""
     L = goldens.SynthLayer(_cfg(arch="qwen3moe", type=12, H=4096, F=1536, k=8, T=T, bias=False, norm=None))
     layer = layer_from_synth(L)
-    if T <= 2:
-        out, ids, w = run_layer(layer, L.x, add_residual=False)
-    else:  # 8 x 8 pairs of 1536 activations exceed one launch's shared memory: slices of the largest size
-        xt = torch.from_numpy(L.x.copy()).cuda()
-        idt = torch.empty((T, L.k), dtype=torch.int32, device="cuda")
-        out = layer.prefill(xt, add_residual=False, ids=idt).cpu().numpy()
-        ids = idt.cpu().numpy().astype(np.int64)
-        assert _lib.device_error() == 0
+    out, ids, w = run_layer(layer, L.x, add_residual=False)
     o_out, o_ids, o_w = _oracle_layer(L)
     np.testing.assert_array_equal(ids, o_ids)
     assert_rel_close(out, o_out, 2e-5, f"qwen3 layer T={T}")
+    if T == 8:  # the slice walk of MoeLayer.prefill takes all 8 rows in one launch now
+        xt = torch.from_numpy(L.x.copy()).cuda()
+        idt = torch.empty((T, L.k), dtype=torch.int32, device="cuda")
+        out2 = layer.prefill(xt, add_residual=False, ids=idt).cpu().numpy()
+        assert layer._slice == 8
+        np.testing.assert_array_equal(idt.cpu().numpy().astype(np.int64), o_ids)
+        assert_rel_close(out2, o_out, 2e-5, "qwen3 layer T=8 via prefill")
+    assert _lib.device_error() == 0
 
 
 def test_fused_layer_bf16_router_and_q8_0_experts():
