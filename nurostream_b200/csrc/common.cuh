@@ -77,6 +77,37 @@ __device__ __forceinline__ float load_float(const void* p, int dtype, int64_t i)
   return __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(p)[i]);
 }
 
+// N values out[u] = p[idx(u)] (0 where idx(u) < 0) of a float tensor of type dtype, with the
+// type switch outside the loads so that all N loads are in flight together.  (load_float in an
+// unrolled loop converts each value right after its load, inside the type branch, which makes
+// every load wait for the one before it.)
+template <int N, typename IdxFn>
+__device__ __forceinline__ void load_floats(const void* p, int dtype, IdxFn idx, float (&out)[N]) {
+  if (dtype == NS_F32) {
+    const float* f = static_cast<const float*>(p);
+#pragma unroll
+    for (int u = 0; u < N; ++u) {
+      const int64_t i = idx(u);
+      out[u] = i >= 0 ? f[i] : 0.f;
+    }
+  } else {
+    const unsigned short* h = static_cast<const unsigned short*>(p);
+    uint32_t r[N];
+#pragma unroll
+    for (int u = 0; u < N; ++u) {
+      const int64_t i = idx(u);
+      r[u] = i >= 0 ? (uint32_t)h[i] : 0u;
+    }
+    if (dtype == NS_F16) {
+#pragma unroll
+      for (int u = 0; u < N; ++u) out[u] = __half2float(__ushort_as_half((unsigned short)r[u]));
+    } else {
+#pragma unroll
+      for (int u = 0; u < N; ++u) out[u] = __uint_as_float(r[u] << 16);  // bf16 -> fp32, exact
+    }
+  }
+}
+
 __device__ __forceinline__ void store_float(void* p, int dtype, int64_t i, float v) {
   if (dtype == NS_F32) reinterpret_cast<float*>(p)[i] = v;
   else if (dtype == NS_F16) reinterpret_cast<__half*>(p)[i] = __float2half_rn(v);
@@ -93,6 +124,14 @@ __device__ __forceinline__ float e8m0_half_scale(uint32_t e) {
 }
 
 // ----------------------------------------------------------------------------- smem byte access
+
+// 32-bit word at a 4-byte aligned shared-memory address (a shared-window address, so the load is
+// an ld.shared: a generic pointer rebuilt from an integer would be a generic load).
+__device__ __forceinline__ uint32_t lds32(uint32_t saddr) {
+  uint32_t v;
+  asm volatile("ld.shared.u32 %0, [%1];" : "=r"(v) : "r"(saddr));
+  return v;
+}
 
 // 32-bit little-endian word at an arbitrary byte address of shared memory.
 __device__ __forceinline__ uint32_t lds_u32_unaligned(const uint8_t* p) {

@@ -215,8 +215,7 @@ __global__ void __launch_bounds__((W + 1) * 32, 1) gemv_kernel(GemvArgs a) {
           v[4 * j] = f.x; v[4 * j + 1] = f.y; v[4 * j + 2] = f.z; v[4 * j + 3] = f.w;
         }
       } else {
-#pragma unroll
-        for (int j = 0; j < 32; ++j) v[j] = load_float(a.x, a.x_dtype, (int64_t)t * a.x_stride + 32 * g + j);
+        load_floats<32>(a.x, a.x_dtype, [&](int j) -> int64_t { return (int64_t)t * a.x_stride + 32 * g + j; }, v);
       }
       float m = 0.f, sum = 0.f;
 #pragma unroll
@@ -271,11 +270,10 @@ __global__ void __launch_bounds__((W + 1) * 32, 1) gemv_kernel(GemvArgs a) {
     constexpr int kB = 8;  // elements per thread whose loads are issued together
     for (int i0 = tid; i0 < NT * K; i0 += kB * kThreads) {
       float vb[kB];
-#pragma unroll
-      for (int b = 0; b < kB; ++b) {
+      load_floats<kB>(a.x, a.x_dtype, [&](int b) -> int64_t {
         const int i = i0 + b * kThreads, t = i / K, k = i - t * K;
-        vb[b] = i < NT * K && t < T ? load_float(a.x, a.x_dtype, (int64_t)t * a.x_stride + k) : 0.f;
-      }
+        return i < NT * K && t < T ? (int64_t)t * a.x_stride + k : -1;
+      }, vb);
 #pragma unroll
       for (int b = 0; b < kB; ++b) {
         const int i = i0 + b * kThreads, t = i / K, k = i - t * K;

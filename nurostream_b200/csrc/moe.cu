@@ -31,7 +31,7 @@ namespace ns {
 
 constexpr int kMaxPairs = NS_MAX_TOKENS * NS_MAX_TOPK;  // (slot, token) pairs
 constexpr int kWsHeader = 1024;  // workspace: barrier counter at 0, activation maxima at 64
-constexpr int kMaxTiles = 320;  // T=8 x k=8 Q4_K (Qwen3-235B batch 8) needs ~280
+constexpr int kMaxTiles = 300;  // Qwen3-235B batch 8 (T=8 x k=8 Q4_K, 2 stages of 8-neuron tiles) needs 277
 constexpr int kMoeSmemBudget = 225 * 1024;
 
 // ----------------------------------------------------------------------------- routing helpers
@@ -409,13 +409,27 @@ __global__ void __launch_bounds__(kMoeThreads, 1) moe_layer_kernel(MoeArgs a) {
   const bool own_expert = c < E;
   for (int t = 0; t < T; ++t) {
     float ss = 0.f, dot = 0.f;
-    for (int i = tid; i < H; i += kMoeThreads) {
-      const float xv = p.x[(int64_t)t * H + i];
-      const float wv = p.norm_w ? p.norm_w[i] : 1.0f;
-      const float rv = own_expert ? load_float(p.router_w, p.router_dtype, (int64_t)c * H + i) : 0.f;
-      h[t * H + i] = xv;
-      ss = fmaf(xv, xv, ss);
-      dot = fmaf(xv * wv, rv, dot);
+    for (int i0 = tid; i0 < H; i0 += 8 * kMoeThreads) {  // 8 elements' loads in flight, then summed in order
+      float xv[8], wv[8], rv[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        const int i = i0 + u * kMoeThreads;
+        xv[u] = i < H ? p.x[(int64_t)t * H + i] : 0.f;
+        wv[u] = i < H && p.norm_w ? p.norm_w[i] : 1.0f;
+      }
+      load_floats<8>(p.router_w, p.router_dtype, [&](int u) -> int64_t {
+        const int i = i0 + u * kMoeThreads;
+        return i < H && own_expert ? (int64_t)c * H + i : -1;
+      }, rv);
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        const int i = i0 + u * kMoeThreads;
+        if (i < H) {
+          h[t * H + i] = xv[u];
+          ss = fmaf(xv[u], xv[u], ss);
+          dot = fmaf(xv[u] * wv[u], rv[u], dot);
+        }
+      }
     }
     ss = warp_sum(ss);
     dot = warp_sum(dot);
@@ -973,6 +987,7 @@ static int dispatch_moe_t(const MoeArgs& a, int grid, size_t smem, cudaStream_t 
 
 // Trace buffer per device (host-side table, set by ns_moe_set_trace).
 static unsigned long long* g_trace_buf[64] = {nullptr};
+static size_t g_trace_bytes[64] = {0};
 static int trace_slot() {
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 0;
@@ -1062,6 +1077,18 @@ static size_t moe_layout(const ns_moe_layer_t* p, const MoePlan& plan, int grid,
     size_t hf = align_up((size_t)n1 * rb_h + 48, 16);
     return align_up(std::max(2 * hf, (size_t)n2 * rb_f + 48), 128);
   };
+  while (a->act_global && stages >= 2 && stage_of(tn, tr) * stages > avail) {
+    // many activation rows (T x k large): keep tiles wide, since the per-CTA tile list grows as
+    // they narrow; shrink the side that sets the stage size, and drop to 2 stages first
+    const bool p1_dominates = 2 * align_up((size_t)tn * rb_h + 48, 16) >= (size_t)tr * rb_f + 48;
+    if (stages > 3) --stages;
+    else if (p1_dominates && tn > 8) tn -= 4;
+    else if (!p1_dominates && tr > 16) tr -= 8;
+    else if (stages > 2) --stages;
+    else if (p1_dominates && tn > 1) tn = tn > 4 ? tn - 4 : tn - 1;
+    else if (!p1_dominates && tr > 1) tr = tr > 8 ? tr - 8 : tr - 1;
+    else --stages;
+  }
   while (stages >= 2 && stage_of(tn, tr) * stages > avail) {
     if (stages > 3) {
       --stages;
@@ -1133,6 +1160,7 @@ extern "C" int ns_moe_set_trace(uint64_t* buf, size_t bytes) {
       return fail(NS_ERR_SIZE, "ns_moe_set_trace: %zu bytes, need %d", bytes, nsm * NS_TRACE_EVENTS * 8);
   }
   g_trace_buf[trace_slot()] = reinterpret_cast<unsigned long long*>(buf);
+  g_trace_bytes[trace_slot()] = buf ? bytes : 0;
   return NS_OK;
 }
 

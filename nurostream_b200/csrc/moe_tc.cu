@@ -363,10 +363,12 @@ __global__ void __launch_bounds__(kTcThreads, 1) moe_tc_kernel(const __grid_cons
 #pragma unroll
   for (int u = 0; u < 8; ++u) {
     const int i = tid + u * kTcThreads;
-    const bool ok = i < H;
-    wv[u] = ok && p.norm_w ? p.norm_w[i] : 1.0f;
-    rv[u] = ok && own_expert ? load_float(p.router_w, p.router_dtype, (int64_t)c * H + i) : 0.f;
+    wv[u] = i < H && p.norm_w ? p.norm_w[i] : 1.0f;
   }
+  load_floats<8>(p.router_w, p.router_dtype, [&](int u) -> int64_t {
+    const int i = tid + u * kTcThreads;
+    return i < H && own_expert ? (int64_t)c * H + i : -1;
+  }, rv);
   griddep_wait();
   // counters of this launch (used only after the routing barrier)
   if (c == 0) {

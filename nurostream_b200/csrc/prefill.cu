@@ -5,7 +5,9 @@
 // rows and multiply the expert's tokens by it, one expert after another.  Here every expert's
 // weights stream from HBM once for all of its tokens (and once more per extra group of 16):
 //
-//   pf_route_kernel    RMSNorm, router logits, top-k, routing weights (T tokens)
+//   pf_norm_kernel     RMSNorm of the T tokens
+//   pf_logits_kernel   router logits (tiled product)
+//   pf_topk_kernel     top-k and routing weights
 //   pf_bucket_kernel   (token, expert) pairs sorted by (expert, token); groups of <= 16 pairs of one
 //                      expert; the work items of both GEMM phases
 //   pf_planes_kernel   digit planes of the normalised input, one copy per pair (pair order)
@@ -44,7 +46,7 @@ constexpr int kPfXchgBytes = kPfGroup * 128 * 4;
 // [256, 384); weight scales 2 x 16 [384, 416); activation scales 2 x 20 [416, 456).
 constexpr int kPfTmemUp = 128, kPfTmemA = 256, kPfTmemSfa = 384, kPfTmemSfb = 416, kPfTmemCols = 512;
 constexpr int kPfSmemBudget = 225 * 1024;
-constexpr int kPfRouteTok = 4;                             // tokens per routing CTA
+constexpr int kPfBucketSmem = 160 * 1024;                  // ids staged by the bucket kernel
 
 struct PfHeader {
   int npairs, ngroups, nitems1, nitems2;
@@ -86,70 +88,98 @@ __device__ __forceinline__ int pf_sf_byte(int slot, int pl, int blk) {
 
 // ----------------------------------------------------------------------------- routing
 
-// RMSNorm, router logits, top-k and weights of kPfRouteTok tokens per CTA (8 warps).  Follows
-// neurostream/model/gpt_oss.py:116-121 (top-k of logits, softmax over the k) and
-// neurostream/moe/router.py:59-69 (softmax, top-k, renormalise).
-__global__ void __launch_bounds__(256) pf_route_kernel(const ns_moe_layer_t p, PfWork w) {
-  extern __shared__ __align__(16) float pf_sm[];
-  const int H = p.H, E = p.n_expert, k = p.k;
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int t0 = blockIdx.x * kPfRouteTok, nt = min(kPfRouteTok, p.T - t0);
-  float* xs = pf_sm;                              // kPfRouteTok x H
-  float* lg = xs + kPfRouteTok * H;               // kPfRouteTok x E
-  float* scr = lg + kPfRouteTok * E;              // kPfRouteTok x E
-  __shared__ float red[8][kPfRouteTok];
-  __shared__ float rsc[kPfRouteTok];
-  __shared__ int sid[kPfRouteTok][NS_MAX_TOPK];
-  __shared__ float swt[kPfRouteTok][NS_MAX_TOPK];
-  for (int t = 0; t < nt; ++t) {
-    float ss = 0.f;
-    for (int i = tid; i < H; i += 256) {
-      const float v = p.x[(int64_t)(t0 + t) * H + i];
-      xs[t * H + i] = v;
-      ss = fmaf(v, v, ss);
-    }
-    ss = warp_sum(ss);
-    if (lane == 0) red[warp][t] = ss;
-  }
+// RMSNorm of one token per CTA: h = x * rsqrt(mean(x^2) + eps) * norm_w (neurostream/model/
+// gpt_oss.py:123-126 via the model's rms_norm), written to the workspace.
+__global__ void __launch_bounds__(256) pf_norm_kernel(const ns_moe_layer_t p, PfWork w) {
+  const int H = p.H, t = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  __shared__ float red[8];
+  const float* x = p.x + (int64_t)t * H;
+  float ss = 0.f;
+  for (int i = tid; i < H; i += 256) ss = fmaf(x[i], x[i], ss);
+  ss = warp_sum(ss);
+  if (lane == 0) red[warp] = ss;
   __syncthreads();
-  if (tid < nt) {
-    float ss = 0.f;
-    for (int i = 0; i < 8; ++i) ss += red[i][tid];
-    rsc[tid] = p.norm_w ? 1.0f / sqrtf(ss / (float)H + p.rms_eps) : 1.0f;
-  }
-  __syncthreads();
-  for (int t = 0; t < nt; ++t)
-    for (int i = tid; i < H; i += 256) {
-      float v = xs[t * H + i];
-      if (p.norm_w) v = __fmul_rn(__fmul_rn(v, rsc[t]), p.norm_w[i]);
-      xs[t * H + i] = v;
-      w.h[(int64_t)(t0 + t) * H + i] = v;
-    }
-  __syncthreads();
-  for (int e = warp; e < E; e += 8) {
-    float acc[kPfRouteTok] = {0.f, 0.f, 0.f, 0.f};
-    for (int i = lane; i < H; i += 32) {
-      const float wv = load_float(p.router_w, p.router_dtype, (int64_t)e * H + i);
+  float tot = 0.f;
+  for (int i = 0; i < 8; ++i) tot += red[i];
+  const float r = p.norm_w ? 1.0f / sqrtf(tot / (float)H + p.rms_eps) : 1.0f;
+  for (int i = tid; i < H; i += 256)
+    w.h[(int64_t)t * H + i] = p.norm_w ? __fmul_rn(__fmul_rn(x[i], r), p.norm_w[i]) : x[i];
+}
+
+// Router logits L[t][e] = h[t] . W[e] + b[e] as a tiled product: a CTA of 128 threads owns 16
+// tokens x 32 experts (2 x 2 per thread), K in steps of 64 through shared memory, the next step's
+// tiles loaded into registers while the current one is multiplied; each output is one fp32 fma
+// chain in ascending k.
+constexpr int kPfLgT = 16, kPfLgE = 32, kPfLgK = 64;
+__global__ void __launch_bounds__(128) pf_logits_kernel(const ns_moe_layer_t p, PfWork w, float* logits) {
+  __shared__ float hs[kPfLgT][kPfLgK + 1];
+  __shared__ float ws[kPfLgE][kPfLgK + 1];
+  const int H = p.H, E = p.n_expert, T = p.T;
+  const int t0 = blockIdx.x * kPfLgT, e0 = blockIdx.y * kPfLgE;
+  const int tid = threadIdx.x, tx = tid & 15, ty = tid >> 4;  // experts e0 + tx, +16; tokens t0 + ty, +8
+  constexpr int kH = kPfLgT * kPfLgK / 128, kW = kPfLgE * kPfLgK / 128;  // loads per thread: 8, 16
+  float hr[kH], wr[kW];
+  auto load = [&](int k0) {
 #pragma unroll
-      for (int t = 0; t < kPfRouteTok; ++t)
-        if (t < nt) acc[t] = fmaf(xs[t * H + i], wv, acc[t]);
+    for (int u = 0; u < kH; ++u) {
+      const int i = tid + 128 * u, r = i / kPfLgK, c = i - r * kPfLgK;
+      hr[u] = t0 + r < T ? w.h[(int64_t)(t0 + r) * H + k0 + c] : 0.f;
+    }
+    load_floats<kW>(p.router_w, p.router_dtype, [&](int u) -> int64_t {
+      const int i = tid + 128 * u, r = i / kPfLgK, c = i - r * kPfLgK;
+      return e0 + r < E ? (int64_t)(e0 + r) * H + k0 + c : -1;
+    }, wr);
+  };
+  float acc[2][2] = {{0.f, 0.f}, {0.f, 0.f}};
+  load(0);
+  for (int k0 = 0; k0 < H; k0 += kPfLgK) {  // H is a multiple of 64
+#pragma unroll
+    for (int u = 0; u < kH; ++u) {
+      const int i = tid + 128 * u;
+      hs[i / kPfLgK][i % kPfLgK] = hr[u];
     }
 #pragma unroll
-    for (int t = 0; t < kPfRouteTok; ++t) {
-      const float v = warp_sum(acc[t]);
-      if (lane == 0 && t < nt) lg[t * E + e] = v + (p.router_b ? p.router_b[e] : 0.f);
+    for (int u = 0; u < kW; ++u) {
+      const int i = tid + 128 * u;
+      ws[i / kPfLgK][i % kPfLgK] = wr[u];
     }
+    __syncthreads();
+    if (k0 + kPfLgK < H) load(k0 + kPfLgK);
+#pragma unroll 16
+    for (int kk = 0; kk < kPfLgK; ++kk) {
+      const float h0 = hs[ty][kk], h1 = hs[ty + 8][kk], w0 = ws[tx][kk], w1 = ws[tx + 16][kk];
+      acc[0][0] = fmaf(h0, w0, acc[0][0]);
+      acc[0][1] = fmaf(h0, w1, acc[0][1]);
+      acc[1][0] = fmaf(h1, w0, acc[1][0]);
+      acc[1][1] = fmaf(h1, w1, acc[1][1]);
+    }
+    __syncthreads();
   }
-  __syncthreads();
-  if (warp < nt) {
-    warp_route(lg + warp * E, E, k, p.route_mode, sid[warp], swt[warp], scr + warp * E, lane);
-    if (lane < k) {
-      const int64_t o = (int64_t)(t0 + warp) * k + lane;
-      w.ids[o] = sid[warp][lane];
-      w.wts[o] = swt[warp][lane];
-      if (p.ids) p.ids[o] = sid[warp][lane];
-      if (p.weights) p.weights[o] = swt[warp][lane];
+#pragma unroll
+  for (int a = 0; a < 2; ++a)
+#pragma unroll
+    for (int b = 0; b < 2; ++b) {
+      const int t = t0 + ty + 8 * a, e = e0 + tx + 16 * b;
+      if (t < T && e < E) logits[(int64_t)t * E + e] = acc[a][b] + (p.router_b ? p.router_b[e] : 0.f);
     }
+}
+
+// Top-k and routing weights, one warp per token: neurostream/model/gpt_oss.py:116-121 (top-k of the
+// logits, softmax over the k) or neurostream/moe/router.py:59-69 (softmax, top-k, renormalise).
+__global__ void __launch_bounds__(256) pf_topk_kernel(const ns_moe_layer_t p, PfWork w, const float* logits) {
+  __shared__ int sid[8][NS_MAX_TOPK];
+  __shared__ float swt[8][NS_MAX_TOPK];
+  __shared__ float scr[8][NS_MAX_EXPERTS];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, k = p.k, E = p.n_expert;
+  const int t = blockIdx.x * 8 + warp;
+  if (t >= p.T) return;
+  warp_route(logits + (int64_t)t * E, E, k, p.route_mode, sid[warp], swt[warp], scr[warp], lane);
+  if (lane < k) {
+    const int64_t o = (int64_t)t * k + lane;
+    w.ids[o] = sid[warp][lane];
+    w.wts[o] = swt[warp][lane];
+    if (p.ids) p.ids[o] = sid[warp][lane];
+    if (p.weights) p.weights[o] = swt[warp][lane];
   }
 }
 
@@ -157,10 +187,18 @@ __global__ void __launch_bounds__(256) pf_route_kernel(const ns_moe_layer_t p, P
 
 // One CTA of 1024 threads.  Pairs of local expert e are the tokens routed to it in ascending
 // order; experts ascend; e's pairs split into ceil(n/16) groups of near-equal size.
-__global__ void __launch_bounds__(1024) pf_bucket_kernel(const ns_moe_layer_t p, PfWork w, int ns1, int nr2) {
+__global__ void __launch_bounds__(1024) pf_bucket_kernel(const ns_moe_layer_t p, PfWork w, int ns1, int nr2,
+                                                        int ids_in_smem) {
+  extern __shared__ int pf_ids_s[];  // T x k ids when they fit (ids_in_smem), else unused
   __shared__ int cnt[NS_MAX_EXPERTS], poff[NS_MAX_EXPERTS], goff[NS_MAX_EXPERTS];
   const int T = p.T, k = p.k, lo = p.expert_lo, nl = p.expert_hi - p.expert_lo;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int* ids = w.ids;
+  if (ids_in_smem) {
+    for (int i = tid; i < T * k; i += 1024) pf_ids_s[i] = w.ids[i];
+    __syncthreads();
+    ids = pf_ids_s;
+  }
   for (int el = warp; el < nl; el += 32) {
     const int e = lo + el;
     int c = 0;
@@ -168,7 +206,7 @@ __global__ void __launch_bounds__(1024) pf_bucket_kernel(const ns_moe_layer_t p,
       const int t = t0 + lane;
       bool hit = false;
       if (t < T)
-        for (int j = 0; j < k; ++j) hit |= w.ids[(int64_t)t * k + j] == e;
+        for (int j = 0; j < k; ++j) hit |= ids[t * k + j] == e;
       c += __popc(__ballot_sync(0xffffffffu, hit));
     }
     if (lane == 0) cnt[el] = c;
@@ -197,7 +235,7 @@ __global__ void __launch_bounds__(1024) pf_bucket_kernel(const ns_moe_layer_t p,
       int jj = -1;
       if (t < T)
         for (int j = 0; j < k; ++j)
-          if (w.ids[(int64_t)t * k + j] == e) jj = j;
+          if (ids[t * k + j] == e) jj = j;
       const unsigned m = __ballot_sync(0xffffffffu, jj >= 0);
       if (jj >= 0) {
         const int pos = base + run + __popc(m & ((1u << lane) - 1u));
@@ -240,6 +278,22 @@ __global__ void __launch_bounds__(256) pf_planes_kernel(int H, PfWork w) {
 
 // ----------------------------------------------------------------------------- grouped GEMM
 
+// tc_wait that adds the time it spun to *acc (the tracer's per-role wait totals).
+__device__ __forceinline__ bool pf_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
+                                        unsigned long long* acc) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = globaltimer_ns();
+  const bool ok = tc_wait(bar, parity, abort_flag);
+  *acc += globaltimer_ns() - t0;
+  return ok;
+}
+
+// Tracer slots of the grouped GEMM (ns_moe_set_trace; per CTA, NS_TRACE_EVENTS values): start and
+// end stamps and, per role, nanoseconds spent waiting on each barrier.
+enum { kPfEvStart = 0, kPfEvEnd, kPfEvProdEmptyRaw, kPfEvProdEmptyB, kPfEvProdItem, kPfEvRepFullRaw,
+       kPfEvRepEmptyCan, kPfEvMmaFullCan, kPfEvMmaFullB, kPfEvMmaEmptyD, kPfEvEpiFullD, kPfEvEpiBusy,
+       kPfEvMmaEnd, kPfEvProdEnd, kPfEvRepEnd, kPfEvEpiEnd };
+
 struct PfGemmArgs {
   CUtensorMap tm_a16[2], tm_a8[2];  // phase 1: gate, up; phase 2: down (index 0)
   CUtensorMap tm_b;                 // planes of this phase: (pairs, blocks, 128 bytes) as u32
@@ -250,6 +304,7 @@ struct PfGemmArgs {
   int act_mode;
   float alpha, limit;
   int off_raw, off_b, off_xchg, off_bars, off_shared;
+  unsigned long long* trace;        // per-CTA tracer slots, or NULL
 };
 
 struct PfShared {
@@ -285,6 +340,9 @@ __global__ void __launch_bounds__(kTcThreads, 1) pf_gemm_kernel(const __grid_con
   PfShared& S = *reinterpret_cast<PfShared*>(smem + a.off_shared);
   volatile int* abort_flag = &S.abort_flag;
 
+  unsigned long long* tr = a.trace ? a.trace + (size_t)blockIdx.x * NS_TRACE_EVENTS : nullptr;
+  unsigned long long w0 = 0, w1 = 0, w2 = 0;  // this thread's wait totals (role-specific)
+  if (tid == 0 && tr) tr[kPfEvStart] = globaltimer_ns();
   if (tid == 0) {
     for (int s = 0; s < kPfRawStages; ++s) {
       mbar_init(&full_raw[s], 1);
@@ -318,19 +376,25 @@ __global__ void __launch_bounds__(kTcThreads, 1) pf_gemm_kernel(const __grid_con
     // ================================================================= producer (TMA)
     if (lane == 0) {
       const uint64_t policy = l2_evict_first_policy();
-      int n = 0;
+      int n = 0, nbq = 0;  // weight chunks and plane stages issued
       for (int i = c; i < nitems && !*abort_flag; i += G) {
+        const uint64_t ti = tr ? globaltimer_ns() : 0;
         const int2 it = items[i];
         const int4 g = W.grp[it.x];
         const int rows = min(128, a.rows_e - 128 * it.y);
         const int gv = rows >= 128 ? 16 : rows / 8;
         const int y0 = (g.x * a.rows_e + 128 * it.y) / 8;
-        for (int hf = 0; hf < NH && !*abort_flag; ++hf) {
-          const CUtensorMap* tm = gv == 16 ? &a.tm_a16[hf] : &a.tm_a8[hf];
-          for (int q = 0; q < nq; ++q, ++n) {
-            const int wb = kTcChunk * q;
-            const int st = n % kPfRawStages, bst = n % kPfBStages;
-            if (!tc_wait(&empty_raw[st], ((n / kPfRawStages) & 1) ^ 1, abort_flag)) break;
+        if (tr) w2 += globaltimer_ns() - ti;
+        // chunk order: (q, gate), (q, up), (q+1, gate), ..: the two halves of a K chunk share one
+        // B stage (the planes of the same 14 blocks of h)
+        for (int q = 0; q < nq && !*abort_flag; ++q) {
+          const int wb = kTcChunk * q;
+          for (int hf = 0; hf < NH; ++hf, ++n) {
+            const CUtensorMap* tm = gv == 16 ? &a.tm_a16[hf] : &a.tm_a8[hf];
+            const int st = n % kPfRawStages, bst = nbq % kPfBStages;
+            // both waits before any copy of this step is issued (an abort then leaves none unaccounted)
+            if (!pf_wait(&empty_raw[st], ((n / kPfRawStages) & 1) ^ 1, abort_flag, &w0)) break;
+            if (hf == 0 && !pf_wait(&empty_b[bst], ((nbq / kPfBStages) & 1) ^ 1, abort_flag, &w1)) break;
             mbar_arrive_expect_tx(&full_raw[st], (uint32_t)(8 * gv * kTcBoxW));
             uint8_t* dst = raw + st * kTcRawBytes;
 #pragma unroll 1
@@ -338,53 +402,67 @@ __global__ void __launch_bounds__(kTcThreads, 1) pf_gemm_kernel(const __grid_con
               const int x0 = ((j * rb + 17 * wb) & ~15) >> 1;  // u16 elements
               tma_load_2d_hint(dst + j * kTcBoxBytes, tm, x0, y0, &full_raw[st], policy);
             }
-            if (!tc_wait(&empty_b[bst], ((n / kPfBStages) & 1) ^ 1, abort_flag)) break;
-            mbar_arrive_expect_tx(&full_b[bst], (uint32_t)kPfBStageBytes);
-            uint8_t* bd = bbuf + bst * kPfBStageBytes;
-            tma_load_3d(bd, &a.tm_b, 0, wb, g.y, &full_b[bst]);
-            bulk_g2s(bd + kPfBBytes, sfimg + (size_t)it.x * sf_bytes + (size_t)(wb >> 2) * 512,
-                     (uint32_t)(kPfSfbAtoms * 512), &full_b[bst]);
+            if (hf == 0) {
+              mbar_arrive_expect_tx(&full_b[bst], (uint32_t)kPfBStageBytes);
+              uint8_t* bd = bbuf + bst * kPfBStageBytes;
+              tma_load_3d(bd, &a.tm_b, 0, wb, g.y, &full_b[bst]);
+              bulk_g2s(bd + kPfBBytes, sfimg + (size_t)it.x * sf_bytes + (size_t)(wb >> 2) * 512,
+                       (uint32_t)(kPfSfbAtoms * 512), &full_b[bst]);
+              ++nbq;
+            }
           }
         }
       }
       // let every issued load land before the CTA can exit
       for (int q = max(0, n - kPfRawStages); q < n; ++q)
         mbar_wait_bounded(&full_raw[q % kPfRawStages], (q / kPfRawStages) & 1);
-      for (int q = max(0, n - kPfBStages); q < n; ++q)
+      for (int q = max(0, nbq - kPfBStages); q < nbq; ++q)
         mbar_wait_bounded(&full_b[q % kPfBStages], (q / kPfBStages) & 1);
+      if (tr) {
+        tr[kPfEvProdEmptyRaw] = w0;
+        tr[kPfEvProdEmptyB] = w1;
+        tr[kPfEvProdItem] = w2;
+        tr[kPfEvProdEnd] = globaltimer_ns();
+      }
     }
   } else if (warp == kTcMmaWarp) {
     // ================================================================= MMA issuer
     if (lane == 0) {
-      int n = 0, nit = 0;
+      int n = 0, nit = 0, nbq = 0;
       bool ok = true;
       for (int i = c; i < nitems && ok; i += G, ++nit) {
         const int2 it = items[i];
         const int ntok = W.grp[it.x].z;
         const int N = 16 * ((ntok + 1) / 2);
-        if (!tc_wait(empty_d, (nit & 1) ^ 1, abort_flag)) break;
+        if (!pf_wait(empty_d, (nit & 1) ^ 1, abort_flag, &w2)) break;
         tc_fence_after();
-        for (int hf = 0; hf < NH && ok; ++hf) {
-          const uint32_t dcol = tbase + (hf ? kPfTmemUp : 0);
-          bool acc = false;
-          for (int q = 0; q < nq; ++q, ++n) {
-            const int wb = kTcChunk * q, nbc = min(kTcChunk, nb - wb);
-            const int cst = n % kTcCanStages, bst = n % kPfBStages;
-            if (!tc_wait(&full_can[cst], (n / kTcCanStages) & 1, abort_flag) ||
-                !tc_wait(&full_b[bst], (n / kPfBStages) & 1, abort_flag)) {
+        bool acc_h[2] = {false, false};  // gate / up accumulators written in this item
+        for (int q = 0; q < nq && ok; ++q) {
+          const int wb = kTcChunk * q, nbc = min(kTcChunk, nb - wb);
+          const int bst = nbq % kPfBStages;
+          if (!pf_wait(&full_b[bst], (nbq / kPfBStages) & 1, abort_flag, &w1)) {
+            ok = false;
+            break;
+          }
+          uint8_t* bd = bbuf + bst * kPfBStageBytes;
+          const uint32_t sfb_col = tbase + kPfTmemSfb + 20 * bst;
+          // B: core matrix (slot t, block b) at t*14*128 + b*128; +256 bytes (+16) per MMA
+          const uint64_t bd0 = umma_desc(smem_addr(bd), 128, kTcChunk * 128);
+          for (int hf = 0; hf < NH; ++hf, ++n) {
+            const int cst = n % kTcCanStages;
+            if (!pf_wait(&full_can[cst], (n / kTcCanStages) & 1, abort_flag, &w0)) {
               ok = false;
               break;
             }
             tc_fence_after();
-            uint8_t* bd = bbuf + bst * kPfBStageBytes;
-            const uint32_t sfb_col = tbase + kPfTmemSfb + 20 * bst;
+            if (hf == 0)  // the chunk's activation scales, once for both halves
 #pragma unroll
-            for (int at = 0; at < kPfSfbAtoms; ++at)
-              tc_cp_sf(sfb_col + 4 * at, umma_desc(smem_addr(bd + kPfBBytes + 512 * at), 128, 128));
+              for (int at = 0; at < kPfSfbAtoms; ++at)
+                tc_cp_sf(sfb_col + 4 * at, umma_desc(smem_addr(bd + kPfBBytes + 512 * at), 128, 128));
+            const uint32_t dcol = tbase + (hf ? kPfTmemUp : 0);
             const uint32_t sfa_col = tbase + kPfTmemSfa + 16 * cst;
             const uint32_t a_col = tbase + kPfTmemA + kTcTmemAStage * cst;
-            // B: core matrix (slot t, block b) at t*14*128 + b*128; +256 bytes (+16) per MMA
-            const uint64_t bd0 = umma_desc(smem_addr(bd), 128, kTcChunk * 128);
+            bool acc = acc_h[hf];
 #pragma unroll
             for (int s = 0; s < kTcChunk / 2; ++s) {
               if (s < nbc / 2) {
@@ -398,15 +476,24 @@ __global__ void __launch_bounds__(kTcThreads, 1) pf_gemm_kernel(const __grid_con
                 acc = true;
               }
             }
+            acc_h[hf] = acc;
             tc_commit(&empty_can[cst]);
-            tc_commit(&empty_b[bst]);
           }
+          if (!ok) break;
+          tc_commit(&empty_b[bst]);  // both halves' MMAs have read the stage
+          ++nbq;
         }
         if (!ok) break;
         tc_commit(full_d);
       }
       tc_commit(mma_done);
       mbar_wait_bounded(mma_done, 0);
+      if (tr) {
+        tr[kPfEvMmaFullCan] = w0;
+        tr[kPfEvMmaFullB] = w1;
+        tr[kPfEvMmaEmptyD] = w2;
+        tr[kPfEvMmaEnd] = globaltimer_ns();
+      }
     }
   } else if (tc_repack_index(warp) >= 0) {
     // ================================================================= repack warps
@@ -423,28 +510,29 @@ __global__ void __launch_bounds__(kTcThreads, 1) pf_gemm_kernel(const __grid_con
       const int rows = min(128, a.rows_e - 128 * it.y);
       const int gv = rows >= 128 ? 16 : rows / 8;
       const bool row_ok = Gr < gv;
-      for (int hf = 0; hf < NH; ++hf) {
-        for (int qc = 0; qc < nq && !*abort_flag; ++qc, ++n) {
+      for (int qc = 0; qc < nq && !*abort_flag; ++qc) {
+        for (int hf = 0; hf < NH; ++hf, ++n) {  // the producer's order: (q, gate), (q, up), ..
           const int wb = kTcChunk * qc, nbc = min(kTcChunk, nb - wb);
           const int st = n % kPfRawStages, cst = n % kTcCanStages;
-          if (!tc_wait(&full_raw[st], (n / kPfRawStages) & 1, abort_flag)) break;
-          const uint8_t* rs = raw + st * kTcRawBytes + j * kTcBoxBytes + Gr * kTcBoxW + ((j * rb + 17 * wb) & 15);
+          if (!pf_wait(&full_raw[st], (n / kPfRawStages) & 1, abort_flag, &w0)) break;
+          // this lane's row in the staged boxes, as a shared-window address (ld.shared below)
+          const uint32_t rs = smem_addr(raw) + st * kTcRawBytes + j * kTcBoxBytes + Gr * kTcBoxW +
+                              ((j * rb + 17 * wb) & 15);
           constexpr int kU = 6;
           uint32_t wv[kU][5];
 #pragma unroll
           for (int u = 0; u < kU; ++u) {
             const int b = wi == 0 ? (u < 4 ? u : u + 8) : 4 * wi + u;
             const bool ok = row_ok && (wi == 0 || u < 4) && b < nbc;
-            const uintptr_t src = reinterpret_cast<uintptr_t>(rs + 17 * b);
-            const uint32_t* wp = reinterpret_cast<const uint32_t*>(src & ~uintptr_t(3));
+            const uint32_t wa = (rs + 17 * b) & ~3u;
 #pragma unroll
-            for (int kk = 0; kk < 5; ++kk) wv[u][kk] = ok ? wp[kk] : 0u;
+            for (int kk = 0; kk < 5; ++kk) wv[u][kk] = ok ? lds32(wa + 4 * kk) : 0u;
           }
           uint32_t pay[4 * kU], sw[2] = {0u, 0u};
 #pragma unroll
           for (int u = 0; u < kU; ++u) {
             const int b = wi == 0 ? (u < 4 ? u : u + 8) : 4 * wi + u;
-            const uint32_t a0 = (uint32_t)(reinterpret_cast<uintptr_t>(rs + 17 * b) & 3);
+            const uint32_t a0 = (rs + 17 * b) & 3u;
             const uint32_t sh = 8 * ((a0 + 1) & 3);
             const bool whole = a0 == 3;
 #pragma unroll
@@ -454,7 +542,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) pf_gemm_kernel(const __grid_con
           }
           __syncwarp();
           if (lane == 0) mbar_arrive(&empty_raw[st]);
-          if (!tc_wait(&empty_can[cst], ((n / kTcCanStages) & 1) ^ 1, abort_flag)) break;
+          if (!pf_wait(&empty_can[cst], ((n / kTcCanStages) & 1) ^ 1, abort_flag, &w1)) break;
           tc_fence_after();
           const uint32_t acol = tbase + kPfTmemA + kTcTmemAStage * cst + taddr_lane;
           const uint32_t scol = tbase + kPfTmemSfa + 16 * cst + q + taddr_lane;
@@ -479,6 +567,11 @@ __global__ void __launch_bounds__(kTcThreads, 1) pf_gemm_kernel(const __grid_con
         }
       }
     }
+    if (tr && rw == 0 && lane == 0) {
+      tr[kPfEvRepFullRaw] = w0;
+      tr[kPfEvRepEmptyCan] = w1;
+      tr[kPfEvRepEnd] = globaltimer_ns();
+    }
   } else if (tc_epi_quadrant(warp) >= 0) {
     // ================================================================= epilogue warps
     const int q = tc_epi_quadrant(warp);
@@ -496,7 +589,8 @@ __global__ void __launch_bounds__(kTcThreads, 1) pf_gemm_kernel(const __grid_con
         if (a.bias0) b0 = a.bias0[(int64_t)g.x * a.rows_e + r];
         if (PH == 0 && a.bias1) b1 = a.bias1[(int64_t)g.x * a.rows_e + r];
       }
-      if (!tc_wait(full_d, nit & 1, abort_flag)) break;
+      if (!pf_wait(full_d, nit & 1, abort_flag, &w0)) break;
+      const uint64_t tb = tr ? globaltimer_ns() : 0;
       tc_fence_after();
       const uint32_t ta = tbase + ((uint32_t)(32 * q) << 16);
       float vg[kPfGroup], vu[kPfGroup];
@@ -524,6 +618,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) pf_gemm_kernel(const __grid_con
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(empty_d);
+      if (tr) w1 += globaltimer_ns() - tb;
       if (PH == 0) {
 #pragma unroll
         for (int t = 0; t < kPfGroup; ++t)
@@ -566,6 +661,11 @@ __global__ void __launch_bounds__(kTcThreads, 1) pf_gemm_kernel(const __grid_con
         named_sync(1, 128);
       }
     }
+    if (tr && q == 0 && lane == 0) {
+      tr[kPfEvEpiFullD] = w0;
+      tr[kPfEvEpiBusy] = w1;
+      tr[kPfEvEpiEnd] = globaltimer_ns();
+    }
   }
 
   tc_fence_before();
@@ -574,6 +674,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) pf_gemm_kernel(const __grid_con
     tc_fence_after();
     tmem_dealloc(tbase, kPfTmemCols);
   }
+  if (tid == 0 && tr) tr[kPfEvEnd] = globaltimer_ns();
 }
 
 // ----------------------------------------------------------------------------- combine
@@ -683,7 +784,7 @@ static int pf_validate(const ns_moe_layer_t* p, PfPlan* pl) {
   pl->off_sf1 = take((size_t)pl->Gmax * pl->sf1_bytes);
   pl->off_planes2 = take((size_t)P * pl->nb_f * 128);
   pl->off_sf2 = take((size_t)pl->Gmax * pl->sf2_bytes);
-  pl->off_ypair = take((size_t)P * p->H * 4);
+  pl->off_ypair = take(std::max((size_t)P * p->H, (size_t)p->T * p->n_expert) * 4);  // + logits scratch
   pl->total = off;
   return NS_OK;
 }
@@ -755,14 +856,20 @@ static int pf_run(const ns_moe_layer_t* p, const PfPlan& pl, uint8_t* ws, cudaSt
   w.sf1_bytes = pl.sf1_bytes;
   w.sf2_bytes = pl.sf2_bytes;
 
-  // 1. route
-  const size_t rsmem = (size_t)kPfRouteTok * (p->H + 2 * p->n_expert) * 4;
-  NS_CUDA_TRY(cudaFuncSetAttribute(pf_route_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                   (int)std::max(rsmem, (size_t)kPfRouteTok * (8192 + 2 * NS_MAX_EXPERTS) * 4)));
-  pf_route_kernel<<<(p->T + kPfRouteTok - 1) / kPfRouteTok, 256, rsmem, s>>>(*p, w);
+  // 1. route: RMSNorm, logits, top-k
+  pf_norm_kernel<<<p->T, 256, 0, s>>>(*p, w);
   NS_CUDA_TRY(cudaGetLastError());
-  // 2. bucket
-  pf_bucket_kernel<<<1, 1024, 0, s>>>(*p, w, pl.ns1, pl.nr2);
+  float* logits = reinterpret_cast<float*>(w.ypair);  // scratch until phase 2 writes ypair
+  pf_logits_kernel<<<dim3((p->T + kPfLgT - 1) / kPfLgT, (p->n_expert + kPfLgE - 1) / kPfLgE), 128, 0, s>>>(*p, w,
+                                                                                                       logits);
+  NS_CUDA_TRY(cudaGetLastError());
+  pf_topk_kernel<<<(p->T + 7) / 8, 256, 0, s>>>(*p, w, logits);
+  NS_CUDA_TRY(cudaGetLastError());
+  // 2. bucket (ids staged in shared memory when they fit)
+  const size_t ids_bytes = (size_t)p->T * p->k * 4;
+  const bool ids_smem = ids_bytes <= (size_t)kPfBucketSmem;
+  NS_CUDA_TRY(cudaFuncSetAttribute(pf_bucket_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kPfBucketSmem));
+  pf_bucket_kernel<<<1, 1024, ids_smem ? ids_bytes : 0, s>>>(*p, w, pl.ns1, pl.nr2, ids_smem ? 1 : 0);
   NS_CUDA_TRY(cudaGetLastError());
   // 3. phase-1 planes
   {
@@ -780,6 +887,9 @@ static int pf_run(const ns_moe_layer_t* p, const PfPlan& pl, uint8_t* ws, cudaSt
   a.act_mode = p->act_mode;
   a.alpha = p->alpha;
   a.limit = p->limit;
+  a.trace = g_trace_buf[trace_slot()];
+  unsigned long long* trace2 = a.trace;  // the down-projection launch: second half when the buffer has room
+  if (a.trace && g_trace_bytes[trace_slot()] >= (size_t)2 * nsm * NS_TRACE_EVENTS * 8) trace2 += (size_t)nsm * NS_TRACE_EVENTS;
   const size_t smem = pf_gemm_smem(&a);
   if (smem > (size_t)kPfSmemBudget)
     return fail(NS_ERR_UNSUPPORTED, "ns_moe_prefill_grouped: layout needs %zu bytes of shared memory", smem);
@@ -815,6 +925,7 @@ static int pf_run(const ns_moe_layer_t* p, const PfPlan& pl, uint8_t* ws, cudaSt
     a.rows_e = p->H;
     a.bias0 = p->down_b;
     a.bias1 = nullptr;
+    a.trace = trace2;
     st = pf_launch_gemm<1>(a, grid, smem, s);
     if (st) return st;
   }
