@@ -381,8 +381,8 @@ int ns_moe_select_kernel(int path);
  * writes, per CTA,
  * NS_TRACE_EVENTS globaltimer stamps (ns) to buf[cta * NS_TRACE_EVENTS + event].
  * ns_moe_prefill_grouped's two GEMM launches write per CTA their start and end
- * stamps and each role's nanoseconds spent waiting (producer, repack, MMA,
- * epilogue), the gate/up launch at buf and the down launch at
+ * stamps (ns) and each role's SM clock cycles spent waiting (producer,
+ * repack, MMA, epilogue), the gate/up launch at buf and the down launch at
  * buf + grid * NS_TRACE_EVENTS when buf holds twice the minimum (else at buf).
  * buf = NULL switches tracing off.  buf must hold grid * NS_TRACE_EVENTS uint64.
  */

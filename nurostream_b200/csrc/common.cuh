@@ -133,6 +133,13 @@ __device__ __forceinline__ uint32_t lds32(uint32_t saddr) {
   return v;
 }
 
+__device__ __forceinline__ void sts32(uint32_t saddr, uint32_t v) {
+  asm volatile("st.shared.u32 [%0], %1;" ::"r"(saddr), "r"(v) : "memory");
+}
+__device__ __forceinline__ void sts128(uint32_t saddr, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
+  asm volatile("st.shared.v4.u32 [%0], {%1, %2, %3, %4};" ::"r"(saddr), "r"(a), "r"(b), "r"(c), "r"(d) : "memory");
+}
+
 // 32-bit little-endian word at an arbitrary byte address of shared memory.
 __device__ __forceinline__ uint32_t lds_u32_unaligned(const uint8_t* p) {
   uintptr_t a = reinterpret_cast<uintptr_t>(p);

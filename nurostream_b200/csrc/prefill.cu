@@ -19,32 +19,45 @@
 // Arithmetic is the decode tensor-core kernel's (moe_tc.cu): weights are the A operand (128 rows of
 // one expert, MXFP4 blocks moved into TMEM as they are, E8M0 bytes as UE8M0 block scales);
 // activations are the B operand as 8 balanced radix-8 digit planes per token (an exact 24-bit
-// fixed-point split per 32-element block), so a group of 16 tokens is N = 128.  D accumulates in
-// fp32 in TMEM.
+// fixed-point split per 32-element block), so a group of 32 tokens is N = 256.  D accumulates in
+// fp32 in TMEM.  One kind::mxf4 MMA (M = 128, K = 64) takes the same time on B200 for any N up to
+// 256, so the kernel makes N as large as the expert's tokens allow: groups of up to 32 tokens.
 //
-// GEMM kernel.  Persistent, one CTA per SM; items (expert, 128-row tile, group) are dealt round
-// robin.  An expert's items are tile-major, so the groups of one tile (same weight bytes) run at
-// the same time on neighbouring CTAs and the second read of the tile is served by L2.  Per K chunk
-// of 14 blocks: the producer issues the weight boxes (8 TMA boxes of row phases, as in the decode
-// kernel), one 3-D TMA box of the group's planes (16 pairs x 14 blocks x 128 bytes, which is the
-// K-major operand layout as stored) and one bulk copy of the group's scale atoms; 12 repack warps
-// move the weight blocks into TMEM; one thread issues the MMAs; 4 epilogue warps drain D.
-// Every wait is bounded; a wait that runs out raises a device error bit, stops the CTA's pipeline,
-// lets in-flight copies and MMAs land, frees TMEM and returns.
+// GEMM kernel.  Persistent, one CTA per SM; items (expert, tile, group) are dealt round robin.  An
+// expert's items are tile-major, so the groups of one tile (same weight bytes) run at the same time
+// on neighbouring CTAs and a second read of the tile is served by L2.  A gate/up tile is 64
+// neurons: its 128 M-rows are the 64 gate rows and the 64 up rows of those neurons, so both
+// projections of a neuron land in one accumulator and the activation is formed in the epilogue; a
+// down tile is 128 rows.  Per K chunk of 10 blocks: the producer issues the weight boxes (TMA row
+// phases of 8-row groups), one 3-D TMA box of the group's planes (32 pairs x 10 blocks x 128
+// bytes, which is the K-major operand layout as stored) and one bulk copy of the group's scale
+// atoms; 12 repack warps move the weight blocks into TMEM; one thread issues the MMAs; 4 epilogue
+// warps drain D.  Every wait is bounded; a wait that runs out raises a device error bit, stops the
+// CTA's pipeline, lets in-flight copies and MMAs land, frees TMEM and returns.
 
 namespace ns {
 
 constexpr int kPfMaxTokens = 65536;
-constexpr int kPfGroup = 16;                               // pairs per group: N = 8 planes x 16
-constexpr int kPfRawStages = 4;                            // weight stages (kTcRawBytes each)
+constexpr int kPfGroup = 32;                               // pairs per group: N = 8 planes x 32
+constexpr int kPfChunk = 10;                               // K blocks (32 elements) per chunk
+constexpr int kPfBoxW = 208;                               // TMA box row (bytes): >= 10*17 + 15; rows of a
+                                                           // box land 52 words (20 banks) apart
+constexpr int kPfBoxBytes = kPfBoxW * 16;                  // one row phase of 16 row groups (128 rows)
+constexpr int kPfRawBytes = 8 * kPfBoxBytes;               // 8 row phases
+constexpr int kPfRawStages = 3;                            // weight stages (staged GGUF rows)
 constexpr int kPfBStages = 2;                              // activation-plane stages
-constexpr int kPfSfbAtoms = 5;                             // 4-block scale atoms a 14-block chunk spans
-constexpr int kPfBBytes = kPfGroup * kTcChunk * 128;       // planes of one chunk
-constexpr int kPfBStageBytes = kPfBBytes + kPfSfbAtoms * 512;
+constexpr int kPfSfbGroups = 3;                            // 4-block scale groups a 10-block chunk spans
+constexpr int kPfBBytes = kPfGroup * kPfChunk * 128;       // planes of one chunk
+constexpr int kPfBStageBytes = kPfBBytes + kPfSfbGroups * 1024;
+// Weight operand of one chunk in shared memory: core matrices of 8 M-rows x 16 bytes (one block's
+// payload), (M-row group g, block b) at g*1280 + b*128.
+constexpr int kPfAOpBytes = 128 * kPfChunk * 16;
+constexpr int kPfAStageBytes = kPfAOpBytes;
 constexpr int kPfXchgBytes = kPfGroup * 128 * 4;
-// TMEM columns: D gate [0, 128) and up [128, 256) (phase 2: [0, 128)); weights (A) 2 stages x 64
-// [256, 384); weight scales 2 x 16 [384, 416); activation scales 2 x 20 [416, 456).
-constexpr int kPfTmemUp = 128, kPfTmemA = 256, kPfTmemSfa = 384, kPfTmemSfb = 416, kPfTmemCols = 512;
+// TMEM columns: D [0, 256); weight scales 2 x 16 [256, 288) (3 atoms x 4 used); activation scales
+// 2 x 24 [288, 336) (3 groups x 8: for N = 256 the scale of B row n sits in lane n % 32, column
+// n / 32 of its group).
+constexpr int kPfTmemSfa = 256, kPfTmemSfb = 288, kPfTmemCols = 512;
 constexpr int kPfSmemBudget = 225 * 1024;
 constexpr int kPfBucketSmem = 160 * 1024;                  // ids staged by the bucket kernel
 
@@ -61,9 +74,9 @@ struct PfWork {
   int32_t* tok_pair;    // T x k: pair index of (token, rank), -1 if the expert is not local
   int32_t* pair_tok;    // P
   float* pair_w;        // P
-  int32_t* pair_gs;     // P: group << 4 | slot in group
+  int32_t* pair_gs;     // P: group << 5 | slot in group
   int4* grp;            // Gmax: local expert, first pair, pairs, 0
-  int2* items1;         // phase-1 items: group, 128-neuron tile
+  int2* items1;         // phase-1 items: group, 64-neuron tile
   int2* items2;         // phase-2 items: group, 128-row tile
   uint8_t* planes1;     // P x nb_h x 128
   uint8_t* sf1;         // Gmax x sf1_bytes
@@ -80,10 +93,12 @@ __device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* tmap, 
       : "memory");
 }
 
-// Byte of scale atom `atom` holding plane `pl` of slot `slot`, block `blk` (blk % 4 within the
-// atom): row m = 8*slot + pl of the B operand at 16*(m%32) + 4*(m/32) + blk%4.
-__device__ __forceinline__ int pf_sf_byte(int slot, int pl, int blk) {
-  return 16 * (8 * (slot & 3) + pl) + 4 * (slot >> 2) + (blk & 3);
+// Byte of a group's scale image holding plane `pl` of slot `slot`, block `blk`: the image is one
+// 1024-byte entry per 4 blocks, two 512-byte atoms (B rows 0..127, 128..255) as tcgen05.cp copies
+// them; row m = 8*slot + pl of the B operand sits at 16*(m%32) + 4*((m/32)%4) + blk%4 of atom m/128.
+__device__ __forceinline__ int pf_sf_off(int slot, int pl, int blk) {
+  const int m = 8 * slot + pl;
+  return (blk >> 2) * 1024 + (m >> 7) * 512 + 16 * (m & 31) + 4 * ((m >> 5) & 3) + (blk & 3);
 }
 
 // ----------------------------------------------------------------------------- routing
@@ -250,7 +265,7 @@ __global__ void __launch_bounds__(1024) pf_bucket_kernel(const ns_moe_layer_t p,
       const int bs = c / ng, rem = c - bs * ng;
       const int start = gi * bs + min(gi, rem), n = bs + (gi < rem ? 1 : 0);
       w.grp[g0 + gi] = make_int4(el, base + start, n, 0);
-      for (int s = 0; s < n; ++s) w.pair_gs[base + start + s] = ((g0 + gi) << 4) | s;
+      for (int s = 0; s < n; ++s) w.pair_gs[base + start + s] = ((g0 + gi) << 5) | s;
     }
     for (int i = lane; i < ns1 * ng; i += 32) w.items1[ns1 * g0 + i] = make_int2(g0 + i % ng, i / ng);
     for (int i = lane; i < nr2 * ng; i += 32) w.items2[nr2 * g0 + i] = make_int2(g0 + i % ng, i / ng);
@@ -269,41 +284,59 @@ __global__ void __launch_bounds__(256) pf_planes_kernel(int H, PfWork w) {
   const int units = w.hdr->npairs * nb;
   for (int u = hw0; u < units; u += nhw) {  // uniform per half-warp
     const int pr = u / nb, b = u - pr * nb;
-    const int t = w.pair_tok[pr], gs = w.pair_gs[pr], g = gs >> 4, s = gs & 15;
+    const int t = w.pair_tok[pr], gs = w.pair_gs[pr], g = gs >> 5, s = gs & 31;
     const float* hb = w.h + (int64_t)t * H + 32 * b + hl;
     halfwarp_block_planes(hb[0], hb[16], w.planes1 + ((size_t)pr * nb + b) * 128,
-                          w.sf1 + (size_t)g * w.sf1_bytes + (b >> 2) * 512 + pf_sf_byte(s, 0, b), 16, hl, mask);
+                          w.sf1 + (size_t)g * w.sf1_bytes + pf_sf_off(s, 0, b), 16, hl, mask);
   }
 }
 
 // ----------------------------------------------------------------------------- grouped GEMM
 
-// tc_wait that adds the time it spun to *acc (the tracer's per-role wait totals).
+// Bounded wait (as tc_wait) that adds the time it spun to *acc (the tracer's per-role wait totals).
+// Roles that wait for long stretches (producer, epilogue) sleep `nap` ns between polls, leaving the
+// issue slots to the repack warps on the same sub-partitions.
+template <int Nap = 0>
 __device__ __forceinline__ bool pf_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
                                         unsigned long long* acc) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = globaltimer_ns();
-  const bool ok = tc_wait(bar, parity, abort_flag);
-  *acc += globaltimer_ns() - t0;
+  const long long c0 = clock64();
+  bool ok = true;
+  while (!mbar_try_wait(bar, parity)) {
+    if (*abort_flag) {
+      ok = false;
+      break;
+    }
+    if (Nap) __nanosleep(Nap);
+    if (globaltimer_ns() - t0 > kWaitLimitNs) {
+      raise_device_error(NS_DEVERR_COPY_WAIT);
+      *abort_flag = 1;
+      ok = false;
+      break;
+    }
+  }
+  *acc += (unsigned long long)(clock64() - c0);
   return ok;
 }
 
 // Tracer slots of the grouped GEMM (ns_moe_set_trace; per CTA, NS_TRACE_EVENTS values): start and
-// end stamps and, per role, nanoseconds spent waiting on each barrier.
+// end stamps (ns) and, per role, SM clock cycles spent waiting on each barrier.
 enum { kPfEvStart = 0, kPfEvEnd, kPfEvProdEmptyRaw, kPfEvProdEmptyB, kPfEvProdItem, kPfEvRepFullRaw,
        kPfEvRepEmptyCan, kPfEvMmaFullCan, kPfEvMmaFullB, kPfEvMmaEmptyD, kPfEvEpiFullD, kPfEvEpiBusy,
        kPfEvMmaEnd, kPfEvProdEnd, kPfEvRepEnd, kPfEvEpiEnd };
 
 struct PfGemmArgs {
-  CUtensorMap tm_a16[2], tm_a8[2];  // phase 1: gate, up; phase 2: down (index 0)
+  CUtensorMap tm_a[2];              // phase 0: gate rows, up rows (8-group boxes); phase 1: down rows
+                                    // with 16-group boxes, and with 8-group boxes for a half tile
   CUtensorMap tm_b;                 // planes of this phase: (pairs, blocks, 128 bytes) as u32
   PfWork w;
-  const float* bias0;               // phase 1 gate_b, phase 2 down_b (local experts x rows), or NULL
-  const float* bias1;               // phase 1 up_b, or NULL
-  int H, F, nb, rb, rows_e;         // rows_e: weight rows per expert (F or H)
+  const float* bias0;               // phase 0 gate_b, phase 1 down_b (local experts x rows), or NULL
+  const float* bias1;               // phase 0 up_b, or NULL
+  int H, F, nb, rb, rows_e;         // rows_e: neurons (phase 0) or down rows (phase 1) per expert
   int act_mode;
   float alpha, limit;
-  int off_raw, off_b, off_xchg, off_bars, off_shared;
+  int off_raw, off_aop, off_b, off_xchg, off_bars, off_shared;
   unsigned long long* trace;        // per-CTA tracer slots, or NULL
 };
 
@@ -312,19 +345,27 @@ struct PfShared {
   int abort_flag;
 };
 
+// Rows of an item's tile: phase 0 a 64-neuron tile is 64 gate + 64 up rows (16 row groups); phase 1
+// a tile is 128 down rows, or 64 for the last tile when H is an odd multiple of 64.
+template <int PH>
+__device__ __forceinline__ int pf_groups(int rows_e, int tile) {
+  return PH == 0 ? 16 : (rows_e - 128 * tile >= 128 ? 16 : 8);
+}
+
 template <int PH>
 __global__ void __launch_bounds__(kTcThreads, 1) pf_gemm_kernel(const __grid_constant__ PfGemmArgs a) {
   extern __shared__ __align__(1024) uint8_t smem[];
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int G = gridDim.x, c = blockIdx.x;
-  constexpr int NH = PH == 0 ? 2 : 1;  // K halves of an item: gate then up, or down
   const PfWork& W = a.w;
   const int2* items = PH == 0 ? W.items1 : W.items2;
   const uint8_t* sfimg = PH == 0 ? W.sf1 : W.sf2;
   const int sf_bytes = PH == 0 ? W.sf1_bytes : W.sf2_bytes;
-  const int nb = a.nb, rb = a.rb, nq = (nb + kTcChunk - 1) / kTcChunk;
+  const int nb = a.nb, rb = a.rb, nq = (nb + kPfChunk - 1) / kPfChunk;
+  constexpr int kTileStep = PH == 0 ? 64 : 128;  // expert rows (neurons or down rows) per tile
 
   uint8_t* raw = smem + a.off_raw;
+  uint8_t* aop = smem + a.off_aop;
   uint8_t* bbuf = smem + a.off_b;
   float* xchg = reinterpret_cast<float*>(smem + a.off_xchg);
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + a.off_bars);
@@ -362,7 +403,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) pf_gemm_kernel(const __grid_con
     fence_mbar_init();
     S.abort_flag = (smem_addr(smem) & 1023u) != 0;
     if (S.abort_flag) raise_device_error(NS_DEVERR_COPY_WAIT);
-    prefetch_tmap(&a.tm_a16[0]);
+    prefetch_tmap(&a.tm_a[0]);
     prefetch_tmap(&a.tm_b);
   }
   if (warp == kTcMmaWarp) tmem_alloc(&S.tmem_base, kPfTmemCols);
@@ -373,42 +414,34 @@ __global__ void __launch_bounds__(kTcThreads, 1) pf_gemm_kernel(const __grid_con
   const int nitems = PH == 0 ? W.hdr->nitems1 : W.hdr->nitems2;
 
   if (warp == kTcProducerWarp) {
-    // ================================================================= producer (TMA)
+    // ================================================================= producers (TMA)
+    // Lane 0 streams the weights, lane 1 the activation planes, each as far ahead as its own ring
+    // allows: the weight prefetch depth does not wait for plane stages.
     if (lane == 0) {
       const uint64_t policy = l2_evict_first_policy();
-      int n = 0, nbq = 0;  // weight chunks and plane stages issued
+      int n = 0;  // weight chunks issued
       for (int i = c; i < nitems && !*abort_flag; i += G) {
-        const uint64_t ti = tr ? globaltimer_ns() : 0;
+        const long long ti = tr ? clock64() : 0;
         const int2 it = items[i];
         const int4 g = W.grp[it.x];
-        const int rows = min(128, a.rows_e - 128 * it.y);
-        const int gv = rows >= 128 ? 16 : rows / 8;
-        const int y0 = (g.x * a.rows_e + 128 * it.y) / 8;
-        if (tr) w2 += globaltimer_ns() - ti;
-        // chunk order: (q, gate), (q, up), (q+1, gate), ..: the two halves of a K chunk share one
-        // B stage (the planes of the same 14 blocks of h)
-        for (int q = 0; q < nq && !*abort_flag; ++q) {
-          const int wb = kTcChunk * q;
-          for (int hf = 0; hf < NH; ++hf, ++n) {
-            const CUtensorMap* tm = gv == 16 ? &a.tm_a16[hf] : &a.tm_a8[hf];
-            const int st = n % kPfRawStages, bst = nbq % kPfBStages;
-            // both waits before any copy of this step is issued (an abort then leaves none unaccounted)
-            if (!pf_wait(&empty_raw[st], ((n / kPfRawStages) & 1) ^ 1, abort_flag, &w0)) break;
-            if (hf == 0 && !pf_wait(&empty_b[bst], ((nbq / kPfBStages) & 1) ^ 1, abort_flag, &w1)) break;
-            mbar_arrive_expect_tx(&full_raw[st], (uint32_t)(8 * gv * kTcBoxW));
-            uint8_t* dst = raw + st * kTcRawBytes;
+        const int gv = pf_groups<PH>(a.rows_e, it.y);
+        const int y0 = (g.x * a.rows_e + kTileStep * it.y) / 8;
+        if (tr) w2 += (unsigned long long)(clock64() - ti);
+        for (int q = 0; q < nq; ++q, ++n) {
+          const int wb = kPfChunk * q;
+          const int st = n % kPfRawStages;
+          if (!pf_wait<64>(&empty_raw[st], ((n / kPfRawStages) & 1) ^ 1, abort_flag, &w0)) break;
+          mbar_arrive_expect_tx(&full_raw[st], (uint32_t)(8 * gv * kPfBoxW));
+          uint8_t* dst = raw + st * kPfRawBytes;
 #pragma unroll 1
-            for (int j = 0; j < 8; ++j) {
-              const int x0 = ((j * rb + 17 * wb) & ~15) >> 1;  // u16 elements
-              tma_load_2d_hint(dst + j * kTcBoxBytes, tm, x0, y0, &full_raw[st], policy);
-            }
-            if (hf == 0) {
-              mbar_arrive_expect_tx(&full_b[bst], (uint32_t)kPfBStageBytes);
-              uint8_t* bd = bbuf + bst * kPfBStageBytes;
-              tma_load_3d(bd, &a.tm_b, 0, wb, g.y, &full_b[bst]);
-              bulk_g2s(bd + kPfBBytes, sfimg + (size_t)it.x * sf_bytes + (size_t)(wb >> 2) * 512,
-                       (uint32_t)(kPfSfbAtoms * 512), &full_b[bst]);
-              ++nbq;
+          for (int j = 0; j < 8; ++j) {
+            const int x0 = ((j * rb + 17 * wb) & ~15) >> 1;  // u16 elements
+            if (PH == 0) {  // gate rows to row groups 0..7, up rows to 8..15 of the row phase
+              tma_load_2d_hint(dst + j * kPfBoxBytes, &a.tm_a[0], x0, y0, &full_raw[st], policy);
+              tma_load_2d_hint(dst + j * kPfBoxBytes + 8 * kPfBoxW, &a.tm_a[1], x0, y0, &full_raw[st], policy);
+            } else {
+              tma_load_2d_hint(dst + j * kPfBoxBytes, gv == 16 ? &a.tm_a[0] : &a.tm_a[1], x0, y0, &full_raw[st],
+                               policy);
             }
           }
         }
@@ -416,72 +449,82 @@ __global__ void __launch_bounds__(kTcThreads, 1) pf_gemm_kernel(const __grid_con
       // let every issued load land before the CTA can exit
       for (int q = max(0, n - kPfRawStages); q < n; ++q)
         mbar_wait_bounded(&full_raw[q % kPfRawStages], (q / kPfRawStages) & 1);
-      for (int q = max(0, nbq - kPfBStages); q < nbq; ++q)
-        mbar_wait_bounded(&full_b[q % kPfBStages], (q / kPfBStages) & 1);
       if (tr) {
         tr[kPfEvProdEmptyRaw] = w0;
-        tr[kPfEvProdEmptyB] = w1;
         tr[kPfEvProdItem] = w2;
         tr[kPfEvProdEnd] = globaltimer_ns();
       }
+    } else if (lane == 1) {
+      int n = 0;  // plane chunks issued
+      for (int i = c; i < nitems && !*abort_flag; i += G) {
+        const int2 it = items[i];
+        const int p0 = W.grp[it.x].y;
+        for (int q = 0; q < nq; ++q, ++n) {
+          const int wb = kPfChunk * q;
+          const int bst = n % kPfBStages;
+          if (!pf_wait<64>(&empty_b[bst], ((n / kPfBStages) & 1) ^ 1, abort_flag, &w1)) break;
+          mbar_arrive_expect_tx(&full_b[bst], (uint32_t)kPfBStageBytes);
+          uint8_t* bd = bbuf + bst * kPfBStageBytes;
+          tma_load_3d(bd, &a.tm_b, 0, wb, p0, &full_b[bst]);  // 32 pairs (one box beats 8-pair boxes)
+          bulk_g2s(bd + kPfBBytes, sfimg + (size_t)it.x * sf_bytes + (size_t)(wb >> 2) * 1024,
+                   (uint32_t)(kPfSfbGroups * 1024), &full_b[bst]);
+        }
+      }
+      for (int q = max(0, n - kPfBStages); q < n; ++q)
+        mbar_wait_bounded(&full_b[q % kPfBStages], (q / kPfBStages) & 1);
+      if (tr) tr[kPfEvProdEmptyB] = w1;
     }
   } else if (warp == kTcMmaWarp) {
     // ================================================================= MMA issuer
     if (lane == 0) {
-      int n = 0, nit = 0, nbq = 0;
+      int n = 0, nit = 0;
       bool ok = true;
       for (int i = c; i < nitems && ok; i += G, ++nit) {
         const int2 it = items[i];
         const int ntok = W.grp[it.x].z;
         const int N = 16 * ((ntok + 1) / 2);
-        if (!pf_wait(empty_d, (nit & 1) ^ 1, abort_flag, &w2)) break;
+        if (!pf_wait<32>(empty_d, (nit & 1) ^ 1, abort_flag, &w2)) break;
         tc_fence_after();
-        bool acc_h[2] = {false, false};  // gate / up accumulators written in this item
-        for (int q = 0; q < nq && ok; ++q) {
-          const int wb = kTcChunk * q, nbc = min(kTcChunk, nb - wb);
-          const int bst = nbq % kPfBStages;
-          if (!pf_wait(&full_b[bst], (nbq / kPfBStages) & 1, abort_flag, &w1)) {
+        bool acc = false;
+        for (int q = 0; q < nq; ++q, ++n) {
+          const int wb = kPfChunk * q, nbc = min(kPfChunk, nb - wb);
+          const int cst = n % kTcCanStages, bst = n % kPfBStages;
+          if (!pf_wait<32>(&full_can[cst], (n / kTcCanStages) & 1, abort_flag, &w0) ||
+              !pf_wait<32>(&full_b[bst], (n / kPfBStages) & 1, abort_flag, &w1)) {
             ok = false;
             break;
           }
+          tc_fence_after();
           uint8_t* bd = bbuf + bst * kPfBStageBytes;
-          const uint32_t sfb_col = tbase + kPfTmemSfb + 20 * bst;
-          // B: core matrix (slot t, block b) at t*14*128 + b*128; +256 bytes (+16) per MMA
-          const uint64_t bd0 = umma_desc(smem_addr(bd), 128, kTcChunk * 128);
-          for (int hf = 0; hf < NH; ++hf, ++n) {
-            const int cst = n % kTcCanStages;
-            if (!pf_wait(&full_can[cst], (n / kTcCanStages) & 1, abort_flag, &w0)) {
-              ok = false;
-              break;
-            }
-            tc_fence_after();
-            if (hf == 0)  // the chunk's activation scales, once for both halves
+          const uint32_t sfb_col = tbase + kPfTmemSfb + 24 * bst;
+          // each copy costs tensor-pipe time: rows 128..255 of a group's scales only when N > 128
 #pragma unroll
-              for (int at = 0; at < kPfSfbAtoms; ++at)
-                tc_cp_sf(sfb_col + 4 * at, umma_desc(smem_addr(bd + kPfBBytes + 512 * at), 128, 128));
-            const uint32_t dcol = tbase + (hf ? kPfTmemUp : 0);
-            const uint32_t sfa_col = tbase + kPfTmemSfa + 16 * cst;
-            const uint32_t a_col = tbase + kPfTmemA + kTcTmemAStage * cst;
-            bool acc = acc_h[hf];
+          for (int gq = 0; gq < kPfSfbGroups; ++gq)
 #pragma unroll
-            for (int s = 0; s < kTcChunk / 2; ++s) {
-              if (s < nbc / 2) {
-                const uint32_t sfa_id = 2u * (s & 1);
-                const int blk = wb + 2 * s;
-                const uint32_t sfb_id = (uint32_t)(blk & 3);
-                const uint32_t tsfa = (sfa_col + 4 * (s >> 1)) | (sfa_id << 30);
-                const uint32_t tsfb = (sfb_col + 4 * ((blk >> 2) - (wb >> 2))) | (sfb_id << 30);
-                mma_mxf4_ts(dcol, a_col + 8 * s, bd0 + (uint64_t)(16 * s), idesc_mxf4(128, N, sfa_id, sfb_id), tsfa,
-                            tsfb, acc ? 1u : 0u);
-                acc = true;
-              }
+            for (int h = 0; h < 2; ++h)
+              if (h == 0 || N > 128)
+                tc_cp_sf(sfb_col + 8 * gq + 4 * h, umma_desc(smem_addr(bd + kPfBBytes + 1024 * gq + 512 * h), 128, 128));
+          const uint8_t* as = aop + cst * kPfAStageBytes;
+          const uint32_t sfa_col = tbase + kPfTmemSfa + 16 * cst;  // stored by the repack warps
+          // A: core matrix (M-row group g, block b) at g*1280 + b*128; B: (slot t, block b) at
+          // t*1280 + b*128; both +256 bytes (+16) per MMA
+          const uint64_t ad0 = umma_desc(smem_addr(as), 128, kPfChunk * 128);
+          const uint64_t bd0 = umma_desc(smem_addr(bd), 128, kPfChunk * 128);
+#pragma unroll
+          for (int s = 0; s < kPfChunk / 2; ++s) {
+            if (s < nbc / 2) {
+              const uint32_t sfa_id = 2u * (s & 1);
+              const int blk = wb + 2 * s;
+              const uint32_t sfb_id = (uint32_t)(blk & 3);
+              const uint32_t tsfa = (sfa_col + 4 * (s >> 1)) | (sfa_id << 30);
+              const uint32_t tsfb = (sfb_col + 8 * ((blk >> 2) - (wb >> 2))) | (sfb_id << 30);
+              mma_mxf4(tbase, ad0 + (uint64_t)(16 * s), bd0 + (uint64_t)(16 * s), idesc_mxf4(128, N, sfa_id, sfb_id),
+                       tsfa, tsfb, acc ? 1u : 0u);
+              acc = true;
             }
-            acc_h[hf] = acc;
-            tc_commit(&empty_can[cst]);
           }
-          if (!ok) break;
-          tc_commit(&empty_b[bst]);  // both halves' MMAs have read the stage
-          ++nbq;
+          tc_commit(&empty_can[cst]);
+          tc_commit(&empty_b[bst]);
         }
         if (!ok) break;
         tc_commit(full_d);
@@ -497,74 +540,68 @@ __global__ void __launch_bounds__(kTcThreads, 1) pf_gemm_kernel(const __grid_con
     }
   } else if (tc_repack_index(warp) >= 0) {
     // ================================================================= repack warps
-    // As in the decode kernel: quadrant q's three warps own M-rows 32q .. 32q+31 and split a
-    // chunk's 14 blocks {0-3, 12-13}, {4-7}, {8-11}; payload bytes to 4 TMEM columns per block,
-    // the E8M0 bytes of a 4-block atom to one TMEM word.
+    // Each lane owns one staged row: tile row (Gr, j) = 8*Gr + j, read from row phase j, row group Gr
+    // (quadrant q's three warps: Gr = 8*(q/2) + lane%8, j = 2*(lane/8) + q%2, so a warp's 32 reads
+    // fall in distinct banks), and M-row m = 32*q + lane of the operand (tc_row_of(m) is its tile
+    // row).  The three warps of a quadrant split a chunk's 10 blocks on scale-atom boundaries {0-3},
+    // {4-7}, {8-9}.  Each block's 16 payload bytes go to the weight operand in shared memory (the 8
+    // lanes of a 16-byte store phase write 8 distinct rows of one core matrix); the E8M0 bytes of a
+    // 4-block atom form one TMEM word (lane m, column 4*atom + m/32), stored from registers so that
+    // the tensor pipe spends no copy on them.
     const int rw = tc_repack_index(warp);
     const int q = rw / 3, wi = rw - 3 * q;
     const int Gr = 8 * (q >> 1) + (lane & 7), j = 2 * (lane >> 3) + (q & 1);
+    const int m = 32 * q + lane;
+    const uint32_t a_row = (uint32_t)((m >> 3) * (kPfChunk * 128) + (m & 7) * 16);
     const uint32_t taddr_lane = (uint32_t)(32 * q) << 16;
+    const int nblk_w = wi < 2 ? 4 : 2;
     int n = 0;
     for (int i = c; i < nitems && !*abort_flag; i += G) {
       const int2 it = items[i];
-      const int rows = min(128, a.rows_e - 128 * it.y);
-      const int gv = rows >= 128 ? 16 : rows / 8;
-      const bool row_ok = Gr < gv;
-      for (int qc = 0; qc < nq && !*abort_flag; ++qc) {
-        for (int hf = 0; hf < NH; ++hf, ++n) {  // the producer's order: (q, gate), (q, up), ..
-          const int wb = kTcChunk * qc, nbc = min(kTcChunk, nb - wb);
-          const int st = n % kPfRawStages, cst = n % kTcCanStages;
-          if (!pf_wait(&full_raw[st], (n / kPfRawStages) & 1, abort_flag, &w0)) break;
-          // this lane's row in the staged boxes, as a shared-window address (ld.shared below)
-          const uint32_t rs = smem_addr(raw) + st * kTcRawBytes + j * kTcBoxBytes + Gr * kTcBoxW +
-                              ((j * rb + 17 * wb) & 15);
-          constexpr int kU = 6;
-          uint32_t wv[kU][5];
+      const bool row_ok = Gr < pf_groups<PH>(a.rows_e, it.y);
+      for (int qc = 0; qc < nq && !*abort_flag; ++qc, ++n) {
+        const int wb = kPfChunk * qc, nbc = min(kPfChunk, nb - wb);
+        const int st = n % kPfRawStages, cst = n % kTcCanStages;
+        if (!pf_wait(&full_raw[st], (n / kPfRawStages) & 1, abort_flag, &w0)) break;
+        // this lane's row in the staged boxes, as a shared-window address (ld.shared below)
+        const uint32_t rs = smem_addr(raw) + st * kPfRawBytes + j * kPfBoxBytes + Gr * kPfBoxW +
+                            ((j * rb + 17 * wb) & 15);
+        uint32_t wv[4][5];
 #pragma unroll
-          for (int u = 0; u < kU; ++u) {
-            const int b = wi == 0 ? (u < 4 ? u : u + 8) : 4 * wi + u;
-            const bool ok = row_ok && (wi == 0 || u < 4) && b < nbc;
-            const uint32_t wa = (rs + 17 * b) & ~3u;
+        for (int u = 0; u < 4; ++u) {
+          const int b = 4 * wi + u;
+          const bool ok = row_ok && u < nblk_w && b < nbc;
+          const uint32_t wa = (rs + 17 * b) & ~3u;
 #pragma unroll
-            for (int kk = 0; kk < 5; ++kk) wv[u][kk] = ok ? lds32(wa + 4 * kk) : 0u;
-          }
-          uint32_t pay[4 * kU], sw[2] = {0u, 0u};
-#pragma unroll
-          for (int u = 0; u < kU; ++u) {
-            const int b = wi == 0 ? (u < 4 ? u : u + 8) : 4 * wi + u;
-            const uint32_t a0 = (rs + 17 * b) & 3u;
-            const uint32_t sh = 8 * ((a0 + 1) & 3);
-            const bool whole = a0 == 3;
-#pragma unroll
-            for (int kk = 0; kk < 4; ++kk)
-              pay[4 * u + kk] = whole ? wv[u][kk + 1] : __funnelshift_r(wv[u][kk], wv[u][kk + 1], sh);
-            sw[u >> 2] |= ((wv[u][0] >> (8 * a0)) & 0xFFu) << (8 * (u & 3));
-          }
-          __syncwarp();
-          if (lane == 0) mbar_arrive(&empty_raw[st]);
-          if (!pf_wait(&empty_can[cst], ((n / kTcCanStages) & 1) ^ 1, abort_flag, &w1)) break;
-          tc_fence_after();
-          const uint32_t acol = tbase + kPfTmemA + kTcTmemAStage * cst + taddr_lane;
-          const uint32_t scol = tbase + kPfTmemSfa + 16 * cst + q + taddr_lane;
-          {
-            uint32_t v16[16];
-#pragma unroll
-            for (int kk = 0; kk < 16; ++kk) v16[kk] = pay[kk];
-            tmem_st_x16(acol + 16 * wi, v16);
-            tmem_st_x1(scol + 4 * wi, sw[0]);
-            if (wi == 0) {
-              uint32_t v8[8];
-#pragma unroll
-              for (int kk = 0; kk < 8; ++kk) v8[kk] = pay[16 + kk];
-              tmem_st_x8(acol + 48, v8);
-              tmem_st_x1(scol + 12, sw[1]);
-            }
-          }
-          tmem_wait_st();
-          tc_fence_before();
-          __syncwarp();
-          if (lane == 0) mbar_arrive(&full_can[cst]);
+          for (int kk = 0; kk < 5; ++kk) wv[u][kk] = ok ? lds32(wa + 4 * kk) : 0u;
         }
+        uint32_t pay[16], sw = 0u;
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const int b = 4 * wi + u;
+          const uint32_t a0 = (rs + 17 * b) & 3u;  // the scale byte's offset in its word
+          const uint32_t sh = 8 * ((a0 + 1) & 3);
+          const bool whole = a0 == 3;                // payload is word-aligned: words 1..4
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk)
+            pay[4 * u + kk] = whole ? wv[u][kk + 1] : __funnelshift_r(wv[u][kk], wv[u][kk + 1], sh);
+          sw |= ((wv[u][0] >> (8 * a0)) & 0xFFu) << (8 * u);
+        }
+        __syncwarp();  // every lane has consumed its staged words: the raw stage can be refilled
+        if (lane == 0) mbar_arrive(&empty_raw[st]);
+        // the operand stage must have been consumed by its earlier MMAs
+        if (!pf_wait(&empty_can[cst], ((n / kTcCanStages) & 1) ^ 1, abort_flag, &w1)) break;
+        const uint32_t as = smem_addr(aop) + cst * kPfAStageBytes;
+#pragma unroll
+        for (int u = 0; u < 4; ++u)
+          if (u < nblk_w) sts128(as + a_row + (4 * wi + u) * 128, pay[4 * u], pay[4 * u + 1], pay[4 * u + 2], pay[4 * u + 3]);
+        tc_fence_after();
+        tmem_st_x1(tbase + kPfTmemSfa + 16 * cst + 4 * wi + q + taddr_lane, sw);
+        fence_proxy_async_smem();  // generic-proxy writes -> visible to the tensor core
+        tmem_wait_st();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&full_can[cst]);
       }
     }
     if (tr && rw == 0 && lane == 0) {
@@ -574,62 +611,74 @@ __global__ void __launch_bounds__(kTcThreads, 1) pf_gemm_kernel(const __grid_con
     }
   } else if (tc_epi_quadrant(warp) >= 0) {
     // ================================================================= epilogue warps
+    // D lane m is M-row m, tile row tc_row_of(m).  Phase 0: tile rows 0..63 are the gate rows and
+    // 64..127 the up rows of the same 64 neurons; quadrants 0, 1 hold gate rows and quadrants 2, 3 the
+    // up rows of the same neurons (lane for lane), which they hand over through shared memory.
     const int q = tc_epi_quadrant(warp);
     const int mrow = 32 * q + lane;
     const int row = tc_row_of(mrow);
+    const bool is_up = PH == 0 && q >= 2;
+    const int rl = PH == 0 ? (row & 63) : row;  // neuron (phase 0) or down row within the tile
     int nit = 0;
     for (int i = c; i < nitems; i += G, ++nit) {
       const int2 it = items[i];
       const int4 g = W.grp[it.x];
       const int ntok = g.z, p0 = g.y;
-      const int r = 128 * it.y + row;  // neuron (phase 1) or output row (phase 2)
+      const int r = kTileStep * it.y + rl;
       const bool valid = r < a.rows_e;
-      float b0 = 0.f, b1 = 0.f;
+      float bias = 0.f;
       if (valid) {
-        if (a.bias0) b0 = a.bias0[(int64_t)g.x * a.rows_e + r];
-        if (PH == 0 && a.bias1) b1 = a.bias1[(int64_t)g.x * a.rows_e + r];
+        const float* bp = is_up ? a.bias1 : a.bias0;
+        if (bp) bias = bp[(int64_t)g.x * a.rows_e + r];
       }
-      if (!pf_wait(full_d, nit & 1, abort_flag, &w0)) break;
-      const uint64_t tb = tr ? globaltimer_ns() : 0;
+      if (!pf_wait<128>(full_d, nit & 1, abort_flag, &w0)) break;
+      const long long tb = tr ? clock64() : 0;
       tc_fence_after();
       const uint32_t ta = tbase + ((uint32_t)(32 * q) << 16);
-      float vg[kPfGroup], vu[kPfGroup];
+      float v[kPfGroup];
 #pragma unroll
-      for (int tp = 0; tp < kPfGroup / 2; ++tp) {
-        vg[2 * tp] = vg[2 * tp + 1] = vu[2 * tp] = vu[2 * tp + 1] = 0.f;
-        if (2 * tp < ntok) {
-          uint32_t v[16], u[16];
-          tmem_ld_x16(ta + 16 * tp, v);
-          if (PH == 0) tmem_ld_x16(ta + kPfTmemUp + 16 * tp, u);
+      for (int t4 = 0; t4 < kPfGroup; t4 += 4) {  // 4 tokens (32 columns) per round trip
+        v[t4] = v[t4 + 1] = v[t4 + 2] = v[t4 + 3] = 0.f;
+        if (t4 < ntok) {
+          uint32_t x0[16], x1[16];
+          tmem_ld_x16(ta + 8 * t4, x0);
+          tmem_ld_x16(ta + 8 * t4 + 16, x1);
           tmem_wait_ld();
 #pragma unroll
           for (int h2 = 0; h2 < 2; ++h2) {
-            float sg = 0.f, su = 0.f;
+            float s0 = 0.f, s1 = 0.f;
 #pragma unroll
             for (int pl = 0; pl < 8; ++pl) {
-              sg += __uint_as_float(v[8 * h2 + pl]);
-              if (PH == 0) su += __uint_as_float(u[8 * h2 + pl]);
+              s0 += __uint_as_float(x0[8 * h2 + pl]);
+              s1 += __uint_as_float(x1[8 * h2 + pl]);
             }
-            vg[2 * tp + h2] = sg;
-            vu[2 * tp + h2] = su;
+            v[t4 + h2] = s0;
+            v[t4 + 2 + h2] = s1;
           }
         }
       }
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(empty_d);
-      if (tr) w1 += globaltimer_ns() - tb;
+      if (tr) w1 += (unsigned long long)(clock64() - tb);
       if (PH == 0) {
+        if (is_up) {
 #pragma unroll
-        for (int t = 0; t < kPfGroup; ++t)
-          if (t < ntok)
-            xchg[t * 128 + row] = valid ? activate(a.act_mode, vg[t] + b0, vu[t] + b1, a.alpha, a.limit) : 0.f;
+          for (int t = 0; t < kPfGroup; ++t)
+            if (t < ntok) xchg[t * 64 + rl] = v[t] + bias;
+        }
         named_sync(1, 128);
-        // digit planes of 32-neuron blocks: warp q takes units (t, b) = u / 4, u % 4 for u = q, q+4, ..
-        for (int u = q; u < ntok * 4; u += 4) {
-          const int t = u >> 2, b = u & 3, blk = 4 * it.y + b;
-          if (32 * blk >= a.F) continue;  // whole warps: F is a multiple of 64
-          const float av = xchg[t * 128 + 32 * b + lane];
+        if (!is_up) {
+#pragma unroll
+          for (int t = 0; t < kPfGroup; ++t)
+            if (t < ntok) xchg[t * 64 + rl] = activate(a.act_mode, v[t] + bias, xchg[t * 64 + rl], a.alpha, a.limit);
+        }
+        named_sync(1, 128);
+        // digit planes of the tile's two 32-neuron blocks: warp q takes units (t, b) = u / 2, u % 2
+        const int nb_f = a.F / 32;
+        for (int u = q; u < 2 * ntok; u += 4) {
+          const int t = u >> 1, b = u & 1, blk = 2 * it.y + b;
+          const float av = xchg[t * 64 + 32 * b + lane];
           float m = fabsf(av);
 #pragma unroll
           for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
@@ -638,20 +687,20 @@ __global__ void __launch_bounds__(kTcThreads, 1) pf_gemm_kernel(const __grid_con
           const uint32_t hi = __shfl_down_sync(0xffffffffu, cd, 16);
           const int pr = p0 + t;
           if (lane < 16) {
-            uint8_t* img = W.planes2 + ((size_t)pr * (a.F / 32) + blk) * 128;
+            uint8_t* img = W.planes2 + ((size_t)pr * nb_f + blk) * 128;
 #pragma unroll
             for (int pl = 0; pl < 8; ++pl)
               img[pl * 16 + lane] = (uint8_t)(((cd >> (4 * pl)) & 15u) | (((hi >> (4 * pl)) & 15u) << 4));
           } else if (lane < 24) {
             const int pl = lane - 16;
-            W.sf2[(size_t)it.x * W.sf2_bytes + (blk >> 2) * 512 + pf_sf_byte(t, pl, blk)] = (uint8_t)plane_scale(pl, be);
+            W.sf2[(size_t)it.x * W.sf2_bytes + pf_sf_off(t, pl, blk)] = (uint8_t)plane_scale(pl, be);
           }
         }
         named_sync(1, 128);
       } else {
 #pragma unroll
         for (int t = 0; t < kPfGroup; ++t)
-          if (t < ntok) xchg[t * 128 + row] = vg[t] + b0;
+          if (t < ntok) xchg[t * 128 + row] = v[t] + bias;
         named_sync(1, 128);
         const int r0 = 128 * it.y;
         for (int t = q; t < ntok; t += 4)
@@ -757,12 +806,12 @@ static int pf_validate(const ns_moe_layer_t* p, PfPlan* pl) {
   const int nl = p->expert_hi - p->expert_lo;
   pl->P = (int)P;
   pl->Gmax = (int)std::min<int64_t>(P, (P + kPfGroup - 1) / kPfGroup + nl);
-  pl->ns1 = (p->F + 127) / 128;
+  pl->ns1 = p->F / 64;  // gate/up tiles of 64 neurons
   pl->nr2 = (p->H + 127) / 128;
   pl->nb_h = p->H / 32;
   pl->nb_f = p->F / 32;
-  pl->sf1_bytes = ((pl->nb_h + 3) / 4 + 4) * 512;
-  pl->sf2_bytes = ((pl->nb_f + 3) / 4 + 4) * 512;
+  pl->sf1_bytes = ((pl->nb_h + 3) / 4 + 2) * 1024;  // + the groups a last chunk's scale copy reads past
+  pl->sf2_bytes = ((pl->nb_f + 3) / 4 + 2) * 1024;
   size_t off = 0;
   auto take = [&](size_t bytes) {
     const size_t o = off;
@@ -789,14 +838,14 @@ static int pf_validate(const ns_moe_layer_t* p, PfPlan* pl) {
   return NS_OK;
 }
 
-// Planes of `P` pairs x `nb` blocks x 128 bytes as a 3-D u32 tensor; box = 16 pairs x 14 blocks.
+// Planes of `P` pairs x `nb` blocks x 128 bytes as a 3-D u32 tensor; box = 32 pairs x 10 blocks.
 static int make_planes_map(CUtensorMap* m, const uint8_t* base, int P, int nb) {
   EncodeTiledFn fn;
   int st = get_encode_fn(&fn);
   if (st) return st;
   const cuuint64_t dims[3] = {32, (cuuint64_t)nb, (cuuint64_t)P};
   const cuuint64_t strides[2] = {128, (cuuint64_t)nb * 128};
-  const cuuint32_t box[3] = {32, (cuuint32_t)kTcChunk, (cuuint32_t)kPfGroup};
+  const cuuint32_t box[3] = {32, (cuuint32_t)kPfChunk, (cuuint32_t)kPfGroup};
   const cuuint32_t estr[3] = {1, 1, 1};
   CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_UINT32, 3, const_cast<uint8_t*>(base), dims, strides, box, estr,
                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
@@ -805,10 +854,29 @@ static int make_planes_map(CUtensorMap* m, const uint8_t* base, int P, int nb) {
   return NS_OK;
 }
 
+// Tensor map over `rows` GGUF rows of `rb` bytes viewed as (rows/8) groups of 8*rb bytes (16-bit
+// elements); the box is kPfBoxW bytes of `box_groups` consecutive groups.
+static int pf_row_group_map(CUtensorMap* m, const uint8_t* base, int64_t rows, int rb, int box_groups) {
+  EncodeTiledFn fn;
+  int st = get_encode_fn(&fn);
+  if (st) return st;
+  const cuuint64_t dims[2] = {(cuuint64_t)4 * rb, (cuuint64_t)(rows / 8)};  // u16 elements (rb is even)
+  const cuuint64_t strides[1] = {(cuuint64_t)8 * rb};
+  const cuuint32_t box[2] = {(cuuint32_t)(kPfBoxW / 2), (cuuint32_t)box_groups};
+  const cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, const_cast<uint8_t*>(base), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(NS_ERR_CUDA, "cuTensorMapEncodeTiled (expert rows) failed (%d)", (int)r);
+  return NS_OK;
+}
+
 static size_t pf_gemm_smem(PfGemmArgs* a) {
   size_t off = 0;
   a->off_raw = 0;
-  off += (size_t)kPfRawStages * kTcRawBytes;
+  off += (size_t)kPfRawStages * kPfRawBytes;
+  a->off_aop = (int)off;
+  off += (size_t)kTcCanStages * kPfAStageBytes;
   a->off_b = (int)off;
   off += (size_t)kPfBStages * kPfBStageBytes;
   off = align_up(off, 128);
@@ -898,10 +966,8 @@ static int pf_run(const ns_moe_layer_t* p, const PfPlan& pl, uint8_t* ws, cudaSt
   const int rb_h = (int)row_bytes_of(p->ggml_type, p->H), rb_f = (int)row_bytes_of(p->ggml_type, p->F);
   {
     const int64_t rows = (int64_t)nl * p->F;
-    st = make_row_group_map(&a.tm_a16[0], p->gate_w, rows, rb_h, 16);
-    if (!st) st = make_row_group_map(&a.tm_a8[0], p->gate_w, rows, rb_h, 8);
-    if (!st) st = make_row_group_map(&a.tm_a16[1], p->up_w, rows, rb_h, 16);
-    if (!st) st = make_row_group_map(&a.tm_a8[1], p->up_w, rows, rb_h, 8);
+    st = pf_row_group_map(&a.tm_a[0], p->gate_w, rows, rb_h, 8);
+    if (!st) st = pf_row_group_map(&a.tm_a[1], p->up_w, rows, rb_h, 8);
     if (!st) st = make_planes_map(&a.tm_b, w.planes1, pl.P, pl.nb_h);
     if (st) return st;
     a.nb = pl.nb_h;
@@ -914,12 +980,10 @@ static int pf_run(const ns_moe_layer_t* p, const PfPlan& pl, uint8_t* ws, cudaSt
   }
   {
     const int64_t rows = (int64_t)nl * p->H;
-    st = make_row_group_map(&a.tm_a16[0], p->down_w, rows, rb_f, 16);
-    if (!st) st = make_row_group_map(&a.tm_a8[0], p->down_w, rows, rb_f, 8);
+    st = pf_row_group_map(&a.tm_a[0], p->down_w, rows, rb_f, 16);
+    if (!st) st = pf_row_group_map(&a.tm_a[1], p->down_w, rows, rb_f, 8);
     if (!st) st = make_planes_map(&a.tm_b, w.planes2, pl.P, pl.nb_f);
     if (st) return st;
-    a.tm_a16[1] = a.tm_a16[0];
-    a.tm_a8[1] = a.tm_a8[0];
     a.nb = pl.nb_f;
     a.rb = rb_f;
     a.rows_e = p->H;
