@@ -234,7 +234,8 @@ int ns_moe_decode_layer_static(const ns_moe_layer_t* p, ns_stream_t stream);
  * Replaces the prefill walk of neurostream/compute/blockffn.py:171-176, 220-229
  * (per-expert dequantize + matmul over blocks) and neurostream/moe/router.py:
  * 158-166.  MXFP4 experts only (NS_ERR_UNSUPPORTED otherwise); H and F
- * multiples of 64 up to 8192; expert tensors, x and out 16-byte aligned.
+ * multiples of 64 up to 8192; expert tensors, router_w, x and out 16-byte
+ * aligned.
  * Workspace: ns_moe_prefill_workspace_bytes, 256-byte aligned, no
  * initialisation needed.  Six stream-ordered launches, no host synchronisation.
  */

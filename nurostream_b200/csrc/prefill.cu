@@ -8,8 +8,8 @@
 //   pf_norm_kernel     RMSNorm of the T tokens
 //   pf_logits_kernel   router logits (tiled product)
 //   pf_topk_kernel     top-k and routing weights
-//   pf_bucket_kernel   (token, expert) pairs sorted by (expert, token); groups of <= 16 pairs of one
-//                      expert; the work items of both GEMM phases
+//   pf_bucket_kernel   (token, expert) pairs sorted by (expert, token); groups of <= 32 pairs of one
+//                      expert; the work items of both GEMM phases (pf_bucket_bits_kernel for T <= 2048)
 //   pf_planes_kernel   digit planes of the normalised input, one copy per pair (pair order)
 //   pf_gemm_kernel<0>  gate/up rows x planes of the group's tokens; clamped SwiGLU / SiLU*up in the
 //                      epilogue, which writes the activation's digit planes (pair order)
@@ -122,54 +122,68 @@ __global__ void __launch_bounds__(256) pf_norm_kernel(const ns_moe_layer_t p, Pf
 }
 
 // Router logits L[t][e] = h[t] . W[e] + b[e] as a tiled product: a CTA of 128 threads owns 16
-// tokens x 32 experts (2 x 2 per thread), K in steps of 64 through shared memory, the next step's
-// tiles loaded into registers while the current one is multiplied; each output is one fp32 fma
-// chain in ascending k.
-constexpr int kPfLgT = 16, kPfLgE = 32, kPfLgK = 64;
+// tokens x 32 experts (2 x 2 per thread), K in steps of 64 through a 4-stage cp.async ring in
+// shared memory (three steps in flight while one is multiplied); each output is one fp32 fma chain
+// in ascending k.  WT: the router weight's element type (float, __half or __nv_bfloat16).
+constexpr int kPfLgT = 16, kPfLgE = 32, kPfLgK = 64, kPfLgStages = 4;
+constexpr int kPfLgHRow = kPfLgK * 4 + 16;                 // bytes per staged h row (padded)
+constexpr int kPfLgWRow = kPfLgK * 4 + 16;                 // room for a staged W row of any type
+constexpr int kPfLgStage = kPfLgT * kPfLgHRow + kPfLgE * kPfLgWRow;
+template <typename WT>
+__device__ __forceinline__ float pf_wval(const uint8_t* row, int k) {
+  if constexpr (sizeof(WT) == 4) return reinterpret_cast<const float*>(row)[k];
+  else if constexpr (std::is_same<WT, __half>::value) return __half2float(reinterpret_cast<const __half*>(row)[k]);
+  else return __uint_as_float((uint32_t)reinterpret_cast<const unsigned short*>(row)[k] << 16);
+}
+template <typename WT>
 __global__ void __launch_bounds__(128) pf_logits_kernel(const ns_moe_layer_t p, PfWork w, float* logits) {
-  __shared__ float hs[kPfLgT][kPfLgK + 1];
-  __shared__ float ws[kPfLgE][kPfLgK + 1];
+  extern __shared__ __align__(16) uint8_t lg_sm[];
   const int H = p.H, E = p.n_expert, T = p.T;
   const int t0 = blockIdx.x * kPfLgT, e0 = blockIdx.y * kPfLgE;
   const int tid = threadIdx.x, tx = tid & 15, ty = tid >> 4;  // experts e0 + tx, +16; tokens t0 + ty, +8
-  constexpr int kH = kPfLgT * kPfLgK / 128, kW = kPfLgE * kPfLgK / 128;  // loads per thread: 8, 16
-  float hr[kH], wr[kW];
-  auto load = [&](int k0) {
-#pragma unroll
-    for (int u = 0; u < kH; ++u) {
-      const int i = tid + 128 * u, r = i / kPfLgK, c = i - r * kPfLgK;
-      hr[u] = t0 + r < T ? w.h[(int64_t)(t0 + r) * H + k0 + c] : 0.f;
+  constexpr int kWBytes = kPfLgK * (int)sizeof(WT);            // bytes of one W row per step
+  const int nsteps = H / kPfLgK;                                // H is a multiple of 64
+  const WT* wbase = static_cast<const WT*>(p.router_w);
+  auto issue = [&](int step) {
+    if (step < nsteps) {
+      uint8_t* st = lg_sm + (step % kPfLgStages) * kPfLgStage;
+      const int k0 = step * kPfLgK;
+      for (int i = tid; i < kPfLgT * (kPfLgK * 4 / 16); i += 128) {  // 16 chunks of 16 B per h row
+        const int r = i >> 4, c = i & 15;
+        const int t = min(t0 + r, T - 1);                                // rows past T: any valid row
+        cp_async16(st + r * kPfLgHRow + 16 * c, w.h + (int64_t)t * H + k0 + 4 * c);
+      }
+      constexpr int kWChunks = kWBytes / 16;
+      for (int i = tid; i < kPfLgE * kWChunks; i += 128) {
+        const int r = i / kWChunks, c = i - r * kWChunks;
+        const int e = min(e0 + r, E - 1);
+        cp_async16(st + kPfLgT * kPfLgHRow + r * kPfLgWRow + 16 * c,
+                   reinterpret_cast<const uint8_t*>(wbase + (int64_t)e * H + k0) + 16 * c);
+      }
     }
-    load_floats<kW>(p.router_w, p.router_dtype, [&](int u) -> int64_t {
-      const int i = tid + 128 * u, r = i / kPfLgK, c = i - r * kPfLgK;
-      return e0 + r < E ? (int64_t)(e0 + r) * H + k0 + c : -1;
-    }, wr);
+    cp_async_commit();  // one group per step, empty ones included, so the wait counts stay uniform
   };
   float acc[2][2] = {{0.f, 0.f}, {0.f, 0.f}};
-  load(0);
-  for (int k0 = 0; k0 < H; k0 += kPfLgK) {  // H is a multiple of 64
-#pragma unroll
-    for (int u = 0; u < kH; ++u) {
-      const int i = tid + 128 * u;
-      hs[i / kPfLgK][i % kPfLgK] = hr[u];
-    }
-#pragma unroll
-    for (int u = 0; u < kW; ++u) {
-      const int i = tid + 128 * u;
-      ws[i / kPfLgK][i % kPfLgK] = wr[u];
-    }
-    __syncthreads();
-    if (k0 + kPfLgK < H) load(k0 + kPfLgK);
+  for (int s = 0; s < kPfLgStages - 1; ++s) issue(s);
+  for (int step = 0; step < nsteps; ++step) {
+    cp_async_wait<kPfLgStages - 2>();
+    __syncthreads();  // the step's tiles are in; every thread is done with the slot reused below
+    issue(step + kPfLgStages - 1);
+    const uint8_t* st = lg_sm + (step % kPfLgStages) * kPfLgStage;
+    const float* h0r = reinterpret_cast<const float*>(st + ty * kPfLgHRow);
+    const float* h1r = reinterpret_cast<const float*>(st + (ty + 8) * kPfLgHRow);
+    const uint8_t* w0r = st + kPfLgT * kPfLgHRow + tx * kPfLgWRow;
+    const uint8_t* w1r = w0r + 16 * kPfLgWRow;
 #pragma unroll 16
     for (int kk = 0; kk < kPfLgK; ++kk) {
-      const float h0 = hs[ty][kk], h1 = hs[ty + 8][kk], w0 = ws[tx][kk], w1 = ws[tx + 16][kk];
-      acc[0][0] = fmaf(h0, w0, acc[0][0]);
-      acc[0][1] = fmaf(h0, w1, acc[0][1]);
-      acc[1][0] = fmaf(h1, w0, acc[1][0]);
-      acc[1][1] = fmaf(h1, w1, acc[1][1]);
+      const float h0 = h0r[kk], h1 = h1r[kk], wv0 = pf_wval<WT>(w0r, kk), wv1 = pf_wval<WT>(w1r, kk);
+      acc[0][0] = fmaf(h0, wv0, acc[0][0]);
+      acc[0][1] = fmaf(h0, wv1, acc[0][1]);
+      acc[1][0] = fmaf(h1, wv0, acc[1][0]);
+      acc[1][1] = fmaf(h1, wv1, acc[1][1]);
     }
-    __syncthreads();
   }
+  cp_async_wait<0>();
 #pragma unroll
   for (int a = 0; a < 2; ++a)
 #pragma unroll
@@ -201,7 +215,7 @@ __global__ void __launch_bounds__(256) pf_topk_kernel(const ns_moe_layer_t p, Pf
 // ----------------------------------------------------------------------------- bucketing
 
 // One CTA of 1024 threads.  Pairs of local expert e are the tokens routed to it in ascending
-// order; experts ascend; e's pairs split into ceil(n/16) groups of near-equal size.
+// order; experts ascend; e's pairs split into ceil(n/32) groups of near-equal size.
 __global__ void __launch_bounds__(1024) pf_bucket_kernel(const ns_moe_layer_t p, PfWork w, int ns1, int nr2,
                                                         int ids_in_smem) {
   extern __shared__ int pf_ids_s[];  // T x k ids when they fit (ids_in_smem), else unused
@@ -266,6 +280,90 @@ __global__ void __launch_bounds__(1024) pf_bucket_kernel(const ns_moe_layer_t p,
       const int start = gi * bs + min(gi, rem), n = bs + (gi < rem ? 1 : 0);
       w.grp[g0 + gi] = make_int4(el, base + start, n, 0);
       for (int s = 0; s < n; ++s) w.pair_gs[base + start + s] = ((g0 + gi) << 5) | s;
+    }
+    for (int i = lane; i < ns1 * ng; i += 32) w.items1[ns1 * g0 + i] = make_int2(g0 + i % ng, i / ng);
+    for (int i = lane; i < nr2 * ng; i += 32) w.items2[nr2 * g0 + i] = make_int2(g0 + i % ng, i / ng);
+  }
+}
+
+// The same bucketing for T <= 2048 without serial loops: each local expert's tokens as a bitmap in
+// shared memory (one atomicOr per routed pair), per-word prefix counts, then every pair finds its
+// position (count of the expert's earlier tokens) in one step.  Same output as pf_bucket_kernel.
+constexpr int kPfBitsMaxT = 2048;
+__global__ void __launch_bounds__(1024) pf_bucket_bits_kernel(const ns_moe_layer_t p, PfWork w, int ns1, int nr2) {
+  extern __shared__ uint32_t pf_bits[];  // nl x nw token bitmaps, then nl x nw 16-bit prefixes
+  __shared__ int cnt[NS_MAX_EXPERTS], poff[NS_MAX_EXPERTS], goff[NS_MAX_EXPERTS];
+  const int T = p.T, k = p.k, lo = p.expert_lo, nl = p.expert_hi - p.expert_lo, nw = (T + 31) / 32;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  unsigned short* pre = reinterpret_cast<unsigned short*>(pf_bits + nl * nw);
+  for (int i = tid; i < nl * nw; i += 1024) pf_bits[i] = 0u;
+  __syncthreads();
+  for (int i = tid; i < T * k; i += 1024) {
+    const int el = w.ids[i] - lo, t = i / k;
+    if (el >= 0 && el < nl) atomicOr(&pf_bits[el * nw + (t >> 5)], 1u << (t & 31));
+  }
+  __syncthreads();
+  for (int el = warp; el < nl; el += 32) {  // exclusive prefix of the word counts, per expert
+    int running = 0;
+    for (int w0 = 0; w0 < nw; w0 += 32) {
+      const int wi = w0 + lane;
+      const int c = wi < nw ? __popc(pf_bits[el * nw + wi]) : 0;
+      int incl = c;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int v = __shfl_up_sync(0xffffffffu, incl, o);
+        if (lane >= o) incl += v;
+      }
+      if (wi < nw) pre[el * nw + wi] = (unsigned short)(running + incl - c);
+      running += __shfl_sync(0xffffffffu, incl, 31);
+    }
+    if (lane == 0) cnt[el] = running;
+  }
+  __syncthreads();
+  if (tid == 0) {
+    int P = 0, G = 0;
+    for (int el = 0; el < nl; ++el) {
+      poff[el] = P;
+      goff[el] = G;
+      P += cnt[el];
+      G += (cnt[el] + kPfGroup - 1) / kPfGroup;
+    }
+    w.hdr->npairs = P;
+    w.hdr->ngroups = G;
+    w.hdr->nitems1 = G * ns1;
+    w.hdr->nitems2 = G * nr2;
+  }
+  __syncthreads();
+  for (int i = tid; i < T * k; i += 1024) {
+    const int el = w.ids[i] - lo, t = i / k;
+    if (el < 0 || el >= nl) {
+      w.tok_pair[i] = -1;
+      continue;
+    }
+    const int wd = el * nw + (t >> 5);
+    const int r = pre[wd] + __popc(pf_bits[wd] & ((1u << (t & 31)) - 1u));  // earlier tokens of el
+    const int pos = poff[el] + r;
+    w.pair_tok[pos] = t;
+    w.pair_w[pos] = w.wts[i];
+    w.tok_pair[i] = pos;
+    const int c = cnt[el], ng = (c + kPfGroup - 1) / kPfGroup, bs = c / ng, rem = c - bs * ng;
+    int gi, sl;
+    if (r < rem * (bs + 1)) {
+      gi = r / (bs + 1);
+      sl = r - gi * (bs + 1);
+    } else {
+      const int r2 = r - rem * (bs + 1);
+      gi = rem + r2 / bs;
+      sl = r2 - (gi - rem) * bs;
+    }
+    w.pair_gs[pos] = ((goff[el] + gi) << 5) | sl;
+  }
+  for (int el = warp; el < nl; el += 32) {
+    const int c = cnt[el], ng = (c + kPfGroup - 1) / kPfGroup, g0 = goff[el], base = poff[el];
+    for (int gi = lane; gi < ng; gi += 32) {
+      const int bs = c / ng, rem = c - bs * ng;
+      const int start = gi * bs + min(gi, rem), n = bs + (gi < rem ? 1 : 0);
+      w.grp[g0 + gi] = make_int4(el, base + start, n, 0);
     }
     for (int i = lane; i < ns1 * ng; i += 32) w.items1[ns1 * g0 + i] = make_int2(g0 + i % ng, i / ng);
     for (int i = lane; i < nr2 * ng; i += 32) w.items2[nr2 * g0 + i] = make_int2(g0 + i % ng, i / ng);
@@ -800,8 +898,8 @@ static int pf_validate(const ns_moe_layer_t* p, PfPlan* pl) {
   if (!p->x || !p->out || !p->router_w || !p->gate_w || !p->up_w || !p->down_w)
     return fail(NS_ERR_INVALID, "ns_moe_prefill_grouped: null tensor");
   auto al16 = [](const void* q) { return (reinterpret_cast<uintptr_t>(q) & 15) == 0; };
-  if (!al16(p->gate_w) || !al16(p->up_w) || !al16(p->down_w) || !al16(p->x) || !al16(p->out))
-    return fail(NS_ERR_INVALID, "ns_moe_prefill_grouped: expert tensors, x and out must be 16-byte aligned");
+  if (!al16(p->gate_w) || !al16(p->up_w) || !al16(p->down_w) || !al16(p->x) || !al16(p->out) || !al16(p->router_w))
+    return fail(NS_ERR_INVALID, "ns_moe_prefill_grouped: expert tensors, router_w, x and out must be 16-byte aligned");
   const int64_t P = (int64_t)p->T * p->k;
   const int nl = p->expert_hi - p->expert_lo;
   pl->P = (int)P;
@@ -928,16 +1026,37 @@ static int pf_run(const ns_moe_layer_t* p, const PfPlan& pl, uint8_t* ws, cudaSt
   pf_norm_kernel<<<p->T, 256, 0, s>>>(*p, w);
   NS_CUDA_TRY(cudaGetLastError());
   float* logits = reinterpret_cast<float*>(w.ypair);  // scratch until phase 2 writes ypair
-  pf_logits_kernel<<<dim3((p->T + kPfLgT - 1) / kPfLgT, (p->n_expert + kPfLgE - 1) / kPfLgE), 128, 0, s>>>(*p, w,
-                                                                                                       logits);
-  NS_CUDA_TRY(cudaGetLastError());
+  {
+    const dim3 lgrid((p->T + kPfLgT - 1) / kPfLgT, (p->n_expert + kPfLgE - 1) / kPfLgE);
+    const size_t lsmem = (size_t)kPfLgStages * kPfLgStage;
+    if (p->router_dtype == NS_F32) {
+      NS_CUDA_TRY(cudaFuncSetAttribute(pf_logits_kernel<float>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)lsmem));
+      pf_logits_kernel<float><<<lgrid, 128, lsmem, s>>>(*p, w, logits);
+    } else if (p->router_dtype == NS_F16) {
+      NS_CUDA_TRY(cudaFuncSetAttribute(pf_logits_kernel<__half>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)lsmem));
+      pf_logits_kernel<__half><<<lgrid, 128, lsmem, s>>>(*p, w, logits);
+    } else {
+      NS_CUDA_TRY(cudaFuncSetAttribute(pf_logits_kernel<__nv_bfloat16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       (int)lsmem));
+      pf_logits_kernel<__nv_bfloat16><<<lgrid, 128, lsmem, s>>>(*p, w, logits);
+    }
+    NS_CUDA_TRY(cudaGetLastError());
+  }
   pf_topk_kernel<<<(p->T + 7) / 8, 256, 0, s>>>(*p, w, logits);
   NS_CUDA_TRY(cudaGetLastError());
-  // 2. bucket (ids staged in shared memory when they fit)
-  const size_t ids_bytes = (size_t)p->T * p->k * 4;
-  const bool ids_smem = ids_bytes <= (size_t)kPfBucketSmem;
-  NS_CUDA_TRY(cudaFuncSetAttribute(pf_bucket_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kPfBucketSmem));
-  pf_bucket_kernel<<<1, 1024, ids_smem ? ids_bytes : 0, s>>>(*p, w, pl.ns1, pl.nr2, ids_smem ? 1 : 0);
+  // 2. bucket: token bitmaps for up to 2048 tokens, else the serial scan (ids staged in shared
+  // memory when they fit)
+  const int nl = p->expert_hi - p->expert_lo;
+  const size_t bits_bytes = (size_t)nl * ((p->T + 31) / 32) * 6;
+  if (p->T <= kPfBitsMaxT && bits_bytes <= (size_t)kPfBucketSmem) {
+    NS_CUDA_TRY(cudaFuncSetAttribute(pf_bucket_bits_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kPfBucketSmem));
+    pf_bucket_bits_kernel<<<1, 1024, align_up(bits_bytes, 16), s>>>(*p, w, pl.ns1, pl.nr2);
+  } else {
+    const size_t ids_bytes = (size_t)p->T * p->k * 4;
+    const bool ids_smem = ids_bytes <= (size_t)kPfBucketSmem;
+    NS_CUDA_TRY(cudaFuncSetAttribute(pf_bucket_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kPfBucketSmem));
+    pf_bucket_kernel<<<1, 1024, ids_smem ? ids_bytes : 0, s>>>(*p, w, pl.ns1, pl.nr2, ids_smem ? 1 : 0);
+  }
   NS_CUDA_TRY(cudaGetLastError());
   // 3. phase-1 planes
   {
@@ -962,7 +1081,6 @@ static int pf_run(const ns_moe_layer_t* p, const PfPlan& pl, uint8_t* ws, cudaSt
   if (smem > (size_t)kPfSmemBudget)
     return fail(NS_ERR_UNSUPPORTED, "ns_moe_prefill_grouped: layout needs %zu bytes of shared memory", smem);
   const int grid = nsm;
-  const int nl = p->expert_hi - p->expert_lo;
   const int rb_h = (int)row_bytes_of(p->ggml_type, p->H), rb_f = (int)row_bytes_of(p->ggml_type, p->F);
   {
     const int64_t rows = (int64_t)nl * p->F;

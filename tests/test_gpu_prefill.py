@@ -39,6 +39,8 @@ def _oracle(L):
     (8, 640, 448, 2, 70),       # ~17 per expert: groups split in two; F = 3.5 tiles (a half tile)
     (32, 2880, 2880, 4, 24),    # GPT-OSS widths: 90 blocks = 6 chunks of 14 + 6
     (16, 1024, 512, 4, 1),      # one token: groups of one
+    (8, 256, 128, 2, 2100),     # past the bitmap bucketing's 2048 tokens: the serial bucketing path;
+                                # 8 blocks of K (one partial chunk), ~525 tokens per expert
 ])
 def test_prefill_matches_oracle(E, H, F, k, T):
     L = goldens.SynthLayer(_cfg(E=E, H=H, F=F, k=k, T=T))
