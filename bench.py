@@ -444,8 +444,9 @@ def run_full_decode(args, rank, world, local_rank, group):
     ``value``: K graph replays back to back, CUDA events on the launching stream, token and position
     already in HBM (the same token at position ``ctx`` every step, so every step is the same work).
     ``e2e``: ``GptOssDecoder.decode`` per step -- token id and position copied in from pinned host
-    memory, the logits copied back out.  Roofline: the step's algorithmic bytes (every weight byte
-    the token needs once, KV history read, activations) over the step time.
+    memory, the logits copied back out.  Roofline: the dominant kernel (``moe_tc_kernel``, timed alone
+    after the timed region), with the whole step's algorithmic bytes (every weight byte the token
+    needs once, KV history read, activations) over the step time beside it.
     """
     import torch
     import torch.distributed as dist
@@ -498,13 +499,37 @@ def run_full_decode(args, rank, world, local_rank, group):
     torch.cuda.synchronize()
     barrier()
     ms_e2e = e0.elapsed_time(e1)
+    # the dominant kernel alone: the MoE launches (moe_tc_kernel) of up to 20 layers back to back in
+    # their own CUDA graph (no host time between launches; each layer's own experts, so no launch
+    # finds its weights in L2), CUDA events around one replay
+    reps = min(20, shape.n_layer)
+
+    def moe_launches():
+        for l in range(reps):
+            _, _, _, xa, nxt = dec._p[l]
+            dec.moe[l](xa.view(1, -1), out=nxt.view(1, -1), add_residual=(rank == 0), ids=dec.ids[l:l + 1])
+
+    moe_launches()
+    torch.cuda.synchronize()
+    mg = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(mg):
+        moe_launches()
+    mg.replay()
+    torch.cuda.synchronize()
+    m0, m1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    m0.record(stream)
+    mg.replay()
+    m1.record(stream)
+    torch.cuda.synchronize()
+    moe_ms = m0.elapsed_time(m1) / reps
+    mg = None
     clk = clocks.stop()
     dec.check_device_errors()
     ids_ok = True
     if world > 1:
-        t = torch.tensor([ms, ms_e2e], device=dev)
+        t = torch.tensor([ms, ms_e2e, moe_ms], device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX, group=group)
-        ms, ms_e2e = float(t[0]), float(t[1])
+        ms, ms_e2e, moe_ms = float(t[0]), float(t[1]), float(t[2])
         gathered = [torch.empty_like(dec.ids) for _ in range(world)]
         dist.all_gather(gathered, dec.ids, group=group)
         ids_ok = all(torch.equal(g_, gathered[0]) for g_ in gathered)
@@ -515,6 +540,8 @@ def run_full_decode(args, rank, world, local_rank, group):
     step_ms = ms / args.steps
     peak, peak_kind = measured_peaks()
     achieved = parts["total"] / (step_ms / 1000.0) / 1e9
+    moe_bytes = parts["experts+router"] / shape.n_layer  # one MoE layer's algorithmic bytes
+    moe_achieved = moe_bytes / (moe_ms / 1000.0) / 1e9
     line = {
         "metric": METRIC, "value": round(1000.0 / step_ms, 2), "unit": UNIT, "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(step_ms, 4), "higher_is_better": True,
@@ -525,21 +552,27 @@ def run_full_decode(args, rank, world, local_rank, group):
         "e2e": {"value": round(1000.0 * args.steps / ms_e2e, 2), "unit": UNIT, "h2d_bytes_per_step": 8,
                 "d2h_bytes_per_step": 4 * shape.vocab_size},
         "gpu_launches": dec.launches_per_step * args.steps,
-        "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
-                     "frac": round(achieved / peak, 4), "traffic": None, "peak_kind": peak_kind,
-                     "kernel": "decode step: ns_embed + 36 x (dense_gemv_kernel q/k/v, attn_decode_kernel, "
-                               "dense_gemv_kernel o-proj, moe_tc_kernel) + dense_gemv_kernel LM head, one CUDA graph",
-                     "algorithmic_bytes_per_step": parts["total"],
-                     "bytes_by_part": {k: v for k, v in parts.items() if k != "total"},
-                     "launch_ms": round(step_ms, 5),
-                     "launch_ms_from": "CUDA events around the K graph replays of the timed region / K"},
+        "roofline": {"bound": "hbm", "achieved": round(moe_achieved, 1), "peak": peak, "unit": "GB/s",
+                     "frac": round(moe_achieved / peak, 4), "traffic": None, "peak_kind": peak_kind,
+                     "kernel": "moe_tc_kernel (the step's largest share: one launch per layer)",
+                     "algorithmic_bytes_per_launch": int(moe_bytes), "launch_ms": round(moe_ms, 5),
+                     "launch_ms_from": "CUDA events around one replay of a graph of the MoE launches of layers "
+                                       "0..19 back to back, after the timed region",
+                     "step": {"achieved": round(achieved, 1), "frac": round(achieved / peak, 4),
+                              "kernels": "ns_embed + 36 x (dense_gemv_kernel q/k/v, attn_decode_kernel, "
+                                         "dense_gemv_kernel o-proj, moe_tc_kernel) + dense_gemv_kernel LM head, "
+                                         "one CUDA graph",
+                              "algorithmic_bytes_per_step": parts["total"],
+                              "bytes_by_part": {k: v for k, v in parts.items() if k != "total"},
+                              "step_ms": round(step_ms, 5),
+                              "step_ms_from": "CUDA events around the K graph replays of the timed region / K"}},
         "cuda_graph": graphed,
         "routing_identical_on_all_ranks": ids_ok,
     }
-    traffic = ROOT / "profiles" / "decode_step_traffic.json"
+    traffic = ROOT / "profiles" / "moe_tc_kernel_traffic.json"
     if traffic.exists():
         try:
-            line["roofline"]["traffic"] = json.loads(traffic.read_text()).get("dram_bytes_per_step")
+            line["roofline"]["traffic"] = json.loads(traffic.read_text()).get("dram_bytes_per_launch")
         except Exception:
             pass
     if clk:
