@@ -249,7 +249,7 @@ def run_ours(args, rank, world, local_rank, group):
     torch.cuda.set_device(dev)
     shape = bench_shape(args)
     B = args.batch
-    dec = MoeDecoder(shape, dev, rank, world, group, use_graph=not args.no_graph, batch=B)
+    dec = MoeDecoder(shape, dev, rank, world, group, use_graph=not args.no_graph, batch=B, combine=args.combine)
     H = shape.hidden
     npool = 64
     pool = torch.empty((npool, B, H), device=dev, dtype=torch.float32)
@@ -343,6 +343,9 @@ def run_ours(args, rank, world, local_rank, group):
     }
     if uniq is not None:
         line["roofline"]["unique_experts_per_layer"] = round(sum(uniq) / len(uniq), 2)
+    if world > 1:
+        line["config"]["combine"] = ("ns_peer_allreduce (NVLink peer stores, one kernel per layer)"
+                                     if args.combine == "peer" else "NCCL all-reduce per layer")
     traffic = ROOT / "profiles" / "moe_tc_kernel_traffic.json"
     if traffic.exists() and shape.arch == "gpt-oss":
         try:
@@ -459,7 +462,7 @@ def run_full_decode(args, rank, world, local_rank, group):
     shape = GptOssShape(n_layer=args.layers)
     clocks = ClockSampler(local_rank)
     dec = GptOssDecoder(shape, dev, seed=0, ctx=args.ctx, max_ctx=args.ctx + 64, rank=rank, world=world,
-                        group=group, use_graph=not args.no_graph)
+                        group=group, use_graph=not args.no_graph, combine=args.combine)
     token = 1234
     dec.set_token(token, args.ctx)
     graphed = dec.capture()
@@ -569,6 +572,9 @@ def run_full_decode(args, rank, world, local_rank, group):
         "cuda_graph": graphed,
         "routing_identical_on_all_ranks": ids_ok,
     }
+    if world > 1:
+        line["config"]["combine"] = ("ns_peer_allreduce (NVLink peer stores, one kernel per layer)"
+                                     if args.combine == "peer" else "NCCL all-reduce per layer")
     traffic = ROOT / "profiles" / "moe_tc_kernel_traffic.json"
     if traffic.exists():
         try:
@@ -1072,6 +1078,8 @@ def main():
     ap.add_argument("--ref-layers", type=int, default=2)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-graph", action="store_true")
+    ap.add_argument("--combine", choices=["peer", "nccl"], default="peer",
+                    help="expert-parallel combine of the decode step (N > 1): NVLink peer memory or NCCL")
     ap.add_argument("--workload", choices=["decode", "moe", "gemv", "qwen3", "prefill", "stream"], default="decode")
     ap.add_argument("--ctx", type=int, default=2048, help="KV-cache positions before the decoded token")
     ap.add_argument("--batch", type=int, default=1, help="token rows per decode step (--workload moe / qwen3)")

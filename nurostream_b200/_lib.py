@@ -103,6 +103,16 @@ class AttnBlockParams(C.Structure):
                 ("v_cache", C.c_void_p), ("out", C.c_void_p)]
 
 
+NS_MAX_PEERS, NS_PEER_MAX_CTAS = 8, 32
+
+
+class PeerReduceParams(C.Structure):
+    """Mirror of ns_peer_reduce_t."""
+
+    _fields_ = [("world", C.c_int), ("rank", C.c_int), ("n", C.c_int64), ("cap", C.c_int64), ("data", C.c_void_p),
+                ("slots", C.c_void_p * NS_MAX_PEERS), ("flags", C.c_void_p * NS_MAX_PEERS), ("ctr", C.c_void_p)]
+
+
 _P, _I, _I64, _U64, _SZ, _F = C.c_void_p, C.c_int, C.c_int64, C.c_uint64, C.c_size_t, C.c_float
 
 SIGNATURES = {
@@ -119,6 +129,12 @@ SIGNATURES = {
     "ns_moe_decode_layer_static": (_I, [C.POINTER(MoeLayerParams), _P]),
     "ns_moe_prefill_workspace_bytes": (_I, [C.POINTER(MoeLayerParams), C.POINTER(_SZ)]),
     "ns_moe_prefill_grouped": (_I, [C.POINTER(MoeLayerParams), _P, _SZ, _P]),
+    "ns_peer_allreduce": (_I, [C.POINTER(PeerReduceParams), _P]),
+    "ns_peer_alloc": (_I, [_SZ, C.POINTER(C.c_void_p)]),
+    "ns_peer_free": (_I, [_P]),
+    "ns_ipc_handle": (_I, [_P, C.c_char_p]),
+    "ns_ipc_open": (_I, [C.c_char_p, C.POINTER(C.c_void_p)]),
+    "ns_ipc_close": (_I, [_P]),
     "ns_synth_fill": (_I, [_P, _U64, _I, _U64, _U64, _U64, _F, _I, _I, _F, _P]),
     "ns_moe_set_trace": (_I, [_P, _SZ]),
     "ns_moe_select_kernel": (_I, [_I]),

@@ -10,3 +10,4 @@
 #include "prefill.cu"
 #include "attn_block.cu"
 #include "synth.cu"
+#include "peer.cu"

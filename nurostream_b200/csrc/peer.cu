@@ -1,0 +1,126 @@
+// ns_peer_allreduce: the expert-parallel combine (a sum over the ranks of one node) through peer
+// memory, for the small per-layer vectors of decode.
+//
+// Under expert parallelism every rank computes its local experts' weighted partial of the layer
+// output (the residual on one rank) and the layer output is the sum over ranks -- the combine of
+// neurostream's _ffn_block / moe_ffn (neurostream/model/gpt_oss.py:139-177, neurostream/moe/
+// router.py:183-219) split by expert.  NCCL's all-reduce of the 11.5 KB vector takes ~9 us a layer;
+// here each rank stores its slice straight into every peer's receive slots over NVLink and raises a
+// flag there, then sums what its peers stored in its own memory:
+//
+//   CTA c of rank q:  slots[r][parity][q][slice c] = data[slice c]   for every rank r (peer stores)
+//                     flags[r][q][c] = epoch                         (release, system scope)
+//                     wait flags[q][r][c] >= epoch for every rank r  (acquire, bounded)
+//                     data[slice c] = sum over r in rank order of slots[q][parity][r][slice c]
+//
+// Every rank sums the same values in the same order, so all ranks hold identical bits.  The epoch is
+// a per-CTA counter kept in device memory (one increment per call, in lockstep on every rank because
+// every rank makes the same calls), so the call can sit in a CUDA graph and be replayed.  Receive
+// slots alternate by epoch parity: a rank can be at most one call ahead of a peer, because finishing
+// a call needs every peer's flag of that call.  Plain peer stores and loads only (no multicast
+// objects).  The wait is bounded: after ~1 s it raises NS_DEVERR_GRID_WAIT and returns.
+
+namespace ns {
+
+constexpr int kPeerThreads = 256;
+
+__device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+__global__ void __launch_bounds__(kPeerThreads) peer_allreduce_kernel(const ns_peer_reduce_t p) {
+  const int c = blockIdx.x, G = gridDim.x, tid = threadIdx.x;
+  const int W = p.world, q = p.rank;
+  const int64_t per = (p.n + G - 1) / G, i0 = min(p.n, (int64_t)c * per), i1 = min(p.n, i0 + per);
+  __shared__ uint32_t s_epoch;
+  if (tid == 0) s_epoch = p.ctr[c] + 1u;
+  __syncthreads();
+  const uint32_t epoch = s_epoch, par = epoch & 1u;
+  // 1. this rank's slice into every rank's receive slot (its own included)
+  for (int r = 0; r < W; ++r) {
+    float* dst = p.slots[r] + ((int64_t)par * W + q) * p.cap;
+    for (int64_t i = i0 + tid; i < i1; i += kPeerThreads) dst[i] = p.data[i];
+  }
+  __syncthreads();
+  if (tid == 0) {
+    __threadfence_system();
+    for (int r = 0; r < W; ++r) st_release_sys(p.flags[r] + (int64_t)q * NS_PEER_MAX_CTAS + c, epoch);
+    // 2. every rank's slice of this CTA has landed here
+    const uint64_t t0 = globaltimer_ns();
+    for (int r = 0; r < W; ++r) {
+      const uint32_t* f = p.flags[q] + (int64_t)r * NS_PEER_MAX_CTAS + c;
+      while ((int32_t)(ld_acquire_sys(f) - epoch) < 0) {
+        if (globaltimer_ns() - t0 > kWaitLimitNs) {
+          raise_device_error(NS_DEVERR_GRID_WAIT);
+          break;
+        }
+        __nanosleep(20);
+      }
+    }
+    p.ctr[c] = epoch;
+  }
+  __syncthreads();
+  // 3. the sum in rank order
+  const float* mine = p.slots[q] + (int64_t)par * W * p.cap;
+  for (int64_t i = i0 + tid; i < i1; i += kPeerThreads) {
+    float s = 0.f;
+    for (int r = 0; r < W; ++r) s = __fadd_rn(s, __ldcg(mine + (int64_t)r * p.cap + i));
+    p.data[i] = s;
+  }
+}
+
+}  // namespace ns
+
+extern "C" int ns_peer_allreduce(const ns_peer_reduce_t* p, ns_stream_t stream) {
+  using namespace ns;
+  if (!p || p->world < 1 || p->world > NS_MAX_PEERS || p->rank < 0 || p->rank >= p->world)
+    return fail(NS_ERR_INVALID, "ns_peer_allreduce: bad world/rank");
+  if (p->n < 0 || p->n > p->cap || !p->data || !p->ctr)
+    return fail(NS_ERR_INVALID, "ns_peer_allreduce: n=%lld outside the slot capacity %lld", (long long)p->n,
+                (long long)p->cap);
+  for (int r = 0; r < p->world; ++r)
+    if (!p->slots[r] || !p->flags[r]) return fail(NS_ERR_INVALID, "ns_peer_allreduce: missing peer %d", r);
+  if (p->n == 0) return NS_OK;
+  const int grid = (int)std::min<int64_t>((p->n + 1023) / 1024, NS_PEER_MAX_CTAS);
+  peer_allreduce_kernel<<<grid, kPeerThreads, 0, reinterpret_cast<cudaStream_t>(stream)>>>(*p);
+  NS_CUDA_TRY(cudaGetLastError());
+  return NS_OK;
+}
+
+extern "C" int ns_peer_alloc(size_t bytes, void** ptr) {
+  if (!ptr || bytes == 0) return ns::fail(NS_ERR_INVALID, "ns_peer_alloc: bad arguments");
+  NS_CUDA_TRY(cudaMalloc(ptr, bytes));
+  NS_CUDA_TRY(cudaMemset(*ptr, 0, bytes));
+  return NS_OK;
+}
+
+extern "C" int ns_peer_free(void* ptr) {
+  if (ptr) NS_CUDA_TRY(cudaFree(ptr));
+  return NS_OK;
+}
+
+extern "C" int ns_ipc_handle(const void* ptr, uint8_t* handle) {
+  if (!ptr || !handle) return ns::fail(NS_ERR_INVALID, "ns_ipc_handle: null argument");
+  cudaIpcMemHandle_t h;
+  NS_CUDA_TRY(cudaIpcGetMemHandle(&h, const_cast<void*>(ptr)));
+  memcpy(handle, &h, sizeof h);
+  return NS_OK;
+}
+
+extern "C" int ns_ipc_open(const uint8_t* handle, void** ptr) {
+  if (!ptr || !handle) return ns::fail(NS_ERR_INVALID, "ns_ipc_open: null argument");
+  cudaIpcMemHandle_t h;
+  memcpy(&h, handle, sizeof h);
+  NS_CUDA_TRY(cudaIpcOpenMemHandle(ptr, h, cudaIpcMemLazyEnablePeerAccess));
+  return NS_OK;
+}
+
+extern "C" int ns_ipc_close(void* ptr) {
+  if (ptr) NS_CUDA_TRY(cudaIpcCloseMemHandle(ptr));
+  return NS_OK;
+}

@@ -72,7 +72,7 @@ def synth_moe_layer(sh: MoeShape, l: int, dev, lo: int, hi: int, max_tokens: int
 class MoeDecoder:
     def __init__(self, shape: MoeShape, device: torch.device | str = "cuda", rank: int = 0, world: int = 1,
                  group=None, use_graph: bool = True, max_tokens: int = 1, keep_layer_outputs: bool = False,
-                 batch: int = 1):
+                 batch: int = 1, combine: str = "peer"):
         self.shape = shape
         self.batch = batch            # token rows of one decode step (each layer one fused launch over all)
         max_tokens = max(max_tokens, batch)
@@ -92,6 +92,19 @@ class MoeDecoder:
         self.graph = None
         self.use_graph = use_graph
         self.launches_per_step = shape.n_layer
+        # expert-parallel combine of the decode step: "peer" (ns_peer_allreduce over NVLink peer
+        # memory) or "nccl" (torch.distributed.all_reduce); prefill always uses NCCL
+        self.peer = None
+        if world > 1 and combine == "peer":
+            from .peer import PeerReduce
+            self.peer = PeerReduce(batch * H, group, self.device)
+            self.launches_per_step = 2 * shape.n_layer
+
+    def _combine(self, t: torch.Tensor) -> None:
+        if self.peer is not None:
+            self.peer(t)
+        else:
+            torch.distributed.all_reduce(t, group=self.group)
 
     def _make_layer(self, l: int) -> MoeLayer:
         return synth_moe_layer(self.shape, l, self.device, self.lo, self.hi, self.max_tokens)
@@ -107,7 +120,7 @@ class MoeDecoder:
             else:  # as many rows per launch as the layer's kernel takes (halved if its activations overflow)
                 layer.prefill(cur, out=nxt, add_residual=(self.rank == 0), ids=self.ids[l])
             if self.world > 1:
-                torch.distributed.all_reduce(nxt, group=self.group)
+                self._combine(nxt)
             cur = nxt
         return cur
 
@@ -171,9 +184,12 @@ class MoeDecoder:
         return cur
 
     def release(self) -> None:
-        """Drop the graph (it may hold NCCL work) before the process group goes away."""
+        """Drop the graph (it may hold NCCL work) and the peer areas before the process group goes away."""
         self.graph = None
         self.out = None
+        if self.peer is not None:
+            self.peer.close()
+            self.peer = None
 
     def check_device_errors(self) -> None:
         bits = _lib.device_error()

@@ -19,7 +19,8 @@ any token at any position.
 
 Expert parallelism (``world > 1``): rank r holds experts [r*E/world, (r+1)*E/world) of every
 layer; everything else is replicated.  Each rank adds its local experts' weighted outputs (rank 0
-also the residual) and one all-reduce(sum) per layer combines them.
+also the residual) and one sum over the ranks per layer combines them: ``ns_peer_allreduce`` over
+NVLink peer memory (``combine="peer"``, the default) or NCCL's all-reduce (``combine="nccl"``).
 """
 from __future__ import annotations
 
@@ -159,7 +160,8 @@ class GptOssDecoder:
 
     def __init__(self, shape: GptOssShape | None = None, device="cuda", seed: int = 0, ctx: int = 2048,
                  max_ctx: int | None = None, rank: int = 0, world: int = 1, group=None, use_graph: bool = True,
-                 keep_layer_outputs: bool = False, l2_prefetch: bool = False, fused_attention: bool = False):
+                 keep_layer_outputs: bool = False, l2_prefetch: bool = False, fused_attention: bool = False,
+                 combine: str = "peer"):
         self.shape = shape = shape or GptOssShape()
         self.device = dev = torch.device(device)
         self.seed, self.ctx = seed, ctx
@@ -205,6 +207,11 @@ class GptOssDecoder:
         self.graph = None
         self.use_graph = use_graph
         self.launches_per_step = 2 + (2 if fused_attention else 4) * shape.n_layer
+        self.peer = None
+        if world > 1 and combine == "peer":
+            from .peer import PeerReduce
+            self.peer = PeerReduce(H, group, dev)
+            self.launches_per_step += shape.n_layer
 
     # ------------------------------------------------------------------ launches of one step
 
@@ -269,7 +276,9 @@ class GptOssDecoder:
                 _lib.call("ns_attn_decode", C.byref(pa), self._attn_ws_ptr, self.attn_ws_bytes, stream)
                 _lib.call("ns_dense_gemv", C.byref(po), stream)
             self.moe[l](xa.view(1, -1), out=nxt.view(1, -1), add_residual=(self.rank == 0), ids=self.ids[l:l + 1])
-            if self.world > 1:
+            if self.peer is not None:
+                self.peer(nxt)
+            elif self.world > 1:
                 torch.distributed.all_reduce(nxt, group=self.group)
         _lib.call("ns_dense_gemv", C.byref(self._head), stream)
         return self.logits
@@ -321,8 +330,11 @@ class GptOssDecoder:
         return logits_host
 
     def release(self) -> None:
-        """Drop the graph (it may hold NCCL work) before the process group goes away."""
+        """Drop the graph (it may hold NCCL work) and the peer areas before the process group goes away."""
         self.graph = None
+        if self.peer is not None:
+            self.peer.close()
+            self.peer = None
 
     def check_device_errors(self) -> None:
         bits = _lib.device_error()

@@ -15,6 +15,7 @@ STRUCTS = {
     "ns_attn_decode_t": _lib.AttnDecodeParams,
     "ns_l2_prefetch_t": _lib.L2Prefetch,
     "ns_attn_block_t": _lib.AttnBlockParams,
+    "ns_peer_reduce_t": _lib.PeerReduceParams,
 }
 
 
