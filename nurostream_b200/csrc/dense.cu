@@ -29,7 +29,10 @@ constexpr int kDenseWarps = 8;                        // compute warps
 constexpr int kDenseThreads = (kDenseWarps + 1) * 32;  // + one producer warp
 constexpr int kDenseTileRows = 8;
 constexpr int kDenseMaxStages = 8;
-constexpr int kDenseSmemBudget = 220 * 1024;
+#ifndef NS_DENSE_SMEM_KB
+#define NS_DENSE_SMEM_KB 220
+#endif
+constexpr int kDenseSmemBudget = NS_DENSE_SMEM_KB * 1024;
 constexpr int kDensePreRows = 1024;  // rows per CTA whose bias / residual are staged in shared memory
 
 struct DenseArgs {
