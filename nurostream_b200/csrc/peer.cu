@@ -38,6 +38,10 @@ __global__ void __launch_bounds__(kPeerThreads) peer_allreduce_kernel(const ns_p
   const int W = p.world, q = p.rank;
   const int64_t per = (p.n + G - 1) / G, i0 = min(p.n, (int64_t)c * per), i1 = min(p.n, i0 + per);
   __shared__ uint32_t s_epoch;
+  // launched with programmatic dependent launch: data and the counters are read after the wait; the
+  // next kernel may start after it (the library's chain invariant: trigger only after the own wait)
+  griddep_wait();
+  griddep_launch_dependents();
   if (tid == 0) s_epoch = p.ctr[c] + 1u;
   __syncthreads();
   const uint32_t epoch = s_epoch, par = epoch & 1u;
@@ -87,8 +91,16 @@ extern "C" int ns_peer_allreduce(const ns_peer_reduce_t* p, ns_stream_t stream) 
     if (!p->slots[r] || !p->flags[r]) return fail(NS_ERR_INVALID, "ns_peer_allreduce: missing peer %d", r);
   if (p->n == 0) return NS_OK;
   const int grid = (int)std::min<int64_t>((p->n + 1023) / 1024, NS_PEER_MAX_CTAS);
-  peer_allreduce_kernel<<<grid, kPeerThreads, 0, reinterpret_cast<cudaStream_t>(stream)>>>(*p);
-  NS_CUDA_TRY(cudaGetLastError());
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(kPeerThreads);
+  cfg.stream = reinterpret_cast<cudaStream_t>(stream);
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  NS_CUDA_TRY(cudaLaunchKernelEx(&cfg, peer_allreduce_kernel, *p));
   return NS_OK;
 }
 
