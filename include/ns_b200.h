@@ -372,28 +372,27 @@ int ns_embed(const void* table, int dtype, int64_t rows, int H, const int32_t* t
  * that follows each MoE layer (every rank holds its local experts' partial of
  * the layer output; neurostream/model/gpt_oss.py:139-177 and
  * neurostream/moe/router.py:183-219 sum the experts' contributions).  Every
- * rank stores its values into every rank's receive slots (NVLink peer
- * stores), raises a flag there and sums, in rank order, what the ranks stored
- * in its own memory; all ranks end with identical bits.  No reference
- * counterpart for the transport (the reference runs on one device).
+ * rank stores each value into every rank's receive slots as one 64-bit word
+ * (value, call epoch) over NVLink, and sums, in rank order, the words of this
+ * call that arrived in its own memory; all ranks end with identical bits.  No
+ * reference counterpart for the transport (the reference runs on one device).
  *
- * slots[r]: rank r's receive area, 2 * world * cap floats; flags[r]: rank r's
- * flags, world * NS_PEER_MAX_CTAS uint32 -- each allocated by its owner with
- * ns_peer_alloc (zeroed) and mapped on the other ranks with ns_ipc_handle /
- * ns_ipc_open.  ctr: this rank's NS_PEER_MAX_CTAS uint32 call counters
- * (zeroed).  Every rank must make the same sequence of calls with the same n.
- * The wait for the peers is bounded (~1 s); one that runs out raises
- * NS_DEVERR_GRID_WAIT.  Stream-ordered, graph-capturable.
+ * slots[r]: rank r's receive area, 2 * world * cap uint64 words, allocated by
+ * its owner with ns_peer_alloc (zeroed) and mapped on the other ranks with
+ * ns_ipc_handle / ns_ipc_open.  ctr: this rank's NS_PEER_MAX_CTAS uint32 call
+ * counters (zeroed).  Every rank must make the same sequence of calls with the
+ * same n.  The wait for the peers is bounded (~1 s); one that runs out raises
+ * NS_DEVERR_GRID_WAIT.  Stream-ordered, graph-capturable, launched with
+ * programmatic dependent launch.
  */
 #define NS_MAX_PEERS 8
 #define NS_PEER_MAX_CTAS 32
 typedef struct ns_peer_reduce {
   int world, rank;
   int64_t n;                     /* floats to sum, <= cap */
-  int64_t cap;                   /* floats per receive slot */
+  int64_t cap;                   /* words per receive slot */
   float* data;                   /* n fp32, this rank's input and the sum */
-  float* slots[NS_MAX_PEERS];    /* rank r's receive area (mapped) */
-  uint32_t* flags[NS_MAX_PEERS]; /* rank r's flags (mapped) */
+  uint64_t* slots[NS_MAX_PEERS]; /* rank r's receive area (mapped) */
   uint32_t* ctr;                 /* this rank's call counters */
 } ns_peer_reduce_t;
 int ns_peer_allreduce(const ns_peer_reduce_t* p, ns_stream_t stream);

@@ -110,7 +110,7 @@ class PeerReduceParams(C.Structure):
     """Mirror of ns_peer_reduce_t."""
 
     _fields_ = [("world", C.c_int), ("rank", C.c_int), ("n", C.c_int64), ("cap", C.c_int64), ("data", C.c_void_p),
-                ("slots", C.c_void_p * NS_MAX_PEERS), ("flags", C.c_void_p * NS_MAX_PEERS), ("ctr", C.c_void_p)]
+                ("slots", C.c_void_p * NS_MAX_PEERS), ("ctr", C.c_void_p)]
 
 
 _P, _I, _I64, _U64, _SZ, _F = C.c_void_p, C.c_int, C.c_int64, C.c_uint64, C.c_size_t, C.c_float

@@ -4,32 +4,32 @@
 // Under expert parallelism every rank computes its local experts' weighted partial of the layer
 // output (the residual on one rank) and the layer output is the sum over ranks -- the combine of
 // neurostream's _ffn_block / moe_ffn (neurostream/model/gpt_oss.py:139-177, neurostream/moe/
-// router.py:183-219) split by expert.  NCCL's all-reduce of the 11.5 KB vector takes ~9 us a layer;
-// here each rank stores its slice straight into every peer's receive slots over NVLink and raises a
-// flag there, then sums what its peers stored in its own memory:
+// router.py:183-219) split by expert.  Each rank stores every value straight into every rank's
+// receive slots over NVLink as one 64-bit word (value, epoch) -- the value and its arrival flag in
+// one single-copy-atomic store, the low-latency packing of NCCL's LL protocol, so no fence and no
+// separate flag -- and each rank sums, in rank order, the words whose epoch says they are this call's:
 //
-//   CTA c of rank q:  slots[r][parity][q][slice c] = data[slice c]   for every rank r (peer stores)
-//                     flags[r][q][c] = epoch                         (release, system scope)
-//                     wait flags[q][r][c] >= epoch for every rank r  (acquire, bounded)
-//                     data[slice c] = sum over r in rank order of slots[q][parity][r][slice c]
+//   thread of CTA c, rank q:  slots[r][parity][q][i] = (data[i], epoch)   for every rank r, i in slice c
+//                             wait slots[q][parity][r][i].epoch == epoch  for every rank r (bounded)
+//                             data[i] = sum over r in rank order of slots[q][parity][r][i].value
 //
 // Every rank sums the same values in the same order, so all ranks hold identical bits.  The epoch is
 // a per-CTA counter kept in device memory (one increment per call, in lockstep on every rank because
 // every rank makes the same calls), so the call can sit in a CUDA graph and be replayed.  Receive
 // slots alternate by epoch parity: a rank can be at most one call ahead of a peer, because finishing
-// a call needs every peer's flag of that call.  Plain peer stores and loads only (no multicast
+// a call needs every peer's words of that call.  Plain peer stores and loads only (no multicast
 // objects).  The wait is bounded: after ~1 s it raises NS_DEVERR_GRID_WAIT and returns.
 
 namespace ns {
 
 constexpr int kPeerThreads = 256;
 
-__device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
-  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+__device__ __forceinline__ void st_sys_u64(uint64_t* p, uint64_t v) {
+  asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
 }
-__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
-  uint32_t v;
-  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+__device__ __forceinline__ uint64_t ld_sys_u64(const uint64_t* p) {
+  uint64_t v;
+  asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
   return v;
 }
 
@@ -45,37 +45,32 @@ __global__ void __launch_bounds__(kPeerThreads) peer_allreduce_kernel(const ns_p
   if (tid == 0) s_epoch = p.ctr[c] + 1u;
   __syncthreads();
   const uint32_t epoch = s_epoch, par = epoch & 1u;
-  // 1. this rank's slice into every rank's receive slot (its own included)
-  for (int r = 0; r < W; ++r) {
-    float* dst = p.slots[r] + ((int64_t)par * W + q) * p.cap;
-    for (int64_t i = i0 + tid; i < i1; i += kPeerThreads) dst[i] = p.data[i];
+  // 1. this rank's values, tagged with the epoch, into every rank's receive slot (its own included)
+  for (int64_t i = i0 + tid; i < i1; i += kPeerThreads) {
+    const uint64_t w = ((uint64_t)epoch << 32) | __float_as_uint(p.data[i]);
+    for (int r = 0; r < W; ++r) st_sys_u64(p.slots[r] + ((int64_t)par * W + q) * p.cap + i, w);
   }
-  __syncthreads();
-  if (tid == 0) {
-    __threadfence_system();
-    for (int r = 0; r < W; ++r) st_release_sys(p.flags[r] + (int64_t)q * NS_PEER_MAX_CTAS + c, epoch);
-    // 2. every rank's slice of this CTA has landed here
-    const uint64_t t0 = globaltimer_ns();
-    for (int r = 0; r < W; ++r) {
-      const uint32_t* f = p.flags[q] + (int64_t)r * NS_PEER_MAX_CTAS + c;
-      while ((int32_t)(ld_acquire_sys(f) - epoch) < 0) {
-        if (globaltimer_ns() - t0 > kWaitLimitNs) {
-          raise_device_error(NS_DEVERR_GRID_WAIT);
-          break;
-        }
-        __nanosleep(20);
-      }
-    }
-    p.ctr[c] = epoch;
-  }
-  __syncthreads();
-  // 3. the sum in rank order
-  const float* mine = p.slots[q] + (int64_t)par * W * p.cap;
+  // 2. + 3. wait for every rank's word of each element, then the sum in rank order
+  const uint64_t* mine = p.slots[q] + (int64_t)par * W * p.cap;
+  const uint64_t t0 = globaltimer_ns();
+  bool late = false;
   for (int64_t i = i0 + tid; i < i1; i += kPeerThreads) {
     float s = 0.f;
-    for (int r = 0; r < W; ++r) s = __fadd_rn(s, __ldcg(mine + (int64_t)r * p.cap + i));
+    for (int r = 0; r < W; ++r) {
+      uint64_t w = ld_sys_u64(mine + (int64_t)r * p.cap + i);
+      while ((uint32_t)(w >> 32) != epoch && !late) {
+        if (globaltimer_ns() - t0 > kWaitLimitNs) {
+          raise_device_error(NS_DEVERR_GRID_WAIT);
+          late = true;
+        }
+        w = ld_sys_u64(mine + (int64_t)r * p.cap + i);
+      }
+      s = __fadd_rn(s, __uint_as_float((uint32_t)w));
+    }
     p.data[i] = s;
   }
+  __syncthreads();
+  if (tid == 0) p.ctr[c] = epoch;
 }
 
 }  // namespace ns
@@ -88,7 +83,7 @@ extern "C" int ns_peer_allreduce(const ns_peer_reduce_t* p, ns_stream_t stream) 
     return fail(NS_ERR_INVALID, "ns_peer_allreduce: n=%lld outside the slot capacity %lld", (long long)p->n,
                 (long long)p->cap);
   for (int r = 0; r < p->world; ++r)
-    if (!p->slots[r] || !p->flags[r]) return fail(NS_ERR_INVALID, "ns_peer_allreduce: missing peer %d", r);
+    if (!p->slots[r]) return fail(NS_ERR_INVALID, "ns_peer_allreduce: missing peer %d", r);
   if (p->n == 0) return NS_OK;
   const int grid = (int)std::min<int64_t>((p->n + 1023) / 1024, NS_PEER_MAX_CTAS);
   cudaLaunchConfig_t cfg = {};

@@ -3,8 +3,8 @@
 Under expert parallelism each rank computes its local experts' partial of a MoE layer's output and
 the layer output is the sum over ranks.  ``PeerReduce`` replaces the NCCL all-reduce of that small
 vector (one per layer in decode) with one kernel: every rank stores its values into every rank's
-receive slots and sums, in rank order, what arrived in its own memory (identical bits on every
-rank).  The receive areas are allocated by their owners and mapped on the other ranks through CUDA
+receive slots as (value, call epoch) words and sums, in rank order, what arrived in its own memory
+(identical bits on every rank).  The receive areas are allocated by their owners and mapped on the other ranks through CUDA
 IPC handles exchanged once over the process group; plain peer stores and loads, no multicast
 objects.  One process per GPU, all ranks on one node with peer access.
 """
@@ -31,35 +31,30 @@ class PeerReduce:
         self.device = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
         self.cap = int(cap)
         W = self.world
-        slot_bytes = 2 * W * self.cap * 4
-        flag_bytes = W * _lib.NS_PEER_MAX_CTAS * 4
+        slot_bytes = 2 * W * self.cap * 8  # (value, epoch) words, two parities
         self._own = []
         self._opened = []
         ptrs = []
-        for nbytes in (slot_bytes, flag_bytes, _lib.NS_PEER_MAX_CTAS * 4):
+        for nbytes in (slot_bytes, _lib.NS_PEER_MAX_CTAS * 4):
             p = C.c_void_p()
             _lib.call("ns_peer_alloc", nbytes, C.byref(p))
             self._own.append(p.value)
             ptrs.append(p.value)
-        slots, flags, self.ctr = ptrs
-        handles = []
-        for p in (slots, flags):
-            h = C.create_string_buffer(64)
-            _lib.call("ns_ipc_handle", p, h)
-            handles.append(h.raw)
+        slots, self.ctr = ptrs
+        h = C.create_string_buffer(64)
+        _lib.call("ns_ipc_handle", slots, h)
         torch.cuda.synchronize(self.device)
         gathered = [None] * W
-        dist.all_gather_object(gathered, handles, group=group)
-        self.slots, self.flags = [0] * W, [0] * W
+        dist.all_gather_object(gathered, h.raw, group=group)
+        self.slots = [0] * W
         for r in range(W):
             if r == self.rank:
-                self.slots[r], self.flags[r] = slots, flags
+                self.slots[r] = slots
                 continue
-            for i, dst in ((0, self.slots), (1, self.flags)):
-                p = C.c_void_p()
-                _lib.call("ns_ipc_open", C.c_char_p(gathered[r][i]), C.byref(p))
-                self._opened.append(p.value)
-                dst[r] = p.value
+            p = C.c_void_p()
+            _lib.call("ns_ipc_open", C.c_char_p(gathered[r]), C.byref(p))
+            self._opened.append(p.value)
+            self.slots[r] = p.value
         dist.barrier(group=group)
 
     def __call__(self, t: torch.Tensor) -> torch.Tensor:
@@ -69,7 +64,7 @@ class PeerReduce:
         p = _lib.PeerReduceParams()
         p.world, p.rank, p.n, p.cap, p.data, p.ctr = self.world, self.rank, t.numel(), self.cap, t.data_ptr(), self.ctr
         for r in range(self.world):
-            p.slots[r], p.flags[r] = self.slots[r], self.flags[r]
+            p.slots[r] = self.slots[r]
         _lib.call("ns_peer_allreduce", C.byref(p), torch.cuda.current_stream(t.device).cuda_stream)
         return t
 
