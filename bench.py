@@ -303,6 +303,9 @@ def run_ours(args, rank, world, local_rank, group):
         gathered = [torch.empty_like(dec.ids) for _ in range(world)]
         dist.all_gather(gathered, dec.ids, group=group)
         ids_ok = all(torch.equal(g, gathered[0]) for g in gathered)
+    # launches of one step: each layer's fused launches (slices of B rows), plus a combine per layer
+    launches_per_layer = 1 if B == 1 else -(-B // max(1, dec.layers[0]._slice))
+    launches = shape.n_layer * (launches_per_layer + (1 if dec.peer is not None else 0))
     dec.release()
 
     if rank != 0:
@@ -329,15 +332,15 @@ def run_ours(args, rank, world, local_rank, group):
         "config": workload_config(shape, world, B),
         "e2e": {"value": round(1000.0 * B * args.steps / ms_e2e, 2), "unit": UNIT,
                 "h2d_bytes_per_step": B * H * 4, "d2h_bytes_per_step": B * H * 4},
-        "gpu_launches": shape.n_layer * args.steps,
+        "gpu_launches": launches * args.steps,
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                      "frac": round(achieved / (peak * (1 if world == 1 else world)), 4),
                      "traffic": None, "peak_kind": peak_kind,
                      "kernel": KERNEL if shape.arch == "gpt-oss" else "moe_layer_kernel",
                      "algorithmic_bytes_per_launch": bytes_layer,
                      "launch_ms": round(per_launch_s * 1000, 5),
-                     "launch_ms_from": "CUDA events over the timed region / layer launches in it (one kernel "
-                                       "per layer, back to back in the graph)"},
+                     "launch_ms_from": "CUDA events over the timed region / layers in it (each layer "
+                                       f"{launches_per_layer} fused launch(es), back to back in the graph)"},
         "cuda_graph": graphed,
         "routing_identical_on_all_ranks": ids_ok,
     }
@@ -763,7 +766,7 @@ def run_prefill(args, rank=0, world=1, local_rank=0, group=None):
     torch.cuda.synchronize()
     barrier()
     ms_e2e = f0.elapsed_time(f1) / args.steps
-    # one layer alone, outside the graph: the grouped GEMM's six launches (CUDA events on this stream)
+    # one layer alone, outside the graph: the grouped GEMM's eight launches (CUDA events on this stream)
     layer = dec.layers[0]
     l0, l1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     reps = 5
@@ -798,18 +801,18 @@ def run_prefill(args, rank=0, world=1, local_rank=0, group=None):
         "dtype": "mxfp4 weights x 24-bit activation digit planes (mxf4 tensor cores), fp32 accumulate",
         "data": "synthetic (seeded splitmix64 GGUF bytes generated in HBM)",
         "config": {"workload": f"gpt-oss-120b-shape MoE prefill: {T} tokens x {shape.n_layer} layers, each layer one "
-                               f"grouped expert GEMM (6 launches: route, bucket, planes, gate/up+SwiGLU, down, combine)"
+                               f"grouped expert GEMM (8 launches: norm, logits, top-k, bucket, planes, gate/up+SwiGLU, down, combine)"
                                + (f" + NCCL all-reduce of the layer output over {world} ranks" if world > 1 else ""),
                    "tokens": T, "layers": shape.n_layer, "experts": E, "top_k": shape.top_k,
                    "parallelism": f"ep{world}" if world > 1 else "single",
                    "l2": "inputs larger than L2 (every layer streams its experts, 1.7 GB, from HBM)"},
         "e2e": {"value": round(T * 1000.0 / ms_e2e, 1), "unit": "tok/s", "h2d_bytes_per_step": T * H * 4,
                 "d2h_bytes_per_step": T * H * 4},
-        "gpu_launches": shape.n_layer * 6 * args.steps,
+        "gpu_launches": shape.n_layer * 8 * args.steps,
         "cuda_graph": graphed,
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                      "frac": round(achieved / peak, 4), "traffic": None, "peak_kind": peak_kind,
-                     "kernel": "pf_gemm_kernel<0>/<1> with route, bucket, planes and combine (one layer's six launches)",
+                     "kernel": "pf_gemm_kernel<0>/<1> with norm, logits, top-k, bucket, planes and combine (one layer's eight launches)",
                      "algorithmic_bytes_per_layer": layer_bytes, "layer_ms": round(layer_ms, 4),
                      "layer_ms_from": "CUDA events around 5 back-to-back calls of one layer, outside the graph",
                      "mxf4_tflops": round(flops * 8 / (layer_ms / 1000.0) / 1e12, 1),

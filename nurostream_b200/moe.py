@@ -201,12 +201,11 @@ class MoeLayer:
         T = x.shape[0]
         if out is None:
             out = torch.empty_like(x)
-        # Slices of 2 rows: MXFP4 runs them on the tensor-core layer kernel, which streams faster per
-        # token than wider CUDA-core slices; for the other types, wider slices hold more activation
-        # rows than shared memory and the kernel then reads them from L2 inside its inner loop, which
-        # measured slower than 2-row slices (Qwen3-235B shape, batch 8).  A slice the library refuses
-        # is halved once and for all.
-        size = self._slice or min(2, self.max_tokens)
+        # MXFP4: slices of 2 rows on the tensor-core layer kernel.  Other types run on the CUDA-core
+        # layer kernel, whose one-row launches measured faster per token than wider ones (Qwen3-235B
+        # shape, Q4_K: 119 us for one row, 370 us for two).  A slice the library refuses is halved
+        # once and for all.
+        size = self._slice or (min(2, self.max_tokens) if self.t == GGMLType.MXFP4 else 1)
         t0 = 0
         while t0 < T:
             t1 = min(T, t0 + size)

@@ -127,15 +127,18 @@ def test_prefill_slices_cover_every_row_and_halve_on_refusal():
 
     x = torch.arange(20, dtype=torch.float32).reshape(20, 1).contiguous()
     ids = torch.zeros((20, 4), dtype=torch.int32)
-    lay = Fake(GGMLType.Q4_K, 8, 1)           # 2-row slices refused -> halved to 1 for good
+    lay = Fake(GGMLType.MXFP4, 8, 1)          # 2-row slices refused -> halved to 1 for good
     out = lay.prefill(x, ids=ids)
     assert [c[0] for c in calls] == [1] * 20 and [c[1] for c in calls] == list(range(20))
     assert all(c[2] == c[0] for c in calls)
     assert torch.equal(out, x + 1.0) and lay._slice == 1
     calls.clear()
-    lay = Fake(GGMLType.MXFP4, 8, 8)          # slices of 2 rows
+    lay = Fake(GGMLType.MXFP4, 8, 8)          # MXFP4: slices of 2 rows
     lay.prefill(x[:5].contiguous())
     assert [c[0] for c in calls] == [2, 2, 1]
+    calls.clear()
+    Fake(GGMLType.Q4_K, 8, 8).prefill(x[:3].contiguous())   # CUDA-core types: one row per launch
+    assert [c[0] for c in calls] == [1, 1, 1]
     with pytest.raises(_lib.NsError):         # a refusal at one row is an error, not a loop
         Fake(GGMLType.Q8_0, 8, 0).prefill(x)
 
