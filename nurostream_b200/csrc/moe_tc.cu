@@ -2,7 +2,7 @@
 //
 // Same contract and results (to fp32 rounding) as moe_layer_kernel in moe.cu;
 // ns_moe_decode_layer picks this kernel when the layer qualifies
-// (moe_tc_eligible).  One cooperative launch, one CTA per SM.
+// (moe_tc_eligible).  One launch, one CTA per SM, every CTA resident at once.
 //
 // Arithmetic.  Every expert projection is D[row, plane] = sum_k W[row, k] *
 // P[plane, k] on `tcgen05.mma.kind::mxf4.block_scale.block32`:
@@ -38,8 +38,18 @@
 // combine of a row block runs when all of its pairs are done.  No grid
 // barrier follows the routing barrier.
 //
-// Warps: 0 producer (TMA), 1 MMA issuer, 2..13 repack raw rows into the
-// operand layout, 14..17 epilogue (TMEM -> registers, finish tiles).  Every
+// Operands that stay put.  Phase 1's B (the token's activation planes) and its
+// scales are built once per launch in shared memory / TMEM.  Phase 2's B (a
+// pair's SwiGLU activation planes, written to the workspace by the phase-1
+// epilogues of every CTA) is brought in once per pair by one bulk copy into
+// one of two shared-memory buffers, as soon as the pair's phase-1 tiles are
+// counted done, and its scales are copied into TMEM as its chunks first need
+// them; the repack warps never wait on other CTAs, so they keep staging
+// phase-2 weights while the activations are still being finished elsewhere.
+//
+// Warps: 0 producer (TMA), 1 MMA issuer, 12 repack warps (raw rows into the
+// operand layout), 4 epilogue warps (TMEM -> registers, finish tiles), 1
+// phase-2 image loader.  Every
 // wait is bounded; a wait that runs out raises a device error bit, stops the
 // CTA's pipeline, lets in-flight copies and MMAs land, frees TMEM and returns.
 
@@ -47,19 +57,20 @@
 
 namespace ns {
 
-constexpr int kTcWarps = 18;
+constexpr int kTcWarps = 19;
 constexpr int kTcThreads = kTcWarps * 32;
 constexpr int kTcRepackWarps = 12;
 // Warp roles.  Warp w issues from SM sub-partition w % 4 and can reach TMEM lanes 32*(w % 4) ..
 // +31.  Producer 0, MMA issuer 1; one epilogue warp and three repack warps per lane quadrant:
-// epilogue 16, 13, 14, 15 (quadrants 0..3), repack {4, 8, 12}, {5, 9, 17}, {2, 6, 10}, {3, 7, 11}.
-constexpr int kTcMmaWarp = 1, kTcProducerWarp = 0;
+// epilogue 16, 13, 14, 15 (quadrants 0..3), repack {4, 8, 12}, {5, 9, 17}, {2, 6, 10}, {3, 7, 11};
+// 18 loads the phase-2 activation images.
+constexpr int kTcMmaWarp = 1, kTcProducerWarp = 0, kTcLoaderWarp = 18;
 __device__ __forceinline__ int tc_epi_quadrant(int w) {
   return w == 16 ? 0 : w == 13 ? 1 : w == 14 ? 2 : w == 15 ? 3 : -1;
 }
 // Repack index 3*quadrant + (0..2), or -1.
 __device__ __forceinline__ int tc_repack_index(int w) {
-  if (w < 2 || w == 13 || w == 14 || w == 15 || w == 16) return -1;
+  if (w < 2 || w == 13 || w == 14 || w == 15 || w == 16 || w >= 18) return -1;
   const int q = w & 3;
   const int wi = w == 17 ? 2 : (w >> 2) - (q <= 1 ? 1 : 0);
   return 3 * q + wi;
@@ -85,15 +96,12 @@ constexpr int kTcBoxW = 272;                         // TMA box row (bytes, 136 
 constexpr int kTcBoxRows = 16;                       // row groups per box (8 for half tiles)
 constexpr int kTcBoxBytes = kTcBoxW * kTcBoxRows;    // one row phase of a chunk
 constexpr int kTcRawBytes = 8 * kTcBoxBytes;         // 8 row phases
-constexpr int kTcCanSFA = 4 * 512;                   // per operand stage: weight scale atoms (4 x 4 blocks)
-constexpr int kTcCanB = 16 * 128;                    // phase-2 B: 8 planes x 14 blocks (+pad)
-constexpr int kTcCanSFB = 4 * 512;                   // phase-2 B scale atoms
-constexpr int kTcCanBytes = kTcCanSFA + kTcCanB + kTcCanSFB;
 constexpr int kTcDCols = 32;                         // D: gate planes at +0, up planes at +16
-// TMEM columns: D buffers [0, 64); weight scales (SFA) [64, 96) and phase-2 activation scales
-// (SFB) [96, 128), 2 stages x 16 each; weights (A) [128, 256), 2 stages x 64 (14 blocks x 4 used);
-// phase-1 activation scales, resident for the whole K, [256, 384) (4 columns per 4-block atom).
-constexpr int kTcTmemSfa = 64, kTcTmemSfb = 96, kTcTmemA = 128, kTcTmemAStage = 64, kTcTmemSfb1 = 256;
+// TMEM columns: D buffers [0, 64); weight scales (SFA) [64, 96), 2 stages x 16; weights (A)
+// [128, 256), 2 stages x 64 (14 blocks x 4 used); activation scales resident for a whole K (4
+// columns per 4-block atom): phase 1 [256, 384), phase 2 (the current pair) [384, 512).
+constexpr int kTcTmemSfa = 64, kTcTmemA = 128, kTcTmemAStage = 64, kTcTmemSfb1 = 256, kTcTmemSfb2 = 384;
+constexpr int kTcB2Bufs = 2;                         // phase-2 activation images in shared memory
 constexpr int kTcTmemCols = 512;
 constexpr int kTcMaxSegs = 8;                        // tiles one CTA touches
 constexpr int kTcMaxSplit = 24;                      // CTAs one tile is split over
@@ -116,11 +124,13 @@ struct MoeTcArgs {
   float* logits;     // T x E
   float* partial;    // per CTA: 2 phase-1 slots of 2*T*128 floats, then 2 phase-2 slots of 128
   int part_floats;   // floats per CTA: (2*T + 1) * 128
-  uint8_t* actimg;   // per pair: planes [nb_f][8][16] then scales [nb_f][8]
+  uint8_t* actimg;   // per pair: planes [nb_f][8][16], then scale atoms [nb_f/4][8][16] (bytes
+                     // 0..3 of row p: plane p's scales of the atom's 4 blocks)
   float* yp;         // per pair: H fp32
   int img_bytes;
   int zero_tiles;    // counters to clear per launch
-  int off_raw, off_b1, off_sfb1, off_can, off_xchg, off_bars, off_shared;
+  int off_raw, off_b1, off_sfb1, off_b2, off_xchg, off_bars, off_shared;
+  int b2_stride;      // bytes per phase-2 image buffer: planes (nb_f * 128), then scale atoms
   int sfb1_atom;     // bytes between phase-1 scale atoms (128 * T)
   unsigned long long* trace;
 };
@@ -308,7 +318,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) moe_tc_kernel(const __grid_cons
   uint8_t* raw = smem + a.off_raw;
   uint8_t* b1 = smem + a.off_b1;
   uint8_t* sfb1 = smem + a.off_sfb1;
-  uint8_t* can = smem + a.off_can;
+  uint8_t* b2 = smem + a.off_b2;
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + a.off_bars);
   uint64_t* full_raw = bars;
   uint64_t* empty_raw = full_raw + TcRaw<NT>::kStages;
@@ -318,6 +328,8 @@ __global__ void __launch_bounds__(kTcThreads, 1) moe_tc_kernel(const __grid_cons
   uint64_t* empty_d = full_d + 2;
   uint64_t* mma_done = empty_d + 2;
   uint64_t* b1_ready = mma_done + 1;  // phase-1 activation planes built (16 builder warps)
+  uint64_t* b2_full = b1_ready + 1;   // a pair's phase-2 image landed (bulk copy)
+  uint64_t* b2_empty = b2_full + kTcB2Bufs;  // the MMAs that read an image buffer are done
   TcShared& S = *reinterpret_cast<TcShared*>(smem + a.off_shared);
   volatile int* abort_flag = &S.abort_flag;
 
@@ -337,6 +349,10 @@ __global__ void __launch_bounds__(kTcThreads, 1) moe_tc_kernel(const __grid_cons
     }
     mbar_init(mma_done, 1);
     mbar_init(b1_ready, kTcRepackWarps + 4);
+    for (int s = 0; s < kTcB2Bufs; ++s) {
+      mbar_init(&b2_full[s], 1);
+      mbar_init(&b2_empty[s], 1);
+    }
     fence_mbar_init();
     // TMA boxes and operand tiles assume a 1024-byte aligned dynamic shared-memory base
     S.abort_flag = (smem_addr(smem) & 1023u) != 0;
@@ -582,7 +598,6 @@ __global__ void __launch_bounds__(kTcThreads, 1) moe_tc_kernel(const __grid_cons
         S.slot_pair0[nslots] = npairs;
         S.nslots = nslots;
         S.npairs = npairs;
-        stamp(a.trace, kEvImages);
       }
       if (c == 0 && act) {
         if (p.ids) p.ids[lane] = e;
@@ -633,6 +648,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) moe_tc_kernel(const __grid_cons
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
+  if (tid == 0) stamp(a.trace, kEvLogits);  // every warp knows the routed work
 
   TcGeom geo;
   geo.ns1 = (F + 127) / 128;
@@ -702,11 +718,53 @@ __global__ void __launch_bounds__(kTcThreads, 1) moe_tc_kernel(const __grid_cons
         mbar_wait_bounded(&full_raw[q % TcRaw<NT>::kStages], (q / TcRaw<NT>::kStages) & 1);
       stamp(a.trace, kEvProducerLast);
     }
+  } else if (warp == kTcLoaderWarp) {
+    if (lane == 0) {
+      // ---- phase-2 activation images: for each pair this CTA's phase-2 segments use (in order),
+      // wait until all its phase-1 tiles are counted done, then one bulk copy of its image into the
+      // next of two buffers (once the MMAs that read that buffer's previous pair are done)
+      const uint32_t pl_bytes = (uint32_t)a.nb_f * 128u, sc_bytes = (uint32_t)((a.nb_f + 3) / 4) * 128u;
+      int k2 = 0, prev = -1;
+      for (int sgi = 0; sgi < nseg && !*abort_flag; ++sgi) {
+        const TcSeg& sg = S.seg[sgi];
+        if (sg.tile < geo.T1 || sg.grp == prev) continue;
+        const int pp = sg.grp, buf = k2 % kTcB2Bufs;
+        if (k2 >= kTcB2Bufs && !tc_wait(&b2_empty[buf], ((k2 / kTcB2Bufs) - 1) & 1, abort_flag)) break;
+        const unsigned* rdy = a.ready + S.pair_slot[pp];
+        const uint64_t t0 = globaltimer_ns();
+        bool ok = true;
+        while (ld_acquire_u32(rdy) < (unsigned)geo.ns1) {
+          if (*abort_flag || globaltimer_ns() - t0 > kWaitLimitNs) {
+            if (!*abort_flag) raise_device_error(NS_DEVERR_GRID_WAIT);
+            *abort_flag = 1;
+            ok = false;
+            break;
+          }
+          __nanosleep(32);
+        }
+        if (!ok) break;
+        if (k2 == 0) stamp(a.trace, kEvBarrier2);
+        // the image was written by other CTAs' generic stores (ordered by the acquire above); the
+        // bulk copy reads it through the async proxy
+        fence_proxy_async_global();
+        const uint8_t* img = a.actimg + (size_t)pp * a.img_bytes;
+        uint8_t* dst = b2 + buf * a.b2_stride;
+        mbar_arrive_expect_tx(&b2_full[buf], pl_bytes + sc_bytes);
+        bulk_g2s(dst, img, pl_bytes, &b2_full[buf]);
+        bulk_g2s(dst + pl_bytes, img + pl_bytes, sc_bytes, &b2_full[buf]);
+        ++k2;
+        prev = pp;
+      }
+      // let the issued copies land before the CTA can exit
+      for (int q = max(0, k2 - kTcB2Bufs); q < k2; ++q) mbar_wait_bounded(&b2_full[q % kTcB2Bufs], (q / kTcB2Bufs) & 1);
+    }
   } else if (warp == kTcMmaWarp) {
     // ================================================================= MMA issuer
     if (lane == 0) {
       int n = 0;
       bool have_b1 = false;
+      int k2 = -1, prev2 = -1;  // phase-2 pairs met so far (image buffer k2 % kTcB2Bufs), current pair
+      uint32_t sfb2_have = 0u;  // scale atoms of the current pair already in TMEM (nb_f <= 128: <= 32)
       for (int sgi = 0; sgi < nseg && !*abort_flag; ++sgi) {
         const TcSeg& sg = S.seg[sgi];
         const int i = sg.tile, ph = i < geo.T1 ? 0 : 1;
@@ -717,6 +775,14 @@ __global__ void __launch_bounds__(kTcThreads, 1) moe_tc_kernel(const __grid_cons
           for (int at = 0; at < (a.nb_h + 3) / 4; ++at)  // phase-1 activation scales, once per launch
             tc_cp_sf(tbase + kTcTmemSfb1 + 4 * at, umma_desc(smem_addr(sfb1 + at * a.sfb1_atom), 128, 128));
           have_b1 = true;
+        }
+        if (ph == 1 && sg.grp != prev2) {  // a new pair: its image must be in shared memory
+          ++k2;
+          prev2 = sg.grp;
+          sfb2_have = 0u;
+          if (!tc_wait(&b2_full[k2 % kTcB2Bufs], (k2 / kTcB2Bufs) & 1, abort_flag)) break;
+          tc_fence_after();
+          if (k2 == 0) stamp(a.trace, kEvImages);
         }
         if (!tc_wait(&empty_d[db], ((sgi >> 1) & 1) ^ 1, abort_flag)) break;
         const uint32_t tmem_d = tbase + kTcDCols * db;
@@ -734,30 +800,37 @@ __global__ void __launch_bounds__(kTcThreads, 1) moe_tc_kernel(const __grid_cons
             break;
           }
           tc_fence_after();
-          uint8_t* cs = can + st * kTcCanBytes;
           const uint32_t sfa_col = tbase + kTcTmemSfa + 16 * st;  // written by the repack warps
-          const uint32_t sfb_col = tbase + kTcTmemSfb + 16 * st;
           const uint32_t a_col = tbase + kTcTmemA + kTcTmemAStage * st;
-          if (ph == 1)  // phase 2: this chunk's activation scales (phase 1 uses the resident copy)
-            for (int at = 0; at < (nbc + 3) / 4; ++at)
-              tc_cp_sf(sfb_col + 4 * at, umma_desc(smem_addr(cs + kTcCanSFA + kTcCanB + at * 512), 128, 128));
           const uint32_t dcol = tmem_d + (up ? 16 : 0);
+          // B: the resident activation planes (phase 1: the token's, phase 2: the pair's image).
           // Descriptors advance by 256 bytes (2 blocks of 128 B) per MMA: +16 in the address field.
-          const uint32_t cs_addr = smem_addr(cs);
-          const uint64_t db0 = ph == 0 ? umma_desc(smem_addr(b1) + (uint32_t)w * 128u, 128, a.nb_h * 128)
-                                       : umma_desc(cs_addr + kTcCanSFA, 128, 1024);
+          const uint64_t db0 =
+              ph == 0 ? umma_desc(smem_addr(b1) + (uint32_t)w * 128u, 128, a.nb_h * 128)
+                      : umma_desc(smem_addr(b2 + (k2 % kTcB2Bufs) * a.b2_stride) + (uint32_t)w * 128u, 128, a.nb_f * 128);
+          const uint32_t sfb_base = tbase + (ph == 0 ? kTcTmemSfb1 : kTcTmemSfb2);
+          if (ph == 1) {
+            // the pair's activation scales this chunk needs, copied into TMEM on first use (after
+            // the previous pair's MMAs: tcgen05 operations of one thread run in issue order)
+            const uint8_t* sc = b2 + (k2 % kTcB2Bufs) * a.b2_stride + a.nb_f * 128;
+            for (int at = w >> 2; at <= (w + nbc - 1) >> 2; ++at)
+              if (!((sfb2_have >> at) & 1u)) {
+                tc_cp_sf(sfb_base + 4 * at, umma_desc(smem_addr(sc + at * 128), 128, 128));
+                sfb2_have |= 1u << at;
+              }
+          }
           const uint32_t idesc0 = idesc_mxf4(128, N, 0, 0);
           bool acc = up ? !fresh_up : !fresh_gate;
 #pragma unroll
           for (int s = 0; s < kTcChunk / 2; ++s) {
             if (s < nbc / 2) {
-              // weight scales: atom s/2 of the chunk; activation scales: phase 1 the resident atom of
-              // block w + 2s (w even), phase 2 atom s/2 of the chunk
+              // weight scales: atom s/2 of the chunk; activation scales: the resident atom of block
+              // w + 2s (w even)
               const uint32_t sfa_id = 2u * (s & 1);
               const int blk = w + 2 * s;
-              const uint32_t sfb_id = ph == 0 ? (uint32_t)(blk & 3) : sfa_id;
+              const uint32_t sfb_id = (uint32_t)(blk & 3);
               const uint32_t tsfa = (sfa_col + 4 * (s >> 1)) | (sfa_id << 30);
-              const uint32_t tsfb = (ph == 0 ? tbase + kTcTmemSfb1 + 4 * (blk >> 2) : sfb_col + 4 * (s >> 1)) | (sfb_id << 30);
+              const uint32_t tsfb = (sfb_base + 4 * (blk >> 2)) | (sfb_id << 30);
               mma_mxf4_ts(dcol, a_col + 8 * s, db0 + (uint64_t)(16 * s), idesc0 | (sfb_id << 4) | (sfa_id << 29),
                           tsfa, tsfb, acc ? 1u : 0u);
               acc = true;
@@ -769,6 +842,9 @@ __global__ void __launch_bounds__(kTcThreads, 1) moe_tc_kernel(const __grid_cons
         }
         if (!ok) break;
         tc_commit(&full_d[db]);
+        if (ph == 0 && (sgi + 1 == nseg || S.seg[sgi + 1].tile >= geo.T1)) stamp(a.trace, kEvPhase1End);
+        // the pair's last segment here: its image buffer may be refilled once these MMAs are done
+        if (ph == 1 && (sgi + 1 == nseg || S.seg[sgi + 1].grp != prev2)) tc_commit(&b2_empty[k2 % kTcB2Bufs]);
       }
       stamp(a.trace, kEvPhase2Images);
       tc_commit(mma_done);
@@ -791,51 +867,17 @@ __global__ void __launch_bounds__(kTcThreads, 1) moe_tc_kernel(const __grid_cons
     const uint32_t taddr_lane = (uint32_t)(32 * q) << 16;
     (void)m;
     int n = 0;
-    int ready_slot = -1;
     for (int sgi = 0; sgi < nseg && !*abort_flag; ++sgi) {
       const TcSeg& sg = S.seg[sgi];
       const int i = sg.tile, ph = i < geo.T1 ? 0 : 1, gv = geo.groups(i);
       const int rb = ph == 0 ? a.rb_h : a.rb_f;
       const bool row_ok = Gr < gv;
-      int pp = 0;
-      if (ph == 1) {
-        pp = sg.grp;
-        const int slot = S.pair_slot[pp];
-        if (slot != ready_slot) {  // this pair's activation planes must be complete (every lane acquires)
-          const unsigned target = (unsigned)geo.ns1;
-          const uint64_t t0 = globaltimer_ns();
-          while (ld_acquire_u32(a.ready + slot) < target) {
-            if (*abort_flag) break;
-            if (globaltimer_ns() - t0 > kWaitLimitNs) {
-              if (lane == 0) raise_device_error(NS_DEVERR_GRID_WAIT);
-              *abort_flag = 1;
-              break;
-            }
-            __nanosleep(64);
-          }
-          __syncwarp();
-          ready_slot = slot;
-        }
-      }
       const int k1 = sg.k1;
       for (int kb = sg.k0; kb < k1 && !*abort_flag; ++n) {
         int w, nbc;
         bool up;
         chunk_of(ph, kb, k1, &w, &nbc, &up);
         const int st = n % TcRaw<NT>::kStages, cst = n % kTcCanStages;
-        // B of phase 2 (this pair's activation planes, from L2): issue the loads before the repack
-        uint4 bv4 = make_uint4(0, 0, 0, 0);
-        uint8_t bsv = 0;
-        const int t2 = rw * 32 + lane;  // 0..383
-        if (ph == 1) {
-          const uint8_t* img = a.actimg + (size_t)pp * a.img_bytes;
-          if (t2 < nbc * 8) {
-            bv4 = __ldcg(reinterpret_cast<const uint4*>(img + (size_t)w * 128) + t2);
-          } else if (t2 >= 128 && t2 < 128 + nbc * 8) {
-            const int qq = t2 - 128;
-            bsv = __ldcg(img + (size_t)a.nb_f * 128 + (size_t)(w + (qq >> 3)) * 8 + (qq & 7));
-          }
-        }
         if (!tc_wait(&full_raw[st], (n / TcRaw<NT>::kStages) & 1, abort_flag)) break;
         if (n == 0 && rw == 0 && lane == 0) stamp(a.trace, kEvFirstTile);
         const uint8_t* rs = raw + st * kTcRawBytes + j * kTcBoxBytes + Gr * kTcBoxW + ((j * rb + 17 * w) & 15);
@@ -868,7 +910,6 @@ __global__ void __launch_bounds__(kTcThreads, 1) moe_tc_kernel(const __grid_cons
         // the operand stage (TMEM columns, phase-2 B) must have been consumed by its earlier MMAs
         if (!tc_wait(&empty_can[cst], ((n / kTcCanStages) & 1) ^ 1, abort_flag)) break;
         tc_fence_after();
-        uint8_t* cs = can + cst * kTcCanBytes;
         const uint32_t acol = tbase + kTcTmemA + kTcTmemAStage * cst + taddr_lane;
         const uint32_t scol = tbase + kTcTmemSfa + 16 * cst + q + taddr_lane;  // column 4*atom + m/32
         {
@@ -885,22 +926,11 @@ __global__ void __launch_bounds__(kTcThreads, 1) moe_tc_kernel(const __grid_cons
             tmem_st_x1(scol + 12, sw[1]);
           }
         }
-        if (ph == 1) {
-          if (t2 < nbc * 8) {
-            *reinterpret_cast<uint4*>(cs + kTcCanSFA + t2 * 16) = bv4;
-          } else if (t2 >= 128 && t2 < 128 + nbc * 8) {
-            const int qq = t2 - 128, bb = qq >> 3, pl8 = qq & 7;
-            cs[kTcCanSFA + kTcCanB + (bb >> 2) * 512 + 16 * pl8 + (bb & 3)] = bsv;
-          }
-        }
         tmem_wait_st();
-        fence_proxy_async_smem();
         tc_fence_before();
         __syncwarp();
         if (lane == 0) {
           mbar_arrive(&full_can[cst]);
-          if (rw == 0 && n == 2) stamp(a.trace, kEvPhase1End);
-          if (rw == 0 && n == 8) stamp(a.trace, kEvBarrier2);
         }
         kb += nbc;
       }
@@ -1066,10 +1096,12 @@ __global__ void __launch_bounds__(kTcThreads, 1) moe_tc_kernel(const __grid_cons
                 const uint32_t bv = ((cd >> (4 * pl)) & 15u) | (((hi >> (4 * pl)) & 15u) << 4);
                 img[(size_t)blk * 128 + pl * 16 + lane] = (uint8_t)bv;
               }
-            } else if (lane < 24) {
+            } else if (lane < 24) {  // scale atom blk/4: row pl, byte blk%4 (tcgen05.cp source layout)
               const int pl = lane - 16;
-              img[(size_t)a.nb_f * 128 + (size_t)blk * 8 + pl] = (uint8_t)plane_scale(pl, be);
+              img[(size_t)a.nb_f * 128 + (size_t)(blk >> 2) * 128 + 16 * pl + (blk & 3)] = (uint8_t)plane_scale(pl, be);
             }
+            // other CTAs bulk-copy the image (async proxy) once the count below says it is done
+            fence_proxy_async_global();
           }
           named_sync(1, 128);  // xchg is reused by the next pair
         }
@@ -1089,10 +1121,23 @@ __global__ void __launch_bounds__(kTcThreads, 1) moe_tc_kernel(const __grid_cons
         if (S.fin) {
           if (r < H)
             for (int t = 0; t < T; ++t) {
+              const float xr = p.add_residual ? p.x[(int64_t)t * H + r] : 0.f;
+              const int np = S.npairs;
               float o = 0.f;
-              for (int q2 = 0; q2 < S.npairs; ++q2)
-                if (S.pair_token[q2] == t) o = __fadd_rn(o, __fmul_rn(S.pair_w[q2], __ldcg(a.yp + (size_t)q2 * H + r)));
-              p.out[(int64_t)t * H + r] = p.add_residual ? __fadd_rn(p.x[(int64_t)t * H + r], o) : o;
+              for (int q0 = 0; q0 < np; q0 += 8) {  // eight pairs' loads in flight, then summed in order
+                float yv[8];
+#pragma unroll
+                for (int u = 0; u < 8; ++u) {
+                  const int q2 = q0 + u;
+                  yv[u] = q2 < np && S.pair_token[q2] == t ? __ldcg(a.yp + (size_t)q2 * H + r) : 0.f;
+                }
+#pragma unroll
+                for (int u = 0; u < 8; ++u) {
+                  const int q2 = q0 + u;
+                  if (q2 < np && S.pair_token[q2] == t) o = __fadd_rn(o, __fmul_rn(S.pair_w[q2], yv[u]));
+                }
+              }
+              p.out[(int64_t)t * H + r] = p.add_residual ? __fadd_rn(xr, o) : o;
             }
         }
       }
@@ -1119,10 +1164,13 @@ struct TcPlan {
 
 // Layers the tensor-core kernel takes: MXFP4 experts, T <= 2, H and F multiples of 64, tiles of
 // a phase split over at most kTcMaxSplit CTAs, 16-byte aligned expert tensors (moe_tc_aligned).
+static size_t moe_tc_smem(const ns_moe_layer_t* p, MoeTcArgs* a);
+
 static bool moe_tc_eligible(const ns_moe_layer_t* p) {
   if (p->ggml_type != NS_GGML_MXFP4 || p->T > 2) return false;
   if (p->H % 64 || p->F % 64) return false;
-  if (p->H / 32 > 128) return false;  // resident phase-1 activation scales: 4 TMEM columns per 4 blocks
+  // resident activation scales: 4 TMEM columns per 4 blocks, 128 columns for each phase
+  if (p->H / 32 > 128 || p->F / 32 > 128) return false;
   // a tile is shared by at most one CTA per chunk
   const int ch1 = 2 * ((p->H / 32 + kTcChunk - 1) / kTcChunk), ch2 = (p->F / 32 + kTcChunk - 1) / kTcChunk;
   if (ch1 > kTcMaxSplit || ch2 > kTcMaxSplit) return false;
@@ -1134,7 +1182,8 @@ static bool moe_tc_eligible(const ns_moe_layer_t* p) {
   const int64_t u1 = (int64_t)pairs * ((p->F + 127) / 128) * 2 * (p->H / 32);
   const int64_t u2 = (int64_t)pairs * ((p->H + 127) / 128) * (p->F / 32);
   if (std::max(u1, u2) * kTcGridMax >= ((int64_t)1 << 32)) return false;
-  return true;
+  MoeTcArgs layout;
+  return moe_tc_smem(p, &layout) <= (size_t)kTcSmemBudget;
 }
 
 static bool moe_tc_aligned(const ns_moe_layer_t* p) {
@@ -1147,7 +1196,7 @@ static void moe_tc_plan(const ns_moe_layer_t* p, int grid, TcPlan* t) {
   const int nb_f = p->F / 32;
   t->grid = grid;
   t->part_floats = (2 * p->T + 1) * 128;
-  t->img_bytes = (int)align_up((size_t)nb_f * 128 + (size_t)nb_f * 8, 256);
+  t->img_bytes = (int)align_up((size_t)nb_f * 128 + (size_t)((nb_f + 3) / 4) * 128, 256);
   t->max_tiles = pairs * ((p->F + 127) / 128) + pairs * ((p->H + 127) / 128);
   size_t off = kTcWsHeader;
   t->off_logits = off;
@@ -1173,9 +1222,12 @@ static size_t moe_tc_smem(const ns_moe_layer_t* p, MoeTcArgs* a) {
   a->off_sfb1 = (int)off;
   a->sfb1_atom = 128 * p->T;
   off += (size_t)((nb_h + 3) / 4) * a->sfb1_atom + 512;
-  off = align_up(off, 1024);
-  a->off_can = (int)off;
-  off += (size_t)kTcCanStages * kTcCanBytes;
+  off = align_up(off, 128);
+  // phase-2 images: planes, then scale atoms (+512: a scale copy reads 32 rows from its atom on)
+  const int nb_f = p->F / 32;
+  a->off_b2 = (int)off;
+  a->b2_stride = (int)align_up((size_t)nb_f * 128 + (size_t)((nb_f + 3) / 4) * 128 + 512, 128);
+  off += (size_t)kTcB2Bufs * a->b2_stride;
   a->off_xchg = (int)off;
   off += 128 * 4;
   off = align_up(off, 64);
@@ -1226,6 +1278,16 @@ static int make_row_group_map(CUtensorMap* m, const uint8_t* base, int64_t rows,
 
 static bool g_tc_pdl = true;  // programmatic dependent launch accepted so far
 
+// The launch is a plain one: with one CTA per SM and a grid of at most the SM count every CTA is
+// resident once the stream's previous kernel has left its SMs, and under programmatic dependent
+// launch each CTA starts (barrier set-up, TMEM, its router row and the norm weight in flight) as
+// soon as its SM frees up instead of all together; the grid-wide waits are bounded, so a grid that
+// could not become resident (other work holding SMs for over a second) ends with a device error
+// bit rather than hanging.  1 builds a cooperative launch (every CTA resident before any starts).
+#ifndef NS_MOE_TC_COOPERATIVE
+#define NS_MOE_TC_COOPERATIVE 0
+#endif
+
 template <int NT>
 static int launch_moe_tc(const MoeTcArgs& a, int grid, size_t smem, cudaStream_t stream) {
   auto kern = moe_tc_kernel<NT>;
@@ -1245,7 +1307,7 @@ static int launch_moe_tc(const MoeTcArgs& a, int grid, size_t smem, cudaStream_t
   // kernel may have written other than the layer's weights.
   cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeCooperative;
-  attr[0].val.cooperative = 1;
+  attr[0].val.cooperative = NS_MOE_TC_COOPERATIVE;
   attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
