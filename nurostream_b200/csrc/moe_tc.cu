@@ -41,7 +41,7 @@
 // Operands that stay put.  Phase 1's B (the token's activation planes) and its
 // scales are built once per launch in shared memory / TMEM.  Phase 2's B (a
 // pair's SwiGLU activation planes, written to the workspace by the phase-1
-// epilogues of every CTA) is brought in once per pair by one bulk copy into
+// epilogues of every CTA) is copied in once per pair by a loader warp into
 // one of two shared-memory buffers, as soon as the pair's phase-1 tiles are
 // counted done, and its scales are copied into TMEM as its chunks first need
 // them; the repack warps never wait on other CTAs, so they keep staging
@@ -328,7 +328,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) moe_tc_kernel(const __grid_cons
   uint64_t* empty_d = full_d + 2;
   uint64_t* mma_done = empty_d + 2;
   uint64_t* b1_ready = mma_done + 1;  // phase-1 activation planes built (16 builder warps)
-  uint64_t* b2_full = b1_ready + 1;   // a pair's phase-2 image landed (bulk copy)
+  uint64_t* b2_full = b1_ready + 1;   // a pair's phase-2 image is in shared memory (loader warp)
   uint64_t* b2_empty = b2_full + kTcB2Bufs;  // the MMAs that read an image buffer are done
   TcShared& S = *reinterpret_cast<TcShared*>(smem + a.off_shared);
   volatile int* abort_flag = &S.abort_flag;
@@ -719,44 +719,45 @@ __global__ void __launch_bounds__(kTcThreads, 1) moe_tc_kernel(const __grid_cons
       stamp(a.trace, kEvProducerLast);
     }
   } else if (warp == kTcLoaderWarp) {
-    if (lane == 0) {
-      // ---- phase-2 activation images: for each pair this CTA's phase-2 segments use (in order),
-      // wait until all its phase-1 tiles are counted done, then one bulk copy of its image into the
-      // next of two buffers (once the MMAs that read that buffer's previous pair are done)
-      const uint32_t pl_bytes = (uint32_t)a.nb_f * 128u, sc_bytes = (uint32_t)((a.nb_f + 3) / 4) * 128u;
-      int k2 = 0, prev = -1;
-      for (int sgi = 0; sgi < nseg && !*abort_flag; ++sgi) {
-        const TcSeg& sg = S.seg[sgi];
-        if (sg.tile < geo.T1 || sg.grp == prev) continue;
-        const int pp = sg.grp, buf = k2 % kTcB2Bufs;
-        if (k2 >= kTcB2Bufs && !tc_wait(&b2_empty[buf], ((k2 / kTcB2Bufs) - 1) & 1, abort_flag)) break;
+    // ---- phase-2 activation images: for each pair this CTA's phase-2 segments use (in order),
+    // lane 0 waits until all its phase-1 tiles are counted done (and the MMAs that read the target
+    // buffer's previous pair are done); then the warp copies the image from L2 into the next of two
+    // buffers with cp.async (plain loads: the epilogues that wrote it need no proxy fence) and hands
+    // it to the tensor core (proxy fence, then one arrival)
+    const int n16 = (a.nb_f * 128 + (a.nb_f + 3) / 4 * 128) / 16;
+    int k2 = 0, prev = -1;
+    for (int sgi = 0; sgi < nseg; ++sgi) {
+      const TcSeg& sg = S.seg[sgi];
+      if (sg.tile < geo.T1 || sg.grp == prev) continue;
+      const int pp = sg.grp, buf = k2 % kTcB2Bufs;
+      int ok = 1;
+      if (lane == 0) {
+        if (k2 >= kTcB2Bufs && !tc_wait(&b2_empty[buf], ((k2 / kTcB2Bufs) - 1) & 1, abort_flag)) ok = 0;
         const unsigned* rdy = a.ready + S.pair_slot[pp];
         const uint64_t t0 = globaltimer_ns();
-        bool ok = true;
-        while (ld_acquire_u32(rdy) < (unsigned)geo.ns1) {
+        while (ok && ld_acquire_u32(rdy) < (unsigned)geo.ns1) {
           if (*abort_flag || globaltimer_ns() - t0 > kWaitLimitNs) {
             if (!*abort_flag) raise_device_error(NS_DEVERR_GRID_WAIT);
             *abort_flag = 1;
-            ok = false;
-            break;
+            ok = 0;
           }
           __nanosleep(32);
         }
-        if (!ok) break;
-        if (k2 == 0) stamp(a.trace, kEvBarrier2);
-        // the image was written by other CTAs' generic stores (ordered by the acquire above); the
-        // bulk copy reads it through the async proxy
-        fence_proxy_async_global();
-        const uint8_t* img = a.actimg + (size_t)pp * a.img_bytes;
-        uint8_t* dst = b2 + buf * a.b2_stride;
-        mbar_arrive_expect_tx(&b2_full[buf], pl_bytes + sc_bytes);
-        bulk_g2s(dst, img, pl_bytes, &b2_full[buf]);
-        bulk_g2s(dst + pl_bytes, img + pl_bytes, sc_bytes, &b2_full[buf]);
-        ++k2;
-        prev = pp;
+        if (ok && k2 == 0) stamp(a.trace, kEvBarrier2);
       }
-      // let the issued copies land before the CTA can exit
-      for (int q = max(0, k2 - kTcB2Bufs); q < k2; ++q) mbar_wait_bounded(&b2_full[q % kTcB2Bufs], (q / kTcB2Bufs) & 1);
+      if (!__shfl_sync(0xffffffffu, ok, 0)) break;  // the whole warp leaves together
+      // lane 0's acquire, then this warp barrier: the other CTAs' image stores are visible to every lane
+      __syncwarp();
+      const uint4* src = reinterpret_cast<const uint4*>(a.actimg + (size_t)pp * a.img_bytes);
+      uint4* dst = reinterpret_cast<uint4*>(b2 + buf * a.b2_stride);
+      for (int i = lane; i < n16; i += 32) cp_async16(dst + i, src + i);
+      cp_async_commit();
+      cp_async_wait<0>();
+      fence_proxy_async_smem();  // generic-proxy writes to shared memory -> read by the MMAs
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&b2_full[buf]);
+      ++k2;
+      prev = pp;
     }
   } else if (warp == kTcMmaWarp) {
     // ================================================================= MMA issuer
@@ -1100,8 +1101,6 @@ __global__ void __launch_bounds__(kTcThreads, 1) moe_tc_kernel(const __grid_cons
               const int pl = lane - 16;
               img[(size_t)a.nb_f * 128 + (size_t)(blk >> 2) * 128 + 16 * pl + (blk & 3)] = (uint8_t)plane_scale(pl, be);
             }
-            // other CTAs bulk-copy the image (async proxy) once the count below says it is done
-            fence_proxy_async_global();
           }
           named_sync(1, 128);  // xchg is reused by the next pair
         }
