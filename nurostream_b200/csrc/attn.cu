@@ -18,7 +18,7 @@
 //
 // The token's own key and value come from the projection output (rotated here); the CTA of the last
 // split also writes them into the cache at slot pos for later tokens.  Under programmatic dependent
-// launch the first key block is requested before griddepcontrol.wait: cache slots below pos were
+// launch the first two key blocks are requested before griddepcontrol.wait: cache slots below pos were
 // written by kernels at least two launches back, which the stream's chain invariant (no kernel lets
 // its dependents launch before its own wait) has already completed.  Slot pos itself is never read
 // from the cache in this launch.
@@ -125,7 +125,9 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attn_decode_kernel(AttnArgs a
     }
     cp_async_commit();
   };
+  // both buffers' blocks before the wait: with 2,048 keys over 16 splits that is all of them
   if (n_blocks > 0) load_block(0);
+  if (n_blocks > 1) load_block(1);
   if (tid == 0) l2_prefetch_share(p.l2, blockIdx.x, gridDim.x);  // the next kernels' weights (hint)
 
   griddep_wait();
@@ -157,12 +159,11 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attn_decode_kernel(AttnArgs a
   float m = -INFINITY, l = 0.f, acc0 = 0.f, acc1 = 0.f;
 
   for (int b = 0; b < n_blocks; ++b) {
-    if (b + 1 < n_blocks) {
-      load_block(b + 1);
+    // block b has landed once at most the one after it is still in flight
+    if (b + 1 < n_blocks)
       cp_async_wait<1>();
-    } else {
+    else
       cp_async_wait<0>();
-    }
     const int kb = j0 + b * kAttnBlock, nb = min(kAttnBlock, j1 - kb);
     float(*dk)[kAttnKPitch] = sk[b & 1];
     float(*dv)[kAttnHd] = sv[b & 1];
@@ -211,7 +212,8 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attn_decode_kernel(AttnArgs a
         acc1 = fmaf(pj, vv.y, acc1);
       }
     }
-    __syncthreads();  // the buffer of block b is refilled by load_block(b + 2)
+    __syncthreads();  // the buffer of block b is free for block b + 2
+    if (b + 2 < n_blocks) load_block(b + 2);
   }
 
   // this split's partial result per head, in shared memory; the splits of kv head g form one thread
