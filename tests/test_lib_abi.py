@@ -76,10 +76,10 @@ def test_moe_workspace_bytes_and_validation(lib):
     # MXFP4, T <= 2: the larger of the two kernels' workspaces.  CUDA-core kernel: header
     # (barrier word, activation maxima) + logits (T*E fp32) + activations (T*k*F fp32).
     # Tensor-core kernel: header with counters + logits + split-tile partials (160 SMs x (one gate/up
-    # slot of 2T x 128 + one down slot of 128) fp32) + activation planes per pair (90 blocks x
-    # (128 + 8) B, 256-aligned) + down outputs per pair.
+    # slot of 2T x 128 + one down slot of 128) fp32) + activation image per pair (90 blocks x 128 B of
+    # planes, then 23 scale atoms x 128 B, 256-aligned) + down outputs per pair.
     v2 = 1024 + 256 + 4 * 2880 * 4
-    tc = 8192 + 256 + 160 * 3 * 128 * 4 + 4 * 12288 + 4 * 2880 * 4
+    tc = 8192 + 256 + 160 * 3 * 128 * 4 + 4 * 14592 + 4 * 2880 * 4
     assert n.value == max(v2, tc)
     assert lib.ns_moe_workspace_bytes(C.byref(_params(ggml_type=int(GGMLType.Q8_0))), C.byref(n)) == 0
     assert n.value == v2
