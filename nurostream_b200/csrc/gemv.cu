@@ -34,7 +34,6 @@ constexpr int kGemvMaxStages = 6;
 constexpr int kGemvEarlyTiles = 1;  // tiles requested before the activations are staged
 constexpr int kSmemBudget = 220 * 1024;
 constexpr int kXG = 36;     // shared-memory floats per 32-element group of x (fp32 path)
-constexpr int kXQG = 112;  // shared-memory bytes per 32-element group of x planes (integer path)
 
 template <int FMT>
 struct GemvInt8 {
@@ -217,36 +216,7 @@ __global__ void __launch_bounds__((W + 1) * 32, 1) gemv_kernel(GemvArgs a) {
       } else {
         load_floats<32>(a.x, a.x_dtype, [&](int j) -> int64_t { return (int64_t)t * a.x_stride + 32 * g + j; }, v);
       }
-      float m = 0.f, sum = 0.f;
-#pragma unroll
-      for (int j = 0; j < 32; ++j) {
-        m = fmaxf(m, fabsf(v[j]));
-        sum += v[j];
-      }
-      // max|x| < 2^e with e = be - 126; groups below 2^-104 (and non-finite ones) are taken as zeros
-      const int be = (int)((__float_as_uint(m) >> 23) & 255u);
-      const bool live = be >= 22 && be < 255;
-      const float to_fixed = __uint_as_float((uint32_t)(275 - be) << 23);  // 2^(22-e)
-      uint32_t pl[3][8] = {};
-#pragma unroll
-      for (int j = 0; j < 32; ++j) {
-        const int X = live ? __float2int_rn(v[j] * to_fixed) : 0;
-        const int d0 = ((X + 128) & 255) - 128;
-        const int X1 = (X - d0) >> 8;
-        const int d1 = ((X1 + 128) & 255) - 128;
-        const int d2 = (X1 - d1) >> 8;
-        pl[0][j >> 2] |= (uint32_t)(d0 & 255) << (8 * (j & 3));
-        pl[1][j >> 2] |= (uint32_t)(d1 & 255) << (8 * (j & 3));
-        pl[2][j >> 2] |= (uint32_t)(d2 & 255) << (8 * (j & 3));
-      }
-      uint4* grp = reinterpret_cast<uint4*>(xq + (size_t)t * xqs + (size_t)g * kXQG);
-#pragma unroll
-      for (int p = 0; p < 3; ++p) {
-        grp[2 * p] = make_uint4(pl[p][0], pl[p][1], pl[p][2], pl[p][3]);
-        grp[2 * p + 1] = make_uint4(pl[p][4], pl[p][5], pl[p][6], pl[p][7]);
-      }
-      xsc[t * ngroups + g] = live ? __uint_as_float((uint32_t)(be - 21) << 23) : 0.f;  // 2^(e-22)
-      xsum[t * ngroups + g] = sum;
+      group_planes_i8(v, xq + (size_t)t * xqs + (size_t)g * kXQG, &xsc[t * ngroups + g], &xsum[t * ngroups + g]);
     }
   } else if (a.x_dtype == NS_F32 && (reinterpret_cast<uintptr_t>(a.x) & 15) == 0 && (a.x_stride & 3) == 0) {
     // fp32 x: 4 elements a load (a group's padded row is 144 B, so float4 stores stay aligned)

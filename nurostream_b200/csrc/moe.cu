@@ -370,9 +370,102 @@ __device__ __forceinline__ void unit_cuda_core(int phase, int gi, int kc, const 
   }
 }
 
+// Layers whose Q8_0 / Q4_K experts run on dp4a against int8 activation planes (one or two tokens:
+// the planes of h and of every pair's activation row fit the shared-memory region).
+__host__ __device__ constexpr bool moe_int8_path(int fmt, int nt) {
+  return (fmt == NS_GGML_Q4_K || fmt == NS_GGML_Q8_0) && nt <= 2;
+}
+
+// The same unit for Q8_0 and Q4_K on dp4a: the activations are int8 digit planes (kXQG bytes per
+// group, token slot t's group g at xq + t*xqs + g*kXQG, its scale and sum at xsc / xsum[t*ngroups
+// + g]); each group's dot product is three exact integer dp4a chains per weight word, combined in
+// fp32 and scaled once (the fused GEMV's integer path).  rows16: the tile's rows start on 16-byte
+// boundaries (Q4_K superblocks then load as three vectors).
+template <int FMT, int NT>
+__device__ __forceinline__ void unit_int8(int phase, int gi, int kc, const uint8_t* s0base, const uint8_t* s1base,
+                                          int nvalid, int rb, int ngroups, const uint8_t* xq, int xqs,
+                                          const float* xsc, const float* xsum, const int (&tok)[NT], int nt,
+                                          float* red, int lane, bool rows16) {
+  const int g0 = (ngroups * kc) / kKChunks, g1 = (ngroups * (kc + 1)) / kKChunks;
+#pragma unroll 1
+  for (int hf = 0; hf < 2; ++hf) {
+    const uint8_t* rs[4];
+#pragma unroll
+    for (int r = 0; r < 4; ++r) rs[r] = tile_row(phase, 8 * gi + 4 * hf + r, s0base, s1base, nvalid, rb);
+    float acc[4][NT];
+#pragma unroll
+    for (int r = 0; r < 4; ++r)
+#pragma unroll
+      for (int t = 0; t < NT; ++t) acc[r][t] = 0.f;
+    for (int g = g0 + lane; g < g1; g += 32) {
+      uint32_t q[4][8];
+      float da[4], db[4];  // Q8_0: d, 0; Q4_K: d*sc, dmin*mn
+#pragma unroll
+      for (int r = 0; r < 4; ++r) {
+        if (FMT == NS_GGML_Q8_0) {
+          uint32_t w[9];
+          lds_words_unaligned<9>(rs[r] + 34 * g, w);
+          da[r] = f16_bits_to_float(w[0]);
+          db[r] = 0.f;
+#pragma unroll
+          for (int i = 0; i < 8; ++i) q[r][i] = __funnelshift_r(w[i], w[i + 1], 16);  // signed int8 x 4
+        } else {
+          QGroup<NS_GGML_Q4_K> qg;
+          if (rows16)
+            qg.load_aligned(rs[r], g);
+          else
+            qg.load(rs[r], g);
+          da[r] = qg.dsc;
+          db[r] = qg.mmn;
+#pragma unroll
+          for (int i = 0; i < 8; ++i) q[r][i] = qg.q[i];  // 0..15 x 4
+        }
+      }
+#pragma unroll
+      for (int t = 0; t < NT; ++t) {
+        if (t >= nt) continue;
+        const uint4* xp = reinterpret_cast<const uint4*>(xq + (size_t)tok[t] * xqs + (size_t)g * kXQG);
+        uint32_t xw[3][8];
+#pragma unroll
+        for (int pl = 0; pl < 3; ++pl) {
+          const uint4 lo = xp[2 * pl], hi = xp[2 * pl + 1];
+          xw[pl][0] = lo.x; xw[pl][1] = lo.y; xw[pl][2] = lo.z; xw[pl][3] = lo.w;
+          xw[pl][4] = hi.x; xw[pl][5] = hi.y; xw[pl][6] = hi.z; xw[pl][7] = hi.w;
+        }
+        const float sc = xsc[tok[t] * ngroups + g], sm = xsum[tok[t] * ngroups + g];
+#pragma unroll
+        for (int r = 0; r < 4; ++r) {
+          int s0 = 0, s1 = 0, s2 = 0;
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            s0 = __dp4a((int)q[r][i], (int)xw[0][i], s0);
+            s1 = __dp4a((int)q[r][i], (int)xw[1][i], s1);
+            s2 = __dp4a((int)q[r][i], (int)xw[2][i], s2);
+          }
+          const float f = fmaf((float)s2, 65536.f, fmaf((float)s1, 256.f, (float)s0)) * sc;
+          acc[r][t] = fmaf(f, da[r], FMT == NS_GGML_Q4_K ? fmaf(-db[r], sm, acc[r][t]) : acc[r][t]);
+        }
+      }
+    }
+#pragma unroll
+    for (int r = 0; r < 4; ++r) {
+#pragma unroll
+      for (int t = 0; t < NT; ++t) {
+        float v = warp_sum(acc[r][t]);
+        if (lane == 0 && t < nt) {
+          const int col = 8 * gi + 4 * hf + r;
+          red[(kc * kTileCols + col) * 16 + 2 * t] = v;
+          red[(kc * kTileCols + col) * 16 + 2 * t + 1] = 0.f;
+        }
+      }
+    }
+  }
+}
+
 template <int FMT, int NT>
 __global__ void __launch_bounds__(kMoeThreads, 1) moe_layer_kernel(MoeArgs a) {
   constexpr bool kMma = (FMT == NS_GGML_MXFP4);
+  constexpr bool kInt = moe_int8_path(FMT, NT);  // dp4a on int8 activation planes
   extern __shared__ __align__(128) uint8_t smem[];
   const ns_moe_layer_t& p = a.p;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -511,8 +604,20 @@ __global__ void __launch_bounds__(kMoeThreads, 1) moe_layer_kernel(MoeArgs a) {
     __syncthreads();
     for (int t = 0; t < T; ++t)
       build_xfrag(h + t * H, a.nb_h, S.sig_tok[t], ximg + t * xfrag_vec_u4(a.nb_h), tid, kMoeThreads);
-  } else if (tid < T) {
-    S.fac_tok[tid] = 1.0f;
+  } else {
+    if (tid < T) S.fac_tok[tid] = 1.0f;
+    if (kInt) {  // h of every token as int8 digit planes, one thread per (token, group)
+      uint8_t* xq = reinterpret_cast<uint8_t*>(ximg);
+      float* xsc = reinterpret_cast<float*>(xq + (size_t)T * a.nb_h * kXQG);
+      float* xsm = xsc + T * a.nb_h;
+      for (int it = tid; it < T * a.nb_h; it += kMoeThreads) {
+        const int t = it / a.nb_h, g = it - t * a.nb_h;
+        float v[32];
+#pragma unroll
+        for (int j = 0; j < 32; ++j) v[j] = h[t * H + 32 * g + j];
+        group_planes_i8(v, xq + (size_t)it * kXQG, &xsc[it], &xsm[it]);
+      }
+    }
   }
   for (int i = tid; i < T * a.rows_cta_max; i += kMoeThreads) o_acc[i] = 0.f;
   if (tid == 0) {
@@ -801,6 +906,22 @@ __global__ void __launch_bounds__(kMoeThreads, 1) moe_layer_kernel(MoeArgs a) {
         img[b * 4 + qq] = make_uint4(hi[0], hi[1], hi[2], hi[3]);
         img[ps + b * 4 + qq] = make_uint4(lo[0], lo[1], lo[2], lo[3]);
       }
+    } else if (kInt) {
+      // every pair's activation row as int8 digit planes, one thread per (pair, group)
+      uint8_t* xq = reinterpret_cast<uint8_t*>(region);
+      float* xsc = reinterpret_cast<float*>(xq + (size_t)np * a.nb_f * kXQG);
+      float* xsm = xsc + np * a.nb_f;
+      for (int it = tid; it < np * a.nb_f; it += kComputeThreads) {
+        const float4* src = reinterpret_cast<const float4*>(a.act + (int64_t)it * 32);  // row pr, group g
+        float v[32];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const float4 f = __ldcg(src + j);
+          v[4 * j] = f.x; v[4 * j + 1] = f.y; v[4 * j + 2] = f.z; v[4 * j + 3] = f.w;
+        }
+        group_planes_i8(v, xq + (size_t)it * kXQG, &xsc[it], &xsm[it]);
+      }
+      for (int pr = tid; pr < np; pr += kComputeThreads) S.fac_pair[pr] = 1.0f;
     } else {
       const int nf = np * F;
       if (!a.act_global)
@@ -870,6 +991,26 @@ __global__ void __launch_bounds__(kMoeThreads, 1) moe_layer_kernel(MoeArgs a) {
         rr[16 + g] = acc[1];
         rr[g + 8] = acc[2];
         rr[16 + g + 8] = acc[3];
+      } else if (kInt) {
+        int tok[NT];
+        const uint8_t* xq;
+        int ng;
+        if (tl.phase == 1) {
+#pragma unroll
+          for (int t = 0; t < NT; ++t) tok[t] = t < nt ? S.pair_token[pr0 + t] : 0;
+          xq = reinterpret_cast<const uint8_t*>(ximg);
+          ng = a.nb_h;
+        } else {
+#pragma unroll
+          for (int t = 0; t < NT; ++t) tok[t] = pr0 + t;
+          xq = reinterpret_cast<const uint8_t*>(region);
+          ng = a.nb_f;
+        }
+        const int nrow = tl.phase == 1 ? T : S.npairs;  // planes' rows: tokens or pairs
+        const float* xsc = reinterpret_cast<const float*>(xq + (size_t)nrow * ng * kXQG);
+        const bool rows16 = ((reinterpret_cast<uintptr_t>(s0base) | reinterpret_cast<uintptr_t>(s1base) | (uintptr_t)rb) & 15) == 0;
+        unit_int8<FMT, NT>(tl.phase, gi, kc, s0base, s1base, nvalid, rb, ng, xq, ng * kXQG, xsc, xsc + nrow * ng,
+                           tok, nt, red, lane, rows16);
       } else {
         int tok[NT];
         const float* x;
@@ -1051,13 +1192,16 @@ static int moe_validate(const ns_moe_layer_t* p, MoePlan* plan) {
 static size_t moe_layout(const ns_moe_layer_t* p, const MoePlan& plan, int grid, MoeArgs* a,
                          bool act_global = false) {
   const bool mma = p->ggml_type == NS_GGML_MXFP4;
-  a->act_global = act_global && !mma;
+  const bool i8 = moe_int8_path(p->ggml_type, p->T);
+  a->act_global = act_global && !mma && !i8;
   const int nb_h = p->H / 32, nb_f = p->F / 32;
-  // region: phase 1 = h (+ h images), phase 2 = activation images (or fp32 activations)
+  // region: phase 1 = h (+ h images or int8 planes), phase 2 = activation images, int8 planes (or
+  // fp32 activations)
   const size_t img_h = (size_t)2 * (nb_h * 4 + 4) * 16, img_f = (size_t)2 * (nb_f * 4 + 4) * 16;
   const size_t h_bytes = align_up((size_t)p->T * p->H * 4, 128);
-  const size_t r1 = h_bytes + (mma ? p->T * img_h : 0);
-  const size_t r2 = mma ? plan.pairs_max * img_f : a->act_global ? 0 : (size_t)plan.pairs_max * p->F * 4;
+  const size_t pl_h = (size_t)p->T * nb_h * (kXQG + 8), pl_f = (size_t)plan.pairs_max * nb_f * (kXQG + 8);
+  const size_t r1 = h_bytes + (mma ? p->T * img_h : i8 ? pl_h : 0);
+  const size_t r2 = mma ? plan.pairs_max * img_f : i8 ? pl_f : a->act_global ? 0 : (size_t)plan.pairs_max * p->F * 4;
   const size_t region = align_up(std::max(r1, r2), 128);
   a->rows_cta_max = (p->H + grid - 1) / grid + 1;
   const size_t oacc = align_up((size_t)p->T * a->rows_cta_max * 4, 128);

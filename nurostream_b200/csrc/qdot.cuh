@@ -49,6 +49,48 @@ __device__ __forceinline__ float byte_as_float(uint32_t w, int i, float bias_plu
 
 constexpr float k2p23 = 8388608.0f;
 
+// ----------------------------------------------------------------------------- int8 activation planes
+
+// Q8_0 and Q4_K dot products on dp4a: the activations of a 32-element group as three int8 digit
+// planes, the balanced radix-256 digits of X = rint(x * 2^(22-e)) with max|x| < 2^e (|X| <= 2^22,
+// so every digit fits int8; an exact 22-bit fixed point of the group).  A group's planes take
+// kXQG bytes (3 x 32, padded so that lanes reading consecutive groups hit different banks).
+constexpr int kXQG = 112;
+
+// v: the group's 32 values.  Writes the planes to grp (16-byte aligned) and returns the group's
+// scale 2^(e-22) (0 for groups below 2^-104 or non-finite, which are taken as zeros) and its sum.
+__device__ __forceinline__ void group_planes_i8(const float (&v)[32], uint8_t* grp, float* scale, float* sum) {
+  float m = 0.f, sm = 0.f;
+#pragma unroll
+  for (int j = 0; j < 32; ++j) {
+    m = fmaxf(m, fabsf(v[j]));
+    sm += v[j];
+  }
+  const int be = (int)((__float_as_uint(m) >> 23) & 255u);  // max|x| < 2^e, e = be - 126
+  const bool live = be >= 22 && be < 255;
+  const float to_fixed = __uint_as_float((uint32_t)(275 - be) << 23);  // 2^(22-e)
+  uint32_t pl[3][8] = {};
+#pragma unroll
+  for (int j = 0; j < 32; ++j) {
+    const int X = live ? __float2int_rn(v[j] * to_fixed) : 0;
+    const int d0 = ((X + 128) & 255) - 128;
+    const int X1 = (X - d0) >> 8;
+    const int d1 = ((X1 + 128) & 255) - 128;
+    const int d2 = (X1 - d1) >> 8;
+    pl[0][j >> 2] |= (uint32_t)(d0 & 255) << (8 * (j & 3));
+    pl[1][j >> 2] |= (uint32_t)(d1 & 255) << (8 * (j & 3));
+    pl[2][j >> 2] |= (uint32_t)(d2 & 255) << (8 * (j & 3));
+  }
+  uint4* out = reinterpret_cast<uint4*>(grp);
+#pragma unroll
+  for (int p = 0; p < 3; ++p) {
+    out[2 * p] = make_uint4(pl[p][0], pl[p][1], pl[p][2], pl[p][3]);
+    out[2 * p + 1] = make_uint4(pl[p][4], pl[p][5], pl[p][6], pl[p][7]);
+  }
+  *scale = live ? __uint_as_float((uint32_t)(be - 21) << 23) : 0.f;  // 2^(e-22)
+  *sum = sm;
+}
+
 // ----------------------------------------------------------------------------- per-format groups
 
 template <int FMT>
