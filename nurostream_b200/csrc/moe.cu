@@ -387,8 +387,13 @@ __device__ __forceinline__ void unit_int8(int phase, int gi, int kc, const uint8
                                           const float* xsc, const float* xsum, const int (&tok)[NT], int nt,
                                           float* red, int lane, bool rows16) {
   const int g0 = (ngroups * kc) / kKChunks, g1 = (ngroups * (kc + 1)) / kKChunks;
+  // a chunk of at most 16 groups (short rows, e.g. the down rows of narrow experts): the two
+  // 4-row halves run at once on the two 16-lane halves of the warp instead of one after the other
+  const bool both = g1 - g0 <= 16;
+  const int step = both ? 16 : 32, ln = both ? (lane & 15) : lane;
 #pragma unroll 1
-  for (int hf = 0; hf < 2; ++hf) {
+  for (int pass = 0; pass < (both ? 1 : 2); ++pass) {
+    const int hf = both ? (lane >> 4) : pass;
     const uint8_t* rs[4];
 #pragma unroll
     for (int r = 0; r < 4; ++r) rs[r] = tile_row(phase, 8 * gi + 4 * hf + r, s0base, s1base, nvalid, rb);
@@ -397,7 +402,7 @@ __device__ __forceinline__ void unit_int8(int phase, int gi, int kc, const uint8
     for (int r = 0; r < 4; ++r)
 #pragma unroll
       for (int t = 0; t < NT; ++t) acc[r][t] = 0.f;
-    for (int g = g0 + lane; g < g1; g += 32) {
+    for (int g = g0 + ln; g < g1; g += step) {
       uint32_t q[4][8];
       float da[4], db[4];  // Q8_0: d, 0; Q4_K: d*sc, dmin*mn
 #pragma unroll
@@ -451,8 +456,11 @@ __device__ __forceinline__ void unit_int8(int phase, int gi, int kc, const uint8
     for (int r = 0; r < 4; ++r) {
 #pragma unroll
       for (int t = 0; t < NT; ++t) {
-        float v = warp_sum(acc[r][t]);
-        if (lane == 0 && t < nt) {
+        float v = acc[r][t];  // sum over the lanes of this half (or of the warp)
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1)
+          if (o < step) v += __shfl_xor_sync(0xffffffffu, v, o);
+        if (ln == 0 && t < nt) {
           const int col = 8 * gi + 4 * hf + r;
           red[(kc * kTileCols + col) * 16 + 2 * t] = v;
           red[(kc * kTileCols + col) * 16 + 2 * t + 1] = 0.f;
