@@ -20,8 +20,10 @@
 // consumer warps split each tile as 3 row-groups x 4 K-chunks; every
 // (group, chunk) partial lands in shared memory and the group's four warps
 // reduce them in a fixed order (results are deterministic).  MXFP4 tiles run
-// on the tensor cores (mma_mxfp4.cuh); the K-quant formats use the CUDA-core
-// group decoders (qdot.cuh).  Every device wait is bounded.
+// on the tensor cores (mma_mxfp4.cuh); Q8_0 and Q4_K launches of one or two
+// tokens run dp4a against int8 digit planes of the activations (unit_int8);
+// the other K-quant cases use the CUDA-core group decoders (qdot.cuh).  Every
+// device wait is bounded.
 #include <mutex>
 
 #include "mma_mxfp4.cuh"
