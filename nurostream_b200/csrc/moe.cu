@@ -1243,6 +1243,10 @@ static size_t moe_layout(const ns_moe_layer_t* p, const MoePlan& plan, int grid,
     else if (!p1_dominates && tr > 1) tr = tr > 8 ? tr - 8 : tr - 1;
     else --stages;
   }
+  // dp4a consumers: whole tiles (every consumer warp busy) on two stages rather than narrower tiles
+  // on three (Qwen3-235B shape: 16-row tiles on three stages left a third of the consumer warps idle;
+  // phase 1 took 36 us against 25 us with 24-row tiles on two)
+  if (i8 && stage_of(tn, tr) * 3 > avail && stage_of(tn, tr) * 2 <= avail) stages = 2;
   while (stages >= 2 && stage_of(tn, tr) * stages > avail) {
     if (stages > 3) {
       --stages;
