@@ -126,7 +126,9 @@ int ns_moe_route(const void* h, int h_dtype, int T, int H,
 /*
  * One fused MoE decode layer: RMSNorm -> router -> top-k -> for every routed
  * expert gate/up (+bias) -> activation -> down (+bias) -> weighted combine
- * (+ residual), as ONE cooperative launch over all SMs.
+ * (+ residual), as ONE launch of one CTA per SM, every CTA resident at once
+ * (a cooperative launch for the CUDA-core kernel; the tensor-core kernel's
+ * plain launch relies on one CTA filling an SM, its grid-wide waits bounded).
  * Replaces neurostream/model/gpt_oss.py:123-177 `GptOssModel._ffn_block` (with
  * stream_expert_ffn, neurostream/compute/blockffn.py:396-449) and
  * neurostream/moe/router.py:173-219 `moe_ffn`.
