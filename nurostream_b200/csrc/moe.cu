@@ -616,11 +616,13 @@ __global__ void __launch_bounds__(kMoeThreads, 1) moe_layer_kernel(MoeArgs a) {
       build_xfrag(h + t * H, a.nb_h, S.sig_tok[t], ximg + t * xfrag_vec_u4(a.nb_h), tid, kMoeThreads);
   } else {
     if (tid < T) S.fac_tok[tid] = 1.0f;
-    if (kInt) {  // h of every token as int8 digit planes, one thread per (token, group)
+    if (kInt && tid >= 32) {
+      // h of every token as int8 digit planes, one thread per (token, group); warp 0 stays free, so
+      // thread 0 polls the grid barrier as soon as it completes
       uint8_t* xq = reinterpret_cast<uint8_t*>(ximg);
       float* xsc = reinterpret_cast<float*>(xq + (size_t)T * a.nb_h * kXQG);
       float* xsm = xsc + T * a.nb_h;
-      for (int it = tid; it < T * a.nb_h; it += kMoeThreads) {
+      for (int it = tid - 32; it < T * a.nb_h; it += kMoeThreads - 32) {
         const int t = it / a.nb_h, g = it - t * a.nb_h;
         float v[32];
 #pragma unroll
