@@ -349,8 +349,9 @@ def run_ours(args, rank, world, local_rank, group):
     if world > 1:
         line["config"]["combine"] = ("ns_peer_allreduce (NVLink peer stores, one kernel per layer)"
                                      if args.combine == "peer" else "NCCL all-reduce per layer")
-    traffic = ROOT / "profiles" / "moe_tc_kernel_traffic.json"
-    if traffic.exists() and shape.arch == "gpt-oss":
+    traffic = ROOT / "profiles" / ("moe_tc_kernel_traffic.json" if shape.arch == "gpt-oss"
+                                   else "moe_layer_kernel_traffic.json")
+    if traffic.exists():
         try:
             line["roofline"]["traffic"] = json.loads(traffic.read_text()).get("dram_bytes_per_launch")
         except Exception:
