@@ -908,7 +908,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) moe_tc_kernel(const __grid_cons
         }
         __syncwarp();  // every lane has consumed its staged words: the raw stage can be refilled
         if (lane == 0) mbar_arrive(&empty_raw[st]);
-        // the operand stage (TMEM columns, phase-2 B) must have been consumed by its earlier MMAs
+        // the operand stage (its A and SFA columns in TMEM) must have been consumed by its earlier MMAs
         if (!tc_wait(&empty_can[cst], ((n / kTcCanStages) & 1) ^ 1, abort_flag)) break;
         tc_fence_after();
         const uint32_t acol = tbase + kTcTmemA + kTcTmemAStage * cst + taddr_lane;
